@@ -1,0 +1,439 @@
+#!/usr/bin/env python3
+"""Decode throughput of the Qwen3.5-9B-shaped hot path on B200.
+
+Workload: 32 layers (24 Gated DeltaNet + 8 gated GQA),
+hidden 4096, FFN 12288 in GF4, every other projection and the 248320-row
+lm_head in Q8_0, greedy argmax head, 4096 positions of context per sequence,
+a batch of --batch sequences per GPU (ragged-batch data parallel: each rank
+owns its own sequences and a full weight replica, no collective).  A "step"
+is one decode step of the whole batch.  Synthetic random-init weights
+(qwowl35_b200.synth) -- there is no network for checkpoints.
+
+Printed JSON line (rank 0):
+  value     tok/s over all ranks, device-timed (CUDA events on the runtime's
+            stream), inputs already resident, steps replayed back to back;
+  e2e       the same metric through the public C ABI in a greedy loop:
+            token ids host->device, argmax ids device->host every step;
+  roofline  the step's dominant kernel, timed alone with CUDA events;
+  cpu_baseline  the CPU oracle port on a bounded sample (rank 0, N=1).
+--impl reference runs the reference's CPU rendering of the path (the oracle
+port: the reference's own GPU code is Metal-only) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+HBM_FALLBACK = 6650.0  # GB/s, pool fallback when MEASURED_PEAKS.json is absent
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the oracle port on a bounded sample (test infrastructure; the
+# product path never touches it)
+# ---------------------------------------------------------------------------
+def cpu_token_seconds(ctx: int = 4096, head_frac: int = 64):
+    """Seconds for one decoded token of the CPU port (b=1), extrapolated from a
+    sample: one GF4 FFN (gate/up/down), one DeltaNet layer (Q8_0 projections +
+    step + out), one attention layer at `ctx` context and 1/head_frac of the
+    Q8_0 lm_head, each timed once and scaled by its per-token count."""
+    import numpy as np
+
+    from oracle import ops as O
+    from oracle import quants as Q
+    rng = np.random.default_rng(0)
+    H, F = 4096, 12288
+    gf4 = [Q.gen_weight(rng, Q.GF4_TYPE, r, k) for r, k in ((F, H), (F, H), (H, F))]
+    proj_d = Q.gen_weight(rng, Q.Q8_0_TYPE, 12352, H, 127.0)
+    proj_a = Q.gen_weight(rng, Q.Q8_0_TYPE, 10240, H, 127.0)
+    outw = Q.gen_weight(rng, Q.Q8_0_TYPE, H, 4096, 127.0)
+    headw = Q.gen_weight(rng, Q.Q8_0_TYPE, 248320 // head_frac, H, 127.0)
+    x = rng.standard_normal((1, H))
+    K = rng.standard_normal((ctx, 4, 256)).astype(np.float16)
+    V = rng.standard_normal((ctx, 4, 256)).astype(np.float16)
+    S = rng.normal(0, 0.01, (32, 128, 128))
+    conv_w, cs = rng.normal(0, 0.3, (8192, 4)), np.zeros((8192, 3))
+
+    t0 = time.perf_counter()
+    g = O.matvec(Q.dequant(Q.GF4_TYPE, gf4[0], F, H), x)
+    u = O.matvec(Q.dequant(Q.GF4_TYPE, gf4[1], F, H), x)
+    O.matvec(Q.dequant(Q.GF4_TYPE, gf4[2], H, F), O.silu(g) * u)
+    t_ffn = time.perf_counter() - t0
+
+    t0 = time.perf_counter()
+    p = O.matvec(Q.dequant(Q.Q8_0_TYPE, proj_d, 12352, H), x)[0]
+    out, _, _ = O.deltanet_step(p[:8192], conv_w, cs, p[12288:12320], p[12320:], np.zeros(32), -np.ones(32), S,
+                                p[8192:12288], np.ones(128))
+    O.matvec(Q.dequant(Q.Q8_0_TYPE, outw, H, 4096), out[None])
+    t_delta = time.perf_counter() - t0
+
+    t0 = time.perf_counter()
+    p = O.matvec(Q.dequant(Q.Q8_0_TYPE, proj_a, 10240, H), x)[0]
+    q, gate, _, _ = O.attn_preprocess(p[:8192], p[8192:9216], p[9216:], np.ones(256), np.ones(256), ctx - 1,
+                                      O.rope_freqs())
+    core = O.gqa_decode(q, gate, K, V).reshape(1, -1)
+    O.matvec(Q.dequant(Q.Q8_0_TYPE, outw, H, 4096), core)
+    t_attn = time.perf_counter() - t0
+
+    t0 = time.perf_counter()
+    O.matvec(Q.dequant(Q.Q8_0_TYPE, headw, 248320 // head_frac, H), x)
+    t_head = (time.perf_counter() - t0) * head_frac
+    total = 32 * t_ffn + 24 * t_delta + 8 * t_attn + t_head
+    sample = (f"1 GF4 FFN + 1 DeltaNet layer + 1 attention layer (ctx {ctx}) + 1/{head_frac} of the Q8_0 "
+              f"head, each timed once (fp64 numpy oracle, b=1), extrapolated to a 32-layer token")
+    return total, sample
+
+
+def cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="qw35clk", suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.gpu)], stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = sorted(r[0] for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[2]) if v.lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# the step's kernels timed alone (roofline of the dominant one)
+# ---------------------------------------------------------------------------
+def kernel_table(B: int, ctx: int, device):
+    """Times each kernel class of the step alone (CUDA events, L2 flushed
+    before every launch) and returns rows of
+    (name, algorithmic bytes per launch, avg seconds, launches per step)."""
+    import torch
+
+    from qwowl35_b200 import ops
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def rnd_weight(t, rows, k):
+        raw = torch.randint(0, 256, (ops.weight_bytes(t, rows, k),), dtype=torch.uint8, device=device)
+        if t == ops.GF4:
+            raw.view(-1, 4)[:, 0] = 0x24
+        elif t == ops.Q8_0:
+            raw.view(-1, 34)[:, 0:2] = torch.tensor([0x00, 0x20], dtype=torch.uint8, device=device)
+        return ops.repack(t, raw, rows, k)
+
+    def timed(fn, reps=8):
+        fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        tot = 0.0
+        for _ in range(reps):
+            flush.fill_(1)
+            s.record()
+            fn()
+            e.record()
+            e.synchronize()
+            tot += s.elapsed_time(e) / 1e3
+        return tot / reps
+
+    H, F = 4096, 12288
+    x = torch.randn(B, H, device=device)
+    h = torch.randn(B, F, device=device)
+    rows = []
+    wg, wu, wd = rnd_weight(ops.GF4, F, H), rnd_weight(ops.GF4, F, H), rnd_weight(ops.GF4, H, F)
+    rows.append(("gate_up_swiglu GF4 12288x4096", 2 * 25165824 + B * (H + F) * 4,
+                 timed(lambda: ops.gate_up_swiglu(ops.GF4, wg, wu, x, F, H)), 32))
+    y = torch.zeros(B, H, device=device)
+    rows.append(("matvec GF4 4096x12288 +residual", 25165824 + B * (F * 4 + H * 8),
+                 timed(lambda: ops.matvec(ops.GF4, wd, h, H, F, y=y, accumulate=True)), 32))
+    del wg, wu, wd
+    for r, cnt in ((12352, 24), (10240, 8)):
+        w = rnd_weight(ops.Q8_0, r, H)
+        yy = torch.empty(B, r, device=device)
+        rows.append((f"matvec Q8_0 {r}x4096", ops.weight_bytes(ops.Q8_0, r, H) + B * (H + r) * 4,
+                     timed(lambda: ops.matvec(ops.Q8_0, w, x, r, H, y=yy)), cnt))
+    w = rnd_weight(ops.Q8_0, H, 4096)
+    rows.append(("matvec Q8_0 4096x4096 +residual", ops.weight_bytes(ops.Q8_0, H, 4096) + B * H * 12,
+                 timed(lambda: ops.matvec(ops.Q8_0, w, x, H, 4096, y=y, accumulate=True)), 32))
+    wh = rnd_weight(ops.Q8_0, 248320, H)
+    ws = ops.argmax_workspace(248320, B, device)
+    rows.append(("argmax head Q8_0 248320x4096", 1080688640 + B * H * 4,
+                 timed(lambda: ops.argmax_head(ops.Q8_0, wh, x, 248320, H, ws=ws), reps=4), 1))
+    del wh, w
+    proj = torch.randn(B, 12352, device=device)
+    conv_w = torch.randn(8192 * 4, device=device) * 0.3
+    dt, a, nw = torch.zeros(32, device=device), -torch.ones(32, device=device), torch.ones(128, device=device)
+    conv = torch.zeros(B, 8192 * 3, device=device)
+    ssm = torch.randn(B, 32 * 128 * 128, device=device) * 0.01
+    rows.append(("deltanet_step (cluster)", B * (2 * 32 * 128 * 128 * 4 + 2 * 8192 * 3 * 4 + 12352 * 4 + 4096 * 4),
+                 timed(lambda: ops.deltanet_step(proj, conv_w, dt, a, nw, conv, ssm)), 24))
+    del ssm
+    plane = 4 * 256 * 256
+    nch = (ctx + 255) // 256
+    pool = torch.randn(B * nch * 2 * plane, device=device).to(torch.float16)
+    base = pool.data_ptr()
+    table = torch.tensor([[base + (s * nch + c) * 2 * plane * 2 for c in range(nch)] for s in range(B)],
+                         dtype=torch.int64, device=device)
+    q, g = torch.randn(B, 16, 256, device=device), torch.randn(B, 16, 256, device=device)
+    lens = torch.full((B,), ctx, dtype=torch.int32, device=device)
+    aws = ops.gqa_workspace(B, ctx, device)
+    out = torch.empty(B, 4096, device=device)
+    rows.append((f"gqa split-K decode ctx {ctx} (+combine)", B * ctx * 4096 + B * 16 * 256 * 12,
+                 timed(lambda: ops.gqa_decode(q, g, lens, ctx, table, 0, plane * 2, ws=aws, out=out)), 8))
+    return rows
+
+
+# ---------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def run_reference(args, world):
+    rank, _, _ = dist_env()
+    if rank != 0:
+        return
+    cores = cpu_cores()
+    times = []
+    sample = ""
+    for i in range(args.warmup + args.steps):
+        t, sample = cpu_token_seconds(ctx=args.ctx_fill, head_frac=256)
+        if i >= args.warmup:
+            times.append(t)
+    tps = 1.0 / (sum(times) / len(times))
+    line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / tps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": workload_config(args, world),
+            "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": "per step: " + sample + "; the reference's own decode path is Metal-only "
+                                       "(unavailable on this box), so its kernels run as the numpy oracle port"},
+            "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "decode tok/s, Qwen3.5-9B-shape (GF4 FFN, Q8_0 projections+head), 4k ctx"
+
+
+def workload_config(args, world):
+    return {"workload": f"config5 full decode step, batch {args.batch}/GPU, ctx {args.ctx_fill}",
+            "global_batch": args.batch * world, "seq_len": args.ctx_fill, "layers": args.layers,
+            "ffn_codec": "gf4", "proj_codec": "q8_0", "head_codec": "q8_0", "vocab": 248320,
+            "parallelism": f"dp{world} (ragged sequences per GPU, no collective)",
+            "l2": "inputs larger than L2: every step streams 5.7 GB of weights plus state/KV"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--ctx-fill", type=int, default=4096)
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel roofline table")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank, world, local = dist_env()
+
+    if args.impl == "reference":
+        run_reference(args, world)
+        return
+
+    import numpy as np
+    import torch
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=device)
+    from qwowl35_b200 import synth
+    from qwowl35_b200.runtime import LogitsMode, Runtime
+
+    B = args.batch
+    cfg = synth.ModelConfig(layers=args.layers)
+    t0 = time.time()
+    model = synth.build(cfg, seed=0, device=device)
+    t_gen = time.time() - t0
+    total_pos = args.ctx_fill + 2 * (args.warmup + args.steps) + args.steps + 8
+    t0 = time.time()
+    rt = Runtime(model, ctx=total_pos, max_seqs=B)
+    t_load = time.time() - t0
+    ids = [0] + [rt.seq_alloc() for _ in range(B - 1)]
+    tok = (np.arange(B, dtype=np.uint32) * 7919) % cfg.vocab
+
+    # context fill: every sequence decodes ctx_fill positions (untimed)
+    t0 = time.time()
+    for p in range(args.ctx_fill):
+        rt.eval_batch(ids, (tok + p) % cfg.vocab, [p] * B, LogitsMode.NONE)
+    rt.sync()
+    t_fill = time.time() - t0
+    pos = args.ctx_fill
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-timed steps (inputs resident, no host reads inside) --------
+    ext = torch.cuda.ExternalStream(rt.stream(), device=device)
+    for _ in range(args.warmup):
+        rt.eval_batch(ids, tok, [pos] * B, LogitsMode.ARGMAX)
+        pos += 1
+    rt.sync()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
+                      int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])) as clk:
+        ev0.record(ext)
+        for _ in range(args.steps):
+            rt.eval_batch(ids, tok, [pos] * B, LogitsMode.ARGMAX)
+            pos += 1
+        ev1.record(ext)
+        ev1.synchronize()
+    rt.sync()
+    barrier()
+    dev_s = max_over_ranks(ev0.elapsed_time(ev1) / 1e3)
+    kernels = rt.last_step_kernels()
+    value = B * world * args.steps / dev_s
+
+    # ---- end to end through the C ABI: greedy loop, H2D ids, D2H argmax ----
+    cur = tok.copy()
+    for _ in range(args.warmup):
+        rt.eval_batch(ids, cur, [pos] * B, LogitsMode.ARGMAX)
+        cur, _ = rt.argmax_batch(B)
+        pos += 1
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        rt.eval_batch(ids, cur, [pos] * B, LogitsMode.ARGMAX)
+        cur, _ = rt.argmax_batch(B)
+        pos += 1
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    barrier()
+
+    # ---- batch 1 on the same runtime (sequence 0) ---------------------------
+    for _ in range(3):
+        rt.eval_batch([0], [1], [pos], LogitsMode.ARGMAX)
+        pos += 1
+    rt.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    n1 = min(args.steps, 8)
+    for _ in range(n1):
+        rt.eval_batch([0], [1], [pos], LogitsMode.ARGMAX)
+        pos += 1
+    e1.record(ext)
+    e1.synchronize()
+    b1_s = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    rt.close()
+    del model
+
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": dev_s / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (random-init, seed 0)",
+            "config": workload_config(args, world), "clocks": clk.summary(),
+            "e2e": {"value": B * world * args.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16 * B,
+                    "d2h_bytes_per_step": 8 * B},
+            "gpu_launches": kernels * args.steps,
+            "b1": {"value": world * n1 / b1_s, "unit": "tok/s", "ms_per_token": b1_s / n1 * 1e3},
+            "setup_s": {"generate": round(t_gen, 1), "upload": round(t_load, 1), "ctx_fill": round(t_fill, 1)}}
+
+    if rank == 0 and not args.no_kernels:
+        peak, kind = peaks()
+        rows = kernel_table(B, args.ctx_fill, device)
+        table = [{"kernel": n, "bytes": b, "us": t * 1e6, "per_step": c, "gbs": b / t / 1e9,
+                  "frac": b / t / 1e9 / peak} for n, b, t, c in rows]
+        dom = max(rows, key=lambda r: r[2] * r[3])
+        achieved = dom[1] / dom[2] / 1e9
+        line["roofline"] = {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak,
+                            "peak_kind": kind, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                            "bytes_per_launch": dom[1], "us_per_launch": dom[2] * 1e6}
+        line["kernels"] = table
+    if rank == 0 and world == 1 and not args.no_cpu:
+        t, sample = cpu_token_seconds(ctx=args.ctx_fill, head_frac=64)
+        line["cpu_baseline"] = {"value": 1.0 / t, "unit": "tok/s", "cores": cpu_cores(), "kind": "port",
+                                "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

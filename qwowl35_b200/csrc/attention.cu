@@ -1,0 +1,308 @@
+// attention.cu -- gated GQA decode attention over the chunk-table KV cache.
+//
+// Reference:
+//   qw35_attn_decode_preprocess_f32        qw35_attention.metal:29-112
+//   qw35_attention_gqa_flash_decode_f32    qw35_attention.metal:211-292
+//   ..._split_f32 (8-way split-K + merge)  qw35_attention.metal:302-414
+//   dispatch / split threshold             Qw35MetalRuntime+Attention.m:80-111
+//
+// KV layout: each sequence owns a table of 256-position chunks; chunk c of
+// sequence i lives at chunk_ptrs[i * max_chunks + c] (any device address, no
+// contiguity between chunks).  Inside a chunk, one attention layer's K plane
+// (at k_off) and V plane (at v_off) are [4 kv heads][256 pos][256 dim] f16, so
+// one (kv head, chunk) tile is a single contiguous 128 KiB run.
+//
+// Decode (B200 design): split-K over fixed 1024-position splits of the
+// attended range; one CTA per (split, kv head, sequence) serves all 4 query
+// heads of the GQA group from ONE read of K and V (the reference re-reads the
+// cache once per query head).  Each warp walks 256 positions, 8 at a time:
+// 128-bit loads of K/V rows, fp32 dots for the 4 heads, a 31-shuffle
+// transpose-reduction, online softmax per head.  A second kernel merges the
+// splits and applies the sigmoid output gate.
+#include "common.cuh"
+#include "ops.h"
+
+namespace qw35 {
+
+constexpr int AH = 16;      // query heads
+constexpr int AKV = 4;      // kv heads
+constexpr int AHD = 256;    // head dim
+constexpr int AGRP = AH / AKV;
+constexpr int ACHUNK = 256; // positions per chunk
+constexpr int ASPLIT = 1024;  // positions per split (4 warps x 256)
+constexpr int QFULL = AH * AHD * 2;  // q | gate per head
+
+// ---- preprocess: RMS norm + NeoX RoPE + f16 KV write -------------------------
+__global__ void __launch_bounds__(256) attn_pre_kernel(AttnPreArgs p) {
+    const int seq = blockIdx.x;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int pos = p.pos[seq];
+    const float *src = p.qkv + (size_t)seq * p.qkv_stride;
+    const int d0 = lane * 8;
+    for (int task = wid; task < AH + AKV; task += 8) {
+        const bool isq = task < AH;
+        const int h = isq ? task : task - AH;
+        const float *x = isq ? src + h * 2 * AHD : src + QFULL + h * AHD;
+        const float *nw = isq ? p.q_norm_w : p.k_norm_w;
+        float v[8];
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { v[i] = x[d0 + i]; ss = fmaf(v[i], v[i], ss); }
+        ss = warp_sum(ss);
+        const float inv = rsqrtf(ss / (float)AHD + p.eps);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = v[i] * inv * nw[d0 + i];
+        // RoPE over dims [0, 64): lanes 0..3 hold dims 0..31, lanes 4..7 hold 32..63
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float partner = __shfl_xor_sync(0xffffffffu, v[i], 4);
+            if (lane < 8) {
+                const int pair = (d0 + i) & 31;
+                const float theta = (float)pos * p.rope_freq[pair];
+                float sn, cs;
+                sincosf(theta, &sn, &cs);
+                o[i] = lane < 4 ? (v[i] * cs - partner * sn) : (partner * sn + v[i] * cs);
+            } else {
+                o[i] = v[i];
+            }
+        }
+        if (isq) {
+            float *qo = p.q_out + ((size_t)seq * AH + h) * AHD + d0;
+            float *go = p.gate_out + ((size_t)seq * AH + h) * AHD + d0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { qo[i] = o[i]; go[i] = x[AHD + d0 + i]; }
+        } else {
+            const size_t trow = p.slots ? (size_t)p.slots[seq] : (size_t)seq;
+            const uint64_t base = p.chunk_ptrs[trow * p.max_chunks + pos / ACHUNK];
+            const size_t row = ((size_t)h * ACHUNK + (pos % ACHUNK)) * AHD + d0;
+            __half *kp = reinterpret_cast<__half *>(base + p.k_off) + row;
+            __half *vp = reinterpret_cast<__half *>(base + p.v_off) + row;
+            const float *vs = src + QFULL + AKV * AHD + h * AHD + d0;
+            __align__(16) __half kh[8], vh[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { kh[i] = __float2half_rn(o[i]); vh[i] = __float2half_rn(vs[i]); }
+            *reinterpret_cast<uint4 *>(kp) = *reinterpret_cast<const uint4 *>(kh);
+            *reinterpret_cast<uint4 *>(vp) = *reinterpret_cast<const uint4 *>(vh);
+        }
+    }
+}
+
+// ---- split-K decode -----------------------------------------------------------
+__device__ __forceinline__ void h8_to_f(const uint4 &u, float *f) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float2 t = __half22float2(*reinterpret_cast<const __half2 *>(&w[k]));
+        f[2 * k] = t.x;
+        f[2 * k + 1] = t.y;
+    }
+}
+
+struct SplitPart {  // per (seq, head, split): m, l then acc[256] in a separate array
+    float m, l;
+};
+
+__device__ __forceinline__ void attended_range(int L, int window, int sink, int &total, int &sk, int &rstart) {
+    sk = max(0, min(sink, L));
+    if (window <= 0 || sk + window >= L) {
+        sk = 0; rstart = 0; total = L;
+    } else {
+        rstart = L - window; total = sk + window;
+    }
+}
+
+__global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_max) {
+    const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int L = p.seq_len[seq];
+    int total, sk, rstart;
+    attended_range(L, p.window, p.sink, total, sk, rstart);
+    const int nsplit = (total + ASPLIT - 1) / ASPLIT;
+    if (split >= nsplit) return;
+
+    __shared__ float wm[4][AGRP], wl[4][AGRP];
+    __shared__ __align__(16) float wacc[4][AGRP][AHD];
+
+    // q for the 4 heads of the group, pre-scaled by sm_scale (1/16: exact)
+    float q[AGRP][8];
+#pragma unroll
+    for (int hh = 0; hh < AGRP; ++hh) {
+        const float4 *qp = reinterpret_cast<const float4 *>(p.q + ((size_t)seq * AH + kvh * AGRP + hh) * AHD + lane * 8);
+        const float4 a = qp[0], b = qp[1];
+        q[hh][0] = a.x * p.scale; q[hh][1] = a.y * p.scale; q[hh][2] = a.z * p.scale; q[hh][3] = a.w * p.scale;
+        q[hh][4] = b.x * p.scale; q[hh][5] = b.y * p.scale; q[hh][6] = b.z * p.scale; q[hh][7] = b.w * p.scale;
+    }
+    float m[AGRP], l[AGRP], acc[AGRP][8];
+#pragma unroll
+    for (int hh = 0; hh < AGRP; ++hh) {
+        m[hh] = -INFINITY; l[hh] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[hh][i] = 0.0f;
+    }
+
+    const int i0 = split * ASPLIT + wid * (ASPLIT / 4);
+    const int i1 = min(i0 + ASPLIT / 4, total);
+    const uint64_t *ctab = p.chunk_ptrs + (p.slots ? (size_t)p.slots[seq] : (size_t)seq) * p.max_chunks;
+    const size_t head_off = (size_t)kvh * ACHUNK * AHD;
+
+    for (int ib = i0; ib < i1; ib += 8) {
+        uint4 kr[8], vr[8];
+        bool valid[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const int idx = ib + t;
+            valid[t] = idx < i1;
+            const int pos = idx < sk ? idx : rstart + (idx - sk);
+            if (valid[t]) {
+                const uint64_t base = ctab[pos / ACHUNK];
+                const size_t off = (head_off + (size_t)(pos % ACHUNK) * AHD + lane * 8) * sizeof(__half);
+                kr[t] = ldg_stream(reinterpret_cast<const void *>(base + p.k_off + off));
+                vr[t] = ldg_stream(reinterpret_cast<const void *>(base + p.v_off + off));
+            } else {
+                kr[t] = make_uint4(0, 0, 0, 0);
+                vr[t] = make_uint4(0, 0, 0, 0);
+            }
+        }
+        // partial dots: s[t*4 + hh]
+        float s[32];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            float kf[8];
+            h8_to_f(kr[t], kf);
+#pragma unroll
+            for (int hh = 0; hh < AGRP; ++hh) {
+                float d = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) d = fmaf(q[hh][i], kf[i], d);
+                s[t * 4 + hh] = d;
+            }
+        }
+        // transpose-reduce: lane j ends with the full dot of value j = (t = j/4, hh = j%4)
+#pragma unroll
+        for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
+            const bool upper = (lane & o) != 0;
+#pragma unroll
+            for (int i = 0; i < n / 2; ++i) {
+                const float send = upper ? s[i] : s[i + n / 2];
+                const float keep = upper ? s[i + n / 2] : s[i];
+                s[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
+        }
+        const int my_t = lane >> 2;
+        const float score = valid[0] && (ib + my_t) < i1 ? s[0] : -INFINITY;
+        // per-head block max: lanes with equal (lane & 3)
+        float bm = score;
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
+        const float mold = m[lane & 3];
+        const float mnew = fmaxf(mold, bm);
+        const float pr = score == -INFINITY ? 0.0f : expf(score - mnew);
+        float ps = pr;
+        ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+#pragma unroll
+        for (int hh = 0; hh < AGRP; ++hh) {
+            const float mn = __shfl_sync(0xffffffffu, mnew, hh);
+            const float psum = __shfl_sync(0xffffffffu, ps, hh);
+            const float alpha = m[hh] == -INFINITY ? 0.0f : expf(m[hh] - mn);
+            l[hh] = l[hh] * alpha + psum;
+            m[hh] = mn;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[hh][i] *= alpha;
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            float vf[8];
+            h8_to_f(vr[t], vf);
+#pragma unroll
+            for (int hh = 0; hh < AGRP; ++hh) {
+                const float pw = __shfl_sync(0xffffffffu, pr, t * 4 + hh);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[hh][i] = fmaf(pw, vf[i], acc[hh][i]);
+            }
+        }
+    }
+
+    // merge the 4 warps, write the split partial
+    if (lane < AGRP) { wm[wid][lane] = m[lane]; wl[wid][lane] = l[lane]; }
+#pragma unroll
+    for (int hh = 0; hh < AGRP; ++hh)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) wacc[wid][hh][lane * 8 + i] = acc[hh][i];
+    __syncthreads();
+    const size_t nsm = (size_t)nsplit_max;
+    SplitPart *parts = static_cast<SplitPart *>(p.ws);
+    float *pacc = reinterpret_cast<float *>(static_cast<uint8_t *>(p.ws) +
+                                            (size_t)p.n_seq * AH * nsm * sizeof(SplitPart));
+    for (int e = threadIdx.x; e < AGRP * AHD; e += 128) {
+        const int hh = e / AHD, d = e % AHD;
+        float ms = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) ms = fmaxf(ms, wm[w][hh]);
+        float ls = 0.0f, as = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const float f = wm[w][hh] == -INFINITY ? 0.0f : expf(wm[w][hh] - ms);
+            ls += f * wl[w][hh];
+            as += f * wacc[w][hh][d];
+        }
+        const size_t slot = ((size_t)seq * AH + kvh * AGRP + hh) * nsm + split;
+        pacc[slot * AHD + d] = as;
+        if (d == 0) { parts[slot].m = ms; parts[slot].l = ls; }
+    }
+}
+
+__global__ void __launch_bounds__(256) attn_combine_kernel(AttnArgs p, int nsplit_max) {
+    const int h = blockIdx.x, seq = blockIdx.y, d = threadIdx.x;
+    const int L = p.seq_len[seq];
+    int total, sk, rstart;
+    attended_range(L, p.window, p.sink, total, sk, rstart);
+    const int nsplit = (total + ASPLIT - 1) / ASPLIT;
+    const size_t nsm = (size_t)nsplit_max;
+    const SplitPart *parts = static_cast<const SplitPart *>(p.ws);
+    const float *pacc = reinterpret_cast<const float *>(static_cast<const uint8_t *>(p.ws) +
+                                                        (size_t)p.n_seq * AH * nsm * sizeof(SplitPart));
+    const size_t base = ((size_t)seq * AH + h) * nsm;
+    float ms = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) ms = fmaxf(ms, parts[base + s].m);
+    float ls = 0.0f, as = 0.0f;
+    for (int s = 0; s < nsplit; ++s) {
+        const float mm = parts[base + s].m;
+        const float f = mm == -INFINITY ? 0.0f : expf(mm - ms);
+        ls += f * parts[base + s].l;
+        as += f * pacc[(base + s) * AHD + d];
+    }
+    float o = ls > 0.0f ? as / ls : 0.0f;
+    if (p.gate) o *= sigmoid_f(p.gate[((size_t)seq * AH + h) * AHD + d]);
+    p.out[(size_t)seq * p.out_stride + h * AHD + d] = o;
+}
+
+size_t attn_workspace_bytes(int n_seq, int max_len) {
+    const size_t ns = (size_t)((max_len + ASPLIT - 1) / ASPLIT);
+    return (size_t)n_seq * AH * ns * (sizeof(SplitPart) + AHD * sizeof(float));
+}
+
+cudaError_t attn_preprocess_run(const AttnPreArgs &a, cudaStream_t st) {
+    if (a.n_seq <= 0) return cudaSuccess;
+    attn_pre_kernel<<<a.n_seq, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t attn_decode_run(const AttnArgs &a, cudaStream_t st) {
+    if (a.n_seq <= 0) return cudaSuccess;
+    if (a.max_len <= 0 || a.n_seq > 65535) return cudaErrorInvalidValue;
+    if (a.ws_bytes < attn_workspace_bytes(a.n_seq, a.max_len)) return cudaErrorInvalidValue;
+    const int ns = (a.max_len + ASPLIT - 1) / ASPLIT;
+    dim3 g1(ns, AKV, a.n_seq);
+    attn_split_kernel<<<g1, 128, 0, st>>>(a, ns);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    dim3 g2(AH, a.n_seq);
+    attn_combine_kernel<<<g2, 256, 0, st>>>(a, ns);
+    return cudaGetLastError();
+}
+
+}  // namespace qw35

@@ -1,0 +1,165 @@
+// core.cu -- weight repack / dequant, embedding gather, RMS norm.
+//
+// Reference: qw35_get_row_q4_k_f32 / qw35_get_row_q8_0_f32
+// (qw35_matvec.metal:100-149), qw35_rms_norm_weight_f32 (qw35_core.metal:14-48).
+#include <mutex>
+
+#include "common.cuh"
+#include "ops.h"
+#include "quant.cuh"
+
+namespace qw35h {
+int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (cached[dev] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cached[dev] = n > 0 ? n : 1;
+    }
+    return cached[dev];
+}
+}  // namespace qw35h
+
+namespace qw35 {
+
+// ---- GGUF -> device layout ------------------------------------------------------
+// Q8_0: one thread per 34-byte block: 32 codes to the codes plane, d to the scales plane.
+__global__ void repack_q8_0_kernel(const uint8_t *src, uint8_t *dst, size_t nblk, size_t rows, uint32_t k) {
+    const size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblk) return;
+    const uint8_t *s = src + b * 34;
+    uint8_t *codes = dst + b * 32;
+    uint16_t *scales = reinterpret_cast<uint16_t *>(dst + rows * k);
+    uint32_t tmp[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        tmp[i] = (uint32_t)s[2 + 4 * i] | ((uint32_t)s[3 + 4 * i] << 8) | ((uint32_t)s[4 + 4 * i] << 16) |
+                 ((uint32_t)s[5 + 4 * i] << 24);
+    reinterpret_cast<uint4 *>(codes)[0] = make_uint4(tmp[0], tmp[1], tmp[2], tmp[3]);
+    reinterpret_cast<uint4 *>(codes)[1] = make_uint4(tmp[4], tmp[5], tmp[6], tmp[7]);
+    scales[b] = (uint16_t)s[0] | ((uint16_t)s[1] << 8);
+}
+
+// Q4_K: one thread per 144-byte block.  GGUF qs byte 32g+l holds element 64g+l
+// (low nibble) and 64g+32+l (high); the device codes plane holds elements in
+// order, two per byte.  The 16-byte header (d, dmin, scales) is kept verbatim.
+__global__ void repack_q4_k_kernel(const uint8_t *src, uint8_t *dst, size_t nblk, size_t rows, uint32_t k) {
+    const size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblk) return;
+    const uint8_t *s = src + b * 144;
+    uint8_t *codes = dst + b * 128;
+    uint8_t *hdr = dst + rows * (k / 2) + b * 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) hdr[i] = s[i];
+    const uint8_t *qs = s + 16;
+    for (int j = 0; j < 128; ++j) {
+        const int e0 = 2 * j, e1 = 2 * j + 1;
+        auto nib = [&](int e) -> uint32_t {
+            const int g = e / 64, r = e % 64;
+            const uint8_t byte = qs[32 * g + (r % 32)];
+            return r < 32 ? (byte & 0xf) : (byte >> 4);
+        };
+        codes[j] = (uint8_t)(nib(e0) | (nib(e1) << 4));
+    }
+}
+
+cudaError_t weight_repack(uint32_t type_id, const void *src, void *dst, uint32_t rows, uint32_t k, cudaStream_t st) {
+    const uint8_t *s = static_cast<const uint8_t *>(src);
+    uint8_t *d = static_cast<uint8_t *>(dst);
+    if (type_id == QW35_GF4_TYPE || type_id == QW35_F32_TYPE) {
+        const size_t bytes = type_id == QW35_GF4_TYPE ? (size_t)rows * k / 2 : (size_t)rows * k * 4;
+        return cudaMemcpyAsync(d, s, bytes, cudaMemcpyDeviceToDevice, st);
+    }
+    if (type_id == QW35_Q8_0_TYPE) {
+        const size_t nb = (size_t)rows * (k / 32);
+        repack_q8_0_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, st>>>(s, d, nb, rows, k);
+        return cudaGetLastError();
+    }
+    if (type_id == QW35_Q4_K_TYPE) {
+        const size_t nb = (size_t)rows * (k / 256);
+        repack_q4_k_kernel<<<(unsigned)((nb + 127) / 128), 128, 0, st>>>(s, d, nb, rows, k);
+        return cudaGetLastError();
+    }
+    return cudaErrorInvalidValue;
+}
+
+// ---- dequantise one element (device layout) ---------------------------------------
+template <bool EXACT>
+__device__ __forceinline__ float dequant_at(uint32_t type_id, const uint8_t *w, size_t rows, uint32_t k, size_t r,
+                                            uint32_t c) {
+    if (type_id == QW35_GF4_TYPE) {
+        const uint32_t word = reinterpret_cast<const uint32_t *>(w)[r * (k / 8) + c / 8];
+        return gf4_weight<EXACT>(word, (int)(c & 7));
+    }
+    if (type_id == QW35_Q8_0_TYPE) {
+        const int8_t q = reinterpret_cast<const int8_t *>(w)[r * k + c];
+        const uint16_t dbits = reinterpret_cast<const uint16_t *>(w + rows * k)[r * (k / 32) + c / 32];
+        return (float)q * __half2float(__ushort_as_half(dbits));
+    }
+    if (type_id == QW35_Q4_K_TYPE) {
+        const uint8_t byte = w[r * (k / 2) + c / 2];
+        const uint32_t q = (c & 1) ? (byte >> 4) : (byte & 0xf);
+        const uint4 h = *reinterpret_cast<const uint4 *>(w + rows * (k / 2) + (r * (k / 256) + c / 256) * 16);
+        float dl, ml;
+        q4k_scale_min(h, (int)((c % 256) / 32), dl, ml);
+        return dl * (float)q - ml;
+    }
+    return reinterpret_cast<const float *>(w)[r * k + c];
+}
+
+template <bool EXACT>
+__global__ void dequant_kernel(uint32_t type_id, const uint8_t *w, float *out, size_t rows, uint32_t k) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * k) return;
+    out[i] = dequant_at<EXACT>(type_id, w, rows, k, i / k, (uint32_t)(i % k));
+}
+
+cudaError_t weight_dequant(uint32_t type_id, const void *w, float *out, uint32_t rows, uint32_t k, uint32_t flags,
+                           cudaStream_t st) {
+    const size_t n = (size_t)rows * k;
+    const unsigned blocks = (unsigned)((n + 255) / 256);
+    if (flags & QW35_MV_GF4_EXACT)
+        dequant_kernel<true><<<blocks, 256, 0, st>>>(type_id, static_cast<const uint8_t *>(w), out, rows, k);
+    else
+        dequant_kernel<false><<<blocks, 256, 0, st>>>(type_id, static_cast<const uint8_t *>(w), out, rows, k);
+    return cudaGetLastError();
+}
+
+// ---- embedding row gather (qw35_matvec.metal:100-149) -------------------------------
+__global__ void embed_kernel(uint32_t type_id, const uint8_t *w, const uint32_t *tokens, size_t vocab, uint32_t k,
+                             float *out) {
+    const int i = blockIdx.y;
+    const uint32_t tok = tokens[i];
+    for (uint32_t c = blockIdx.x * blockDim.x + threadIdx.x; c < k; c += gridDim.x * blockDim.x)
+        out[(size_t)i * k + c] = dequant_at<true>(type_id, w, vocab, k, tok, c);
+}
+
+cudaError_t embed_rows(uint32_t type_id, const void *w, size_t vocab, const uint32_t *tokens, int n,
+                             uint32_t k, float *out, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    dim3 grid((k + 255) / 256, n);
+    embed_kernel<<<grid, 256, 0, st>>>(type_id, static_cast<const uint8_t *>(w), tokens, vocab, k, out);
+    return cudaGetLastError();
+}
+
+// ---- RMS norm (qw35_core.metal:14-48), one CTA per row ------------------------------
+__global__ void __launch_bounds__(256) rms_norm_kernel(const float *x, const float *w, float *out, int k, float eps) {
+    __shared__ float red[32];
+    const float *xr = x + (size_t)blockIdx.x * k;
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < k; i += 256) s = fmaf(xr[i], xr[i], s);
+    s = block_sum(s, red);
+    const float inv = rsqrtf(s / (float)k + eps);
+    for (int i = threadIdx.x; i < k; i += 256) out[(size_t)blockIdx.x * k + i] = xr[i] * inv * w[i];
+}
+
+cudaError_t rms_norm_run(const float *x, const float *w, float *out, int n, int k, float eps, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    rms_norm_kernel<<<n, 256, 0, st>>>(x, w, out, k, eps);
+    return cudaGetLastError();
+}
+
+}  // namespace qw35

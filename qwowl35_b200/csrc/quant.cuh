@@ -1,0 +1,110 @@
+// quant.cuh -- device layouts and per-chunk decode+dot of the weight codecs.
+//
+// Device layouts (rows x K matrix; total bytes equal to the GGUF encoding):
+//   GF4  : words [rows][K/8] uint32, byte-identical to the GGUF tensor
+//          (bits 0..7 e5m2 scale, bits 8+3i prepared 3-bit code i).
+//   Q8_0 : codes plane [rows][K] int8, then scales plane [rows][K/32] fp16.
+//   Q4_K : codes plane [rows][K/2] (byte j = element 2j | element 2j+1 << 4),
+//          then headers plane [rows][K/256] x 16 B {f16 d, f16 dmin, u8 scales[12]}.
+// The repack from GGUF blocks happens once at upload (qw35_cuda_weight_repack);
+// splitting codes from scales makes every code load a 16-byte aligned,
+// fully coalesced 128-bit transaction.
+//
+// A "chunk" is 32 consecutive weights of one row; every codec's chunk is one
+// or two 16-byte loads plus (Q8_0, Q4_K) a small scale/header load.
+#pragma once
+#include "common.cuh"
+
+namespace qw35 {
+
+// ---- GF4 ------------------------------------------------------------------
+// Reference semantics: qw35-server/src/metal/qw35_gf4.metal:8-20 (decode) and
+// tools/qw35_cook_common.py:67-119 (format).  Per word:
+//   dot = (-0.25 * s) * sum_j (q_raw_j - 4) * x_j      (exact mode)
+//   metal mode adds junk * 2^-13 * x_4 inside the sum, junk = (w >> 11) & 0x1ff,
+//   reproducing the unmasked i == 0 shift of the reference kernel.
+// `xs4` holds 4 * sum_j x_j per word; `x4s` holds x_4 * 2^-13 per word.
+template <bool EXACT>
+__device__ __forceinline__ float gf4_word_dot(uint32_t w, const float *x, float xs4, float x4s) {
+    float acc = -xs4;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t q = ((w >> (8 + 3 * j)) & 7u) ^ 4u;  // q_raw
+        acc = fmaf(u23_to_float(q), x[j], acc);
+    }
+    if (!EXACT) acc = fmaf(u23_to_float((w >> 11) & 0x1ffu), x4s, acc);
+    return acc * (e5m2_to_float(w) * -0.25f);
+}
+
+// Dequantised weight j of a GF4 word (bit-exact with the oracle).
+template <bool EXACT>
+__device__ __forceinline__ float gf4_weight(uint32_t w, int j) {
+    const float s = e5m2_to_float(w);
+    const uint32_t p = (w >> (8 + 3 * j)) & 7u;
+    if (EXACT) {
+        const float q = (float)(p ^ 4u);
+        return (4.0f - q) * 0.25f * s;
+    }
+    int v = ((int)(p ^ 4u) - 4) * 8192;
+    if (j == 4) v += (int)((w >> 11) & 0x1ffu);
+    return (float)v * (s * -0.25f * 0.0001220703125f);
+}
+
+// ---- Q8_0 -----------------------------------------------------------------
+// Reference: qw35_matvec.metal:630-654.  Codes are int8; each 32-chunk has one
+// fp16 scale.  The dot uses unsigned bytes (q + 128) built as floats with the
+// 2^23 magic: sum (u - 128) x = sum_b (float(0x4B0000uu) - (2^23 + 128)) x.
+__device__ __forceinline__ float q8_word_dot(uint32_t wd, const float *x) {
+    const uint32_t wx = wd ^ 0x80808080u;
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t r = __byte_perm(wx, 0x4B000000u, (uint32_t)k | 0x7540u);
+        acc = fmaf(__uint_as_float(r) - 8388736.0f, x[k], acc);
+    }
+    return acc;
+}
+
+__device__ __forceinline__ float q8_chunk_dot(uint4 a, uint4 b, const float *x) {
+    float acc = q8_word_dot(a.x, x + 0);
+    acc += q8_word_dot(a.y, x + 4);
+    acc += q8_word_dot(a.z, x + 8);
+    acc += q8_word_dot(a.w, x + 12);
+    acc += q8_word_dot(b.x, x + 16);
+    acc += q8_word_dot(b.y, x + 20);
+    acc += q8_word_dot(b.z, x + 24);
+    acc += q8_word_dot(b.w, x + 28);
+    return acc;
+}
+
+// ---- Q4_K -----------------------------------------------------------------
+// Reference: qw35_types.metal:70-83 (6-bit scale/min unpack) and
+// qw35_matvec.metal:2-12 (w = d*sc*q - dmin*m).
+__device__ __forceinline__ uint32_t hdr_byte(const uint4 &h, int i) {  // i over the 12 scale bytes
+    const uint32_t word = i < 4 ? h.y : (i < 8 ? h.z : h.w);
+    return (word >> (8 * (i & 3))) & 0xffu;
+}
+
+__device__ __forceinline__ void q4k_scale_min(const uint4 &h, int j, float &dl, float &ml) {
+    uint32_t sc, m;
+    if (j < 4) {
+        sc = hdr_byte(h, j) & 63u;
+        m = hdr_byte(h, j + 4) & 63u;
+    } else {
+        sc = (hdr_byte(h, j + 4) & 0x0fu) | ((hdr_byte(h, j - 4) >> 6) << 4);
+        m = (hdr_byte(h, j + 4) >> 4) | ((hdr_byte(h, j) >> 6) << 4);
+    }
+    const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffffu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    dl = d * (float)sc;
+    ml = dmin * (float)m;
+}
+
+__device__ __forceinline__ float q4_word_dot(uint32_t w, const float *x) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) acc = fmaf(u23_to_float((w >> (4 * n)) & 0xfu), x[n], acc);
+    return acc;
+}
+
+}  // namespace qw35

@@ -1,0 +1,111 @@
+"""GQA decode attention over a non-contiguous 256-position chunk table vs the
+oracle (qw35_attention.metal:29-414).  KV-chunk indexing must be exact;
+outputs within max relative error 1e-3."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops as O
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+PLANE = 4 * 256 * 256  # f16 elements of one K (or V) plane in a chunk
+
+
+def relerr(y, ref):
+    return float(np.max(np.abs(np.asarray(y, np.float64) - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def make_pool(rng, lens, layers=1):
+    """Chunks hold `layers` x (K plane, V plane); order in the pool is shuffled."""
+    nchunks = [(L + 255) // 256 for L in lens]
+    total = sum(nchunks)
+    per_chunk = layers * 2 * PLANE
+    pool = torch.empty(total * per_chunk, dtype=torch.float16, device="cuda")
+    pool.normal_()
+    perm = rng.permutation(total)
+    maxc = max(nchunks)
+    table = np.zeros((len(lens), maxc), dtype=np.uint64)
+    base = pool.data_ptr()
+    i = 0
+    for s, c in enumerate(nchunks):
+        for j in range(c):
+            table[s, j] = base + int(perm[i]) * per_chunk * 2
+            i += 1
+    return pool, perm, table, per_chunk
+
+
+def gather_kv(pool, perm, table_rows, L, layer, per_chunk):
+    """Host copy of K, V [L, 4, 256] of one sequence through its chunk list."""
+    host = pool.view(-1, per_chunk).cpu().numpy()
+    K = np.empty((L, 4, 256), np.float16)
+    V = np.empty((L, 4, 256), np.float16)
+    for t in range(L):
+        c = table_rows[t // 256]
+        blk = host[c]
+        kpl = blk[layer * 2 * PLANE: layer * 2 * PLANE + PLANE].reshape(4, 256, 256)
+        vpl = blk[layer * 2 * PLANE + PLANE: (layer + 1) * 2 * PLANE].reshape(4, 256, 256)
+        K[t] = kpl[:, t % 256, :]
+        V[t] = vpl[:, t % 256, :]
+    return K, V
+
+
+@pytest.mark.parametrize("lens,window,sink", [([1], 0, 0), ([300], 0, 0), ([1025, 7, 5000], 0, 0),
+                                              ([4096, 2048], 512, 4), ([3000], 1024, 0), ([700], 2000, 10)])
+def test_gqa_decode_matches_oracle(lens, window, sink):
+    rng = np.random.default_rng(sum(lens))
+    layers, layer = 2, 1
+    pool, perm, table, per_chunk = make_pool(rng, lens, layers)
+    n = len(lens)
+    q = rng.normal(0, 1, (n, 16, 256)).astype(np.float32)
+    gate = rng.normal(0, 1, (n, 16, 256)).astype(np.float32)
+    from qwowl35_b200 import ops
+    k_off = layer * 2 * PLANE * 2
+    v_off = k_off + PLANE * 2
+    out = ops.gqa_decode(torch.from_numpy(q).cuda(), torch.from_numpy(gate).cuda(),
+                         torch.tensor(lens, dtype=torch.int32, device="cuda"), max(lens),
+                         torch.from_numpy(table.view(np.int64)).cuda(), k_off, v_off, window, sink).cpu().numpy()
+    # chunk index of table entries -> pool block id
+    base = pool.data_ptr()
+    blocks = ((table.astype(np.int64) - base) // (per_chunk * 2))
+    for s, L in enumerate(lens):
+        K, V = gather_kv(pool, perm, blocks[s], L, layer, per_chunk)
+        ref = O.gqa_decode(q[s], gate[s], K, V, window, sink)
+        assert relerr(out[s].reshape(16, 256), ref) < TOL
+
+
+def test_preprocess_writes_kv_rows_and_rope():
+    rng = np.random.default_rng(7)
+    lens = [600, 257]
+    pool, perm, table, per_chunk = make_pool(rng, lens, 1)
+    n = len(lens)
+    pos = np.array([599, 256], dtype=np.int32)
+    qkv = rng.normal(0, 1, (n, 10240)).astype(np.float32)
+    qn = np.abs(rng.normal(1, 0.1, 256)).astype(np.float32)
+    kn = np.abs(rng.normal(1, 0.1, 256)).astype(np.float32)
+    freq = O.rope_freqs(1.0e7)
+    from qwowl35_b200 import ops
+    q, gate = ops.attn_preprocess(torch.from_numpy(qkv).cuda(), torch.from_numpy(qn).cuda(),
+                                  torch.from_numpy(kn).cuda(), torch.from_numpy(freq).cuda(),
+                                  torch.from_numpy(pos).cuda(), torch.from_numpy(table.view(np.int64)).cuda(),
+                                  0, PLANE * 2)
+    torch.cuda.synchronize()
+    base = pool.data_ptr()
+    blocks = ((table.astype(np.int64) - base) // (per_chunk * 2))
+    for s in range(n):
+        rq, rg, rk, rv = O.attn_preprocess(qkv[s, :8192], qkv[s, 8192:9216], qkv[s, 9216:], qn, kn, int(pos[s]), freq)
+        assert relerr(q[s].cpu().numpy(), rq) < 1e-5
+        np.testing.assert_array_equal(gate[s].cpu().numpy(), rg.astype(np.float32))
+        K, V = gather_kv(pool, perm, blocks[s], int(pos[s]) + 1, 0, per_chunk)
+        np.testing.assert_array_equal(V[pos[s]], rv)                      # V: exact f16 RNE
+        kd = np.abs(K[pos[s]].astype(np.float32).view(np.int32) if False else
+                    K[pos[s]].view(np.int16).astype(np.int32) - rk.view(np.int16).astype(np.int32))
+        assert kd.max() <= 1                                              # K: within 1 f16 ulp
+
+
+def test_kv_chunk_address_math():
+    table = np.array([7, 3, 9], dtype=np.uint64)
+    assert O.kv_address(table, 0) == (7, 0)
+    assert O.kv_address(table, 255) == (7, 255)
+    assert O.kv_address(table, 256) == (3, 0)
+    assert O.kv_address(table, 700) == (9, 188)

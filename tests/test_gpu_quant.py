@@ -1,0 +1,152 @@
+"""GPU parity of the dequant and fused dequant-matvec kernels against the oracle.
+
+Bit-exact: repack + dequantised weights (all codecs, both GF4 modes) and
+argmax token ids.  Matvec family: max relative error 1e-3 (north-star
+tolerance) measured as max|y - y_ref| / max|y_ref|, fp64 reference.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import ops as O
+from oracle import quants as Q
+from qwowl35_b200 import ops
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+CODECS = [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE]
+
+
+def relerr(y, ref):
+    y = np.asarray(y, dtype=np.float64)
+    return float(np.max(np.abs(y - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def make(t, rows, k, seed=0):
+    rng = np.random.default_rng(seed)
+    raw = Q.gen_weight(rng, t, rows, k)
+    return raw, ops.upload(t, raw, rows, k)
+
+
+@pytest.mark.parametrize("t", CODECS)
+@pytest.mark.parametrize("exact", [False, True])
+def test_dequant_bit_exact(t, exact):
+    if exact and t != Q.GF4_TYPE:
+        pytest.skip("mode only affects GF4")
+    rows, k = 64, 4096
+    raw, w = make(t, rows, k, 1)
+    got = ops.dequant(t, w, rows, k, exact=exact).cpu().numpy()
+    ref = Q.dequant(t, raw, rows, k, gf4_exact=exact)
+    np.testing.assert_array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_gf4_dequant_of_reference_cooker_words():
+    g = np.load("tests/golden/gf4.npz")
+    words = g["words"][:48]
+    raw = words.astype("<u4").view(np.uint8).reshape(-1)
+    w = ops.upload(Q.GF4_TYPE, raw, 48, 512)
+    got = ops.dequant(Q.GF4_TYPE, w, 48, 512, exact=True).cpu().numpy()
+    np.testing.assert_array_equal(got.view(np.uint32), g["x_hat"][:48].astype(np.float32).view(np.uint32))
+
+
+def test_q8_0_and_q4_k_dequant_of_gguf_golden():
+    g = np.load("tests/golden/q8_0.npz")
+    w = ops.upload(Q.Q8_0_TYPE, g["raw"], 32, 256)
+    np.testing.assert_array_equal(ops.dequant(Q.Q8_0_TYPE, w, 32, 256).cpu().numpy().view(np.uint32),
+                                  g["deq"].view(np.uint32))
+    g = np.load("tests/golden/q4_k.npz")
+    w = ops.upload(Q.Q4_K_TYPE, g["raw"], 16, 1024)
+    np.testing.assert_array_equal(ops.dequant(Q.Q4_K_TYPE, w, 16, 1024).cpu().numpy().view(np.uint32),
+                                  g["deq"].view(np.uint32))
+
+
+@pytest.mark.parametrize("t", CODECS)
+@pytest.mark.parametrize("shape", [(12288, 4096), (4096, 12288), (1024, 4096), (80, 256), (333, 1280)])
+@pytest.mark.parametrize("b", [1, 2, 3])
+def test_matvec_parity(t, shape, b):
+    rows, k = shape
+    raw, w = make(t, rows, k, 2)
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((b, k)).astype(np.float32)
+    y = ops.matvec(t, w, torch.from_numpy(x).cuda(), rows, k).cpu().numpy()
+    ref = O.matvec(Q.dequant(t, raw, rows, k), x)
+    assert relerr(y, ref) < TOL
+
+
+@pytest.mark.parametrize("t", CODECS)
+def test_matvec_f16_input_and_accumulate(t):
+    rows, k = 4096, 4096
+    raw, w = make(t, rows, k, 4)
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((2, k)).astype(np.float16)
+    base = rng.standard_normal((2, rows)).astype(np.float32)
+    y = torch.from_numpy(base.copy()).cuda()
+    ops.matvec(t, w, torch.from_numpy(x).cuda(), rows, k, y=y, accumulate=True)
+    ref = base + O.matvec(Q.dequant(t, raw, rows, k), x.astype(np.float32))
+    assert relerr(y.cpu().numpy(), ref) < TOL
+
+
+def test_gf4_exact_mode_matvec():
+    rows, k = 2048, 4096
+    raw, w = make(Q.GF4_TYPE, rows, k, 6)
+    x = np.random.default_rng(7).standard_normal((1, k)).astype(np.float32)
+    y = ops.matvec(Q.GF4_TYPE, w, torch.from_numpy(x).cuda(), rows, k, exact=True).cpu().numpy()
+    assert relerr(y, O.matvec(Q.dequant(Q.GF4_TYPE, raw, rows, k, gf4_exact=True), x)) < TOL
+
+
+@pytest.mark.parametrize("t", CODECS)
+@pytest.mark.parametrize("b", [1, 2, 5])
+def test_gate_up_swiglu(t, b):
+    rows, k = 12288, 4096
+    rawg, wg = make(t, rows, k, 8)
+    rawu, wu = make(t, rows, k, 9)
+    x = np.random.default_rng(10).standard_normal((b, k)).astype(np.float32)
+    h = ops.gate_up_swiglu(t, wg, wu, torch.from_numpy(x).cuda(), rows, k).cpu().numpy()
+    ref = O.gate_up_swiglu(Q.dequant(t, rawg, rows, k), Q.dequant(t, rawu, rows, k), x)
+    assert relerr(h, ref) < TOL
+
+
+@pytest.mark.parametrize("t", [Q.Q8_0_TYPE, Q.GF4_TYPE])
+@pytest.mark.parametrize("b", [1, 3])
+def test_argmax_head_matches_logits_bit_exact(t, b):
+    rows, k = 50000, 4096
+    raw, w = make(t, rows, k, 11)
+    x = np.random.default_rng(12).standard_normal((b, k)).astype(np.float32)
+    tok, val, logits = ops.argmax_head(t, w, torch.from_numpy(x).cuda(), rows, k, want_logits=True)
+    logits = logits.cpu().numpy()
+    for i in range(b):
+        ref_id, ref_v = O.argmax_lowest(logits[i])
+        assert int(tok[i]) == ref_id and float(val[i]) == ref_v
+    ref = O.matvec(Q.dequant(t, raw, rows, k), x)
+    assert relerr(logits, ref) < TOL
+    for i in range(b):
+        top2 = np.sort(ref[i])[-2:]
+        if top2[1] - top2[0] > 1e-3 * np.abs(ref[i]).max():
+            assert int(tok[i]) == int(np.argmax(ref[i]))
+
+
+def test_argmax_ties_resolve_to_lowest_id():
+    # rows identical -> identical logits everywhere: the lowest id must win
+    rows, k = 4096, 256
+    rng = np.random.default_rng(13)
+    one = Q.gen_weight(rng, Q.Q8_0_TYPE, 1, k)
+    raw = np.tile(one, rows)
+    w = ops.upload(Q.Q8_0_TYPE, raw, rows, k)
+    x = torch.from_numpy(rng.standard_normal((2, k)).astype(np.float32)).cuda()
+    tok, _, _ = ops.argmax_head(Q.Q8_0_TYPE, w, x, rows, k)
+    assert tok.tolist() == [0, 0]
+    # a duplicated maximum late in the vocabulary: lowest of the two ids
+    raw2 = Q.gen_weight(rng, Q.Q8_0_TYPE, rows, k)
+    blk = Q.row_bytes(Q.Q8_0_TYPE, k)
+    raw2[3000 * blk:3001 * blk] = raw2[1234 * blk:1235 * blk]
+    w2 = ops.upload(Q.Q8_0_TYPE, raw2, rows, k)
+    _, _, logits = ops.argmax_head(Q.Q8_0_TYPE, w2, x, rows, k, want_logits=True)
+    lg = logits.cpu().numpy()
+    # force the duplicated rows to be the maximum by choosing x along row 1234
+    deq = Q.dequant(Q.Q8_0_TYPE, raw2, rows, k)
+    xs = torch.from_numpy(np.stack([deq[1234], deq[1234]]).astype(np.float32)).cuda()
+    tok2, _, lg2 = ops.argmax_head(Q.Q8_0_TYPE, w2, xs, rows, k, want_logits=True)
+    lg2 = lg2.cpu().numpy()
+    if lg2[0, 1234] == lg2[0].max():
+        assert tok2.tolist() == [1234, 1234]
+    assert lg.shape == (2, rows)

@@ -1,0 +1,148 @@
+"""End-to-end decode through the drop-in C ABI (qw35_metal_* and the batched
+extensions) on a small synthetic model, against the fp64 oracle model."""
+import numpy as np
+import pytest
+
+from oracle.model import OracleModel
+from qwowl35_b200 import synth
+from qwowl35_b200.runtime import LogitsMode, Runtime
+from qwowl35_b200._lib import Qw35Error
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def relerr(y, ref):
+    return float(np.max(np.abs(np.asarray(y, np.float64) - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def small():
+    cfg = synth.ModelConfig(layers=4, ffn=1024, vocab=4096)
+    return synth.build(cfg, seed=3)
+
+
+TOKENS = [17, 4000, 5, 123, 77, 2048, 9]
+
+
+def test_full_logits_match_oracle(small):
+    rt = Runtime(small, ctx=512)
+    orc = OracleModel(small)
+    for pos, tok in enumerate(TOKENS):
+        rt.eval_token(tok, pos, LogitsMode.FULL)
+        got = rt.copy_logits()
+        ref = orc.step(tok, pos)
+        assert relerr(got, ref) < TOL, pos
+    rt.close()
+
+
+def test_argmax_mode_equals_full_logits_argmax(small):
+    rt = Runtime(small, ctx=512)
+    full = []
+    for pos, tok in enumerate(TOKENS):
+        rt.eval_token(tok, pos, LogitsMode.FULL)
+        full.append(rt.copy_logits())
+    rt.reset()
+    for pos, tok in enumerate(TOKENS):
+        rt.eval_token(tok, pos, LogitsMode.ARGMAX)
+        t, v = rt.argmax()
+        m = full[pos].max()
+        assert t == int(np.flatnonzero(full[pos] == m)[0]) and v == m
+    rt.close()
+
+
+def test_prefill_chunk_equals_token_steps(small):
+    rt = Runtime(small, ctx=512, prefill_chunk=8)
+    rt.eval_prefill_chunk(TOKENS, 0, LogitsMode.FULL)
+    a = rt.copy_logits()
+    rt.reset()
+    for pos, tok in enumerate(TOKENS):
+        rt.eval_token(tok, pos, LogitsMode.FULL if pos == len(TOKENS) - 1 else LogitsMode.NONE)
+    b = rt.copy_logits()
+    np.testing.assert_array_equal(a, b)
+    rt.close()
+
+
+def test_batch_equals_single_sequence_bitwise(small):
+    seqs = [[3, 9, 27, 81], [100, 200, 300, 400], [4095, 0, 1, 2]]
+    single = []
+    rt1 = Runtime(small, ctx=512)
+    for s in seqs:
+        rt1.reset()
+        for pos, tok in enumerate(s):
+            rt1.eval_token(tok, pos, LogitsMode.FULL)
+        single.append(rt1.copy_logits())
+    rt1.close()
+    rt = Runtime(small, ctx=512, max_seqs=4)
+    ids = [0] + [rt.seq_alloc() for _ in range(2)]
+    for pos in range(4):
+        rt.eval_batch(ids, [s[pos] for s in seqs], [pos] * 3, LogitsMode.FULL)
+    out = rt.copy_logits_batch(3)
+    for i in range(3):
+        np.testing.assert_array_equal(out[i], single[i])
+    rt.close()
+
+
+def test_ragged_positions_in_one_batch(small):
+    rt = Runtime(small, ctx=2048, max_seqs=2)
+    b = rt.seq_alloc()
+    orc0, orc1 = OracleModel(small), OracleModel(small)
+    # sequence 0 runs ahead alone past a chunk boundary, then both step together
+    for pos in range(300):
+        rt.eval_token(pos % 4096, pos, LogitsMode.NONE)
+        orc0.step(pos % 4096, pos)
+    rt.eval_batch([0, b], [11, 12], [300, 0], LogitsMode.FULL)
+    got = rt.copy_logits_batch(2)
+    assert relerr(got[0], orc0.step(11, 300)) < TOL
+    assert relerr(got[1], orc1.step(12, 0)) < TOL
+    rt.close()
+
+
+def test_state_export_import_replays_bitwise(small):
+    rt = Runtime(small, ctx=512)
+    for pos, tok in enumerate(TOKENS[:3]):
+        rt.eval_token(tok, pos, LogitsMode.NONE)
+    st = rt.state_export()
+    assert len(st) == rt.state_size() == 3 * (8192 * 3 + 32 * 128 * 128) * 4
+    rt.eval_token(TOKENS[3], 3, LogitsMode.NONE)
+    rt.eval_token(TOKENS[4], 4, LogitsMode.FULL)
+    a = rt.copy_logits()
+    rt.state_import(st)
+    rt.eval_token(TOKENS[3], 3, LogitsMode.NONE)
+    rt.eval_token(TOKENS[4], 4, LogitsMode.FULL)
+    np.testing.assert_array_equal(a, rt.copy_logits())
+    with pytest.raises(Qw35Error, match="size mismatch"):
+        rt.state_import(st[:-4])
+    rt.close()
+
+
+def test_host_side_guards(small):
+    rt = Runtime(small, ctx=64)
+    with pytest.raises(Qw35Error, match="exceeds allocated context"):
+        rt.eval_token(1, 64)
+    with pytest.raises(Qw35Error, match="outside the Qw35 vocabulary"):
+        rt.eval_token(4096, 0)
+    rt.eval_token(1, 0, LogitsMode.NONE)
+    with pytest.raises(Qw35Error, match="argmax"):
+        rt.argmax()
+    rt.set_ctx_size(32)          # lower: no-op success
+    rt.set_ctx_size(128)
+    rt.eval_token(2, 100, LogitsMode.ARGMAX)
+    with pytest.raises(Qw35Error, match="exceeds the maximum"):
+        rt.set_ctx_size(1 << 20)
+    with pytest.raises(Qw35Error):
+        rt.seq_alloc()           # only one slot
+    rt.close()
+    with pytest.raises(Qw35Error, match="not implemented"):
+        Runtime(small, ctx=64, kv_cache_type=1)
+
+
+def test_window_and_sink_match_oracle(small):
+    rt = Runtime(small, ctx=1024, window=64, sink=4)
+    orc = OracleModel(small, window=64, sink=4)
+    for pos in range(80):
+        mode = LogitsMode.FULL if pos == 79 else LogitsMode.NONE
+        rt.eval_token((pos * 7) % 4096, pos, mode)
+        ref = orc.step((pos * 7) % 4096, pos)
+    assert relerr(rt.copy_logits(), ref) < TOL
+    rt.close()
