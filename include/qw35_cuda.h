@@ -44,6 +44,9 @@ extern "C" {
 int qw35_cuda_device_count(void);
 int qw35_cuda_set_device(int device, char *err, uintptr_t err_len);
 const char *qw35_cuda_build_info(void);
+// Bounded device-side waits record a nonzero code here instead of hanging;
+// returns the code seen since the last call (0 = none) and clears it.
+uint32_t qw35_cuda_device_error(void);
 
 // Weights ---------------------------------------------------------------------
 // Bytes of a rows x k matrix of `type_id` (identical for GGUF and device layouts).

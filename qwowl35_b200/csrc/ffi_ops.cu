@@ -53,6 +53,8 @@ int qw35_cuda_set_device(int device, char *err, uintptr_t err_len) {
     return cuda_ok(cudaSetDevice(device), "cudaSetDevice", err, err_len);
 }
 
+uint32_t qw35_cuda_device_error(void) { return qw35::device_error_read_and_clear(); }
+
 const char *qw35_cuda_build_info(void) { return "qw35cuda sm_100a (" __DATE__ ")"; }
 
 uint64_t qw35_cuda_weight_bytes(uint32_t type_id, uint32_t rows, uint32_t k) {

@@ -9,25 +9,29 @@
 //   qw35_output_argmax_reduce_partials_f32       qw35_output.metal:141-182
 //   qw35_rms_norm_weight_f32 (fused as a prologue) qw35_core.metal:14-48
 //
-// Design (B200): the activation row stays in REGISTERS for the whole launch.
-// A CTA is KW x RS warps: KW warps span K (lane l of warp kw owns the 32
-// consecutive columns of chunk kw*32+l), RS independent row streams walk the
-// CTA's contiguous row range in groups of G rows.  Every weight byte is
-// loaded exactly once with a 128-bit non-allocating load; x is read once per
-// CTA (not once per row), so the only steady-state traffic is the weight
-// stream.  Per-row partials reduce with warp shuffles, then across the KW
-// warps through shared memory.  The grid is persistent (<= resident CTAs),
-// rows are split evenly across CTAs.
+// B200 design.  A persistent CTA owns a contiguous range of rows.  One
+// producer warp streams the packed weights of G-row groups into a ring of
+// shared-memory stages with bulk copies (the TMA engine, untiled, L2
+// evict-first) completing on mbarriers; it starts before the previous kernel
+// has finished (programmatic dependent launch), because weights do not
+// depend on it.  KW x RS consumer warps then wait for the activation row
+// (griddepcontrol.wait), keep it in registers for the whole launch (lane l of
+// warp kw owns the 32 columns of chunk kw*32+l), and decode every code with
+// one logic op + one FMA (quant.cuh "fast decode").  Per-row partials reduce
+// with warp shuffles, then across the KW warps through shared memory.
 #include <cstdio>
-#include <mutex>
+#include <cstdlib>
 
 #include "common.cuh"
-#include "quant.cuh"
 #include "ops.h"
+#include "pipe.cuh"
+#include "quant.cuh"
 
 namespace qw35 {
 
 enum MvMode { MV_STORE = 0, MV_ACCUM = 1, MV_SWIGLU = 2, MV_ARGMAX = 3 };
+
+constexpr int kStages = 4;
 
 struct MvParams {
     const uint8_t *w0;
@@ -38,60 +42,15 @@ struct MvParams {
     float *y;            // [B][rows] (MV_ARGMAX: optional logits)
     float *part_val;     // MV_ARGMAX partials [grid][B]
     uint32_t *part_idx;
-    int rows, K, rows_per_cta, kw;
+    int rows, K, rows_per_cta, kw, rs, G;
+    uint32_t code_row, scale_row;  // bytes per row in the codes / scales planes
+    uint32_t stage_bytes;          // per matrix
 };
 
-template <int CODEC> struct CodecTraits;
-template <> struct CodecTraits<QW35_GF4_TYPE> { static constexpr int G = 8; };
-template <> struct CodecTraits<QW35_Q8_0_TYPE> { static constexpr int G = 4; };
-template <> struct CodecTraits<QW35_Q4_K_TYPE> { static constexpr int G = 8; };
-
-template <int CODEC>
-struct ChunkLoad {
-    uint4 a, b;      // codes (b only for Q8_0)
-    uint32_t s;      // Q8_0 fp16 scale bits
-    uint4 h;         // Q4_K header
-};
-
-template <int CODEC>
-__device__ __forceinline__ void load_chunk(ChunkLoad<CODEC> &L, const uint8_t *w, int rows, int K, int row, int c) {
-    if constexpr (CODEC == QW35_GF4_TYPE) {
-        L.a = ldg_stream(w + (size_t)row * (K / 2) + (size_t)c * 16);
-    } else if constexpr (CODEC == QW35_Q8_0_TYPE) {
-        const uint8_t *codes = w + (size_t)row * K + (size_t)c * 32;
-        L.a = ldg_stream(codes);
-        L.b = ldg_stream(codes + 16);
-        const uint16_t *sc = reinterpret_cast<const uint16_t *>(w + (size_t)rows * K);
-        L.s = __ldg(sc + (size_t)row * (K / 32) + c);
-    } else {
-        L.a = ldg_stream(w + (size_t)row * (K / 2) + (size_t)c * 16);
-        const uint8_t *hdr = w + (size_t)rows * (K / 2) + ((size_t)row * (K / 256) + (c >> 3)) * 16;
-        L.h = __ldg(reinterpret_cast<const uint4 *>(hdr));
-    }
-}
-
-template <int CODEC, bool EXACT>
-__device__ __forceinline__ float chunk_dot(const ChunkLoad<CODEC> &L, const float *x, const float *aux, int c) {
-    if constexpr (CODEC == QW35_GF4_TYPE) {
-        // aux[0..3] = 4*sum(x) per word, aux[4..7] = x_4 * 2^-13 per word
-        float r = gf4_word_dot<EXACT>(L.a.x, x + 0, aux[0], aux[4]);
-        r += gf4_word_dot<EXACT>(L.a.y, x + 8, aux[1], aux[5]);
-        r += gf4_word_dot<EXACT>(L.a.z, x + 16, aux[2], aux[6]);
-        r += gf4_word_dot<EXACT>(L.a.w, x + 24, aux[3], aux[7]);
-        return r;
-    } else if constexpr (CODEC == QW35_Q8_0_TYPE) {
-        const float d = __half2float(__ushort_as_half((unsigned short)L.s));
-        return q8_chunk_dot(L.a, L.b, x) * d;
-    } else {
-        float dl, ml;
-        q4k_scale_min(L.h, c & 7, dl, ml);
-        float acc = q4_word_dot(L.a.x, x + 0);
-        acc += q4_word_dot(L.a.y, x + 8);
-        acc += q4_word_dot(L.a.z, x + 16);
-        acc += q4_word_dot(L.a.w, x + 24);
-        return dl * acc - ml * aux[0];  // aux[0] = sum of the chunk's x
-    }
-}
+template <int CODEC> struct Codec;
+template <> struct Codec<QW35_GF4_TYPE> { static constexpr int NC = 8; };   // per-lane constants per b
+template <> struct Codec<QW35_Q8_0_TYPE> { static constexpr int NC = 1; };
+template <> struct Codec<QW35_Q4_K_TYPE> { static constexpr int NC = 2; };
 
 template <typename XT>
 __device__ __forceinline__ void load_x32(float *dst, const XT *src) {
@@ -99,14 +58,14 @@ __device__ __forceinline__ void load_x32(float *dst, const XT *src) {
         const float4 *p = reinterpret_cast<const float4 *>(src);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const float4 v = __ldg(p + i);
+            const float4 v = p[i];
             dst[4 * i] = v.x; dst[4 * i + 1] = v.y; dst[4 * i + 2] = v.z; dst[4 * i + 3] = v.w;
         }
     } else {
         const uint4 *p = reinterpret_cast<const uint4 *>(src);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const uint4 v = __ldg(p + i);
+            const uint4 v = p[i];
             const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -118,37 +77,171 @@ __device__ __forceinline__ void load_x32(float *dst, const XT *src) {
     }
 }
 
-constexpr int kMaxKW = 16;
+// Turn the lane's 32 activations into the codec's scaled form + constants.
+template <int CODEC, bool EXACT>
+__device__ __forceinline__ void prep_x(float *xs, float *cst) {
+    if constexpr (CODEC == QW35_GF4_TYPE) {
+#pragma unroll
+        for (int wd = 0; wd < 4; ++wd) {
+            float s = 0.0f, sx = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float x = xs[8 * wd + j];
+                s += x;
+                sx += x * gf4_xscale(j);
+            }
+            const float x4 = xs[8 * wd + 4];
+            cst[wd] = sx + 4.0f * s + (EXACT ? 0.0f : 0.5f * x4);
+            cst[4 + wd] = 0.5f * x4;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) xs[8 * wd + j] *= gf4_xscale(j);
+        }
+    } else if constexpr (CODEC == QW35_Q8_0_TYPE) {
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s += xs[i];
+        cst[0] = kQ8Bias * s;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) xs[i] *= kQ8Scale;
+    } else {
+        float s = 0.0f, sx = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            s += xs[i];
+            xs[i] *= q4_xscale(i & 7);
+            sx += xs[i];
+        }
+        cst[0] = sx;
+        cst[1] = s;
+    }
+}
 
+// Dot of the lane's chunk of one row (weights in shared memory) with x.
+template <int CODEC, bool EXACT>
+__device__ __forceinline__ float chunk_fast(const uint8_t *codes, const uint8_t *scales, int c, const float *xs,
+                                            const float *cst) {
+    if constexpr (CODEC == QW35_GF4_TYPE) {
+        const uint4 w = *reinterpret_cast<const uint4 *>(codes + c * 16);
+        float r = gf4_word_fast<EXACT>(w.x, xs + 0, cst[0], cst[4]);
+        r += gf4_word_fast<EXACT>(w.y, xs + 8, cst[1], cst[5]);
+        r += gf4_word_fast<EXACT>(w.z, xs + 16, cst[2], cst[6]);
+        r += gf4_word_fast<EXACT>(w.w, xs + 24, cst[3], cst[7]);
+        return r;
+    } else if constexpr (CODEC == QW35_Q8_0_TYPE) {
+        const uint4 a = *reinterpret_cast<const uint4 *>(codes + c * 32);
+        const uint4 b = *reinterpret_cast<const uint4 *>(codes + c * 32 + 16);
+        const unsigned short sb = *reinterpret_cast<const unsigned short *>(scales + c * 2);
+        float acc = -cst[0];
+        acc = q8_word_fast(a.x, xs + 0, acc);
+        acc = q8_word_fast(a.y, xs + 4, acc);
+        acc = q8_word_fast(a.z, xs + 8, acc);
+        acc = q8_word_fast(a.w, xs + 12, acc);
+        acc = q8_word_fast(b.x, xs + 16, acc);
+        acc = q8_word_fast(b.y, xs + 20, acc);
+        acc = q8_word_fast(b.z, xs + 24, acc);
+        acc = q8_word_fast(b.w, xs + 28, acc);
+        return acc * __half2float(__ushort_as_half(sb));
+    } else {
+        const uint4 w = *reinterpret_cast<const uint4 *>(codes + c * 16);
+        const uint4 h = *reinterpret_cast<const uint4 *>(scales + (c >> 3) * 16);
+        float dl, ml;
+        q4k_scale_min(h, c & 7, dl, ml);
+        float acc = -cst[0];
+        acc = q4_word_fast(w.x, xs + 0, acc);
+        acc = q4_word_fast(w.y, xs + 8, acc);
+        acc = q4_word_fast(w.z, xs + 16, acc);
+        acc = q4_word_fast(w.w, xs + 24, acc);
+        return dl * acc - ml * cst[1];
+    }
+}
+
+// Shared-memory carve-up (dynamic): [NM][kStages][stage_bytes] weights |
+// [2][G][B][NM][KW] partials | 64 floats scratch | 2*kStages mbarriers | abort.
 template <int CODEC, int B, int MODE, bool EXACT, typename XT>
-__global__ void __launch_bounds__(384) mv_kernel(MvParams p) {
-    constexpr int G = CodecTraits<CODEC>::G;
+__global__ void __launch_bounds__(416, 1) mv_kernel(MvParams p) {
     constexpr int NM = MODE == MV_SWIGLU ? 2 : 1;
-    constexpr int NAUX = CODEC == QW35_GF4_TYPE ? 8 : 1;
-    extern __shared__ float smem[];  // [2 buf][RS][G][B][NM][KW] partials + 32 scratch
+    constexpr int NC = Codec<CODEC>::NC;
+    extern __shared__ __align__(128) uint8_t smem[];
 
-    const int lane = threadIdx.x & 31;
-    const int wid = threadIdx.x >> 5;
-    const int KW = p.kw;
-    const int RS = (blockDim.x >> 5) / KW;
-    const int kw = wid % KW;
-    const int stream = wid / KW;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int KW = p.kw, RS = p.rs, G = p.G;
+    const int ncw = KW * RS;  // consumer warps
+    const int ncons = ncw * 32;
+    const uint32_t SB = p.stage_bytes;
+    uint8_t *wbuf = smem;
+    float *part = reinterpret_cast<float *>(smem + (size_t)NM * kStages * SB);
+    float *red = part + 2 * G * B * NM * KW;
+    uint64_t *full = reinterpret_cast<uint64_t *>(red + 64);
+    uint64_t *empty = full + kStages;
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStages);
+
+    const int r0 = blockIdx.x * p.rows_per_cta;
+    const int r1 = min(p.rows, r0 + p.rows_per_cta);
+    const int ngroups = r1 > r0 ? (r1 - r0 + G - 1) / G : 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], ncw);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+
+    if (wid == ncw) {
+        // ------------------------------ producer ---------------------------
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            const uint8_t *mats[2] = {p.w0, p.w1};
+            const size_t codes_plane = (size_t)p.rows * p.code_row;
+            int issued = 0;
+            for (int g = 0; g < ngroups; ++g) {
+                const int s = g % kStages;
+                if (g >= kStages && !*abort_flag) {
+                    if (!mbar_wait(&empty[s], ((g / kStages) - 1) & 1, 1u)) *abort_flag = 1;
+                }
+                if (*abort_flag) break;
+                const int row0 = r0 + g * G;
+                const int nr = min(G, r1 - row0);
+                const uint32_t cb = nr * p.code_row, sbytes = nr * p.scale_row;
+                mbar_arrive_expect_tx(&full[s], NM * (cb + sbytes));
+#pragma unroll
+                for (int m = 0; m < NM; ++m) {
+                    uint8_t *dst = wbuf + ((size_t)m * kStages + s) * SB;
+                    bulk_g2s(dst, mats[m] + (size_t)row0 * p.code_row, cb, &full[s], pol);
+                    if (sbytes)
+                        bulk_g2s(dst + (size_t)G * p.code_row, mats[m] + codes_plane + (size_t)row0 * p.scale_row,
+                                 sbytes, &full[s], pol);
+                }
+                issued = g + 1;
+            }
+            if (*abort_flag) {  // never leave with copies in flight
+                for (int g = max(0, issued - kStages); g < issued; ++g)
+                    mbar_wait(&full[g % kStages], (g / kStages) & 1, 4u);
+            }
+        }
+        return;
+    }
+
+    // -------------------------------- consumers ------------------------------
+    const int kw = wid % KW, rs = wid / KW;
     const int nchunk = p.K >> 5;
     const int c = kw * 32 + lane;
     const bool active = c < nchunk;
-    float *red = smem + 2 * RS * G * B * NM * KW;  // 32 + B floats of scratch
+    pdl_wait();  // the activation row is written by the previous kernel
 
-    // ---- x (+ fused RMS norm) into registers -------------------------------
-    float xr[B][32];
-    float aux[B][NAUX];
+    float xs[B][32];
+    float cst[B][NC];
     const XT *xg = reinterpret_cast<const XT *>(p.x);
 #pragma unroll
     for (int b = 0; b < B; ++b) {
         if (active) {
-            load_x32<XT>(xr[b], xg + (size_t)b * p.K + (size_t)c * 32);
+            load_x32<XT>(xs[b], xg + (size_t)b * p.K + (size_t)c * 32);
         } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) xr[b][i] = 0.0f;
+            for (int i = 0; i < 32; ++i) xs[b][i] = 0.0f;
         }
     }
     if (p.norm_w != nullptr) {
@@ -156,117 +249,94 @@ __global__ void __launch_bounds__(384) mv_kernel(MvParams p) {
         for (int b = 0; b < B; ++b) {
             float ss = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ss = fmaf(xr[b][i], xr[b][i], ss);
+            for (int i = 0; i < 32; ++i) ss = fmaf(xs[b][i], xs[b][i], ss);
             ss = warp_sum(ss);
-            if (lane == 0 && stream == 0) red[kw] = ss;
-            __syncthreads();
+            if (lane == 0 && rs == 0) red[kw] = ss;
+            named_sync(1, ncons);
             float tot = 0.0f;
             for (int i = 0; i < KW; ++i) tot += red[i];
-            __syncthreads();
+            named_sync(1, ncons);
             const float inv = rsqrtf(tot / (float)p.K + p.eps);
             if (active) {
                 const float4 *nw = reinterpret_cast<const float4 *>(p.norm_w + (size_t)c * 32);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const float4 w4 = __ldg(nw + i);
-                    xr[b][4 * i] = xr[b][4 * i] * inv * w4.x;
-                    xr[b][4 * i + 1] = xr[b][4 * i + 1] * inv * w4.y;
-                    xr[b][4 * i + 2] = xr[b][4 * i + 2] * inv * w4.z;
-                    xr[b][4 * i + 3] = xr[b][4 * i + 3] * inv * w4.w;
+                    xs[b][4 * i] = xs[b][4 * i] * inv * w4.x;
+                    xs[b][4 * i + 1] = xs[b][4 * i + 1] * inv * w4.y;
+                    xs[b][4 * i + 2] = xs[b][4 * i + 2] * inv * w4.z;
+                    xs[b][4 * i + 3] = xs[b][4 * i + 3] * inv * w4.w;
                 }
             }
         }
     }
 #pragma unroll
-    for (int b = 0; b < B; ++b) {
-        if constexpr (CODEC == QW35_GF4_TYPE) {
-#pragma unroll
-            for (int wd = 0; wd < 4; ++wd) {
-                float s = 0.0f;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) s += xr[b][8 * wd + j];
-                aux[b][wd] = 4.0f * s;
-                aux[b][4 + wd] = xr[b][8 * wd + 4] * 0.0001220703125f;
-            }
-        } else {
-            float s = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) s += xr[b][i];
-            aux[b][0] = s;
-        }
-    }
+    for (int b = 0; b < B; ++b) prep_x<CODEC, EXACT>(xs[b], cst[b]);
 
-    // ---- stream the CTA's rows -------------------------------------------
-    const int r0 = blockIdx.x * p.rows_per_cta;
-    const int r1 = min(p.rows, r0 + p.rows_per_cta);
-    const int iters = (p.rows_per_cta + RS * G - 1) / (RS * G);
-    float best_v[B];
-    uint32_t best_i[B];
-#pragma unroll
-    for (int b = 0; b < B; ++b) { best_v[b] = -INFINITY; best_i[b] = 0xffffffffu; }
-    const int fin_slots = RS * G * B;  // finaliser threads, one per (stream, g, b)
+    float best_v = -INFINITY;
+    uint32_t best_i = 0xffffffffu;
+    const int fin_slots = G * B;
     const int ft = threadIdx.x;
-    const int f_s = ft / (G * B), f_g = (ft / B) % G, f_b = ft % B;
+    const int f_i = ft / B, f_b = ft % B;
 
-    for (int it = 0; it < iters; ++it) {
-        const int base = r0 + (it * RS + stream) * G;
-        float acc[NM][G][B];
+    for (int g = 0; g < ngroups; ++g) {
+        const int s = g % kStages;
+        if (!*abort_flag) {
+            if (!mbar_wait(&full[s], (g / kStages) & 1, 2u)) *abort_flag = 1;
+        }
+        const int row0 = r0 + g * G;
+        const int nr = min(G, r1 - row0);
+        float *pg = part + (g & 1) * G * B * NM * KW;
+        for (int i = rs; i < G; i += RS) {
+            float acc[NM][B];
 #pragma unroll
-        for (int m = 0; m < NM; ++m) {
-            ChunkLoad<CODEC> L[G];
-#pragma unroll
-            for (int g = 0; g < G; ++g)
-                if (active && base + g < r1) load_chunk<CODEC>(L[g], m ? p.w1 : p.w0, p.rows, p.K, base + g, c);
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
+            for (int m = 0; m < NM; ++m) {
+                const uint8_t *st = wbuf + ((size_t)m * kStages + s) * SB;
+                const uint8_t *codes = st + (size_t)i * p.code_row;
+                const uint8_t *scales = st + (size_t)G * p.code_row + (size_t)i * p.scale_row;
 #pragma unroll
                 for (int b = 0; b < B; ++b)
-                    acc[m][g][b] = (active && base + g < r1) ? chunk_dot<CODEC, EXACT>(L[g], xr[b], aux[b], c) : 0.0f;
+                    acc[m][b] = (active && i < nr) ? chunk_fast<CODEC, EXACT>(codes, scales, c, xs[b], cst[b]) : 0.0f;
             }
-        }
-        float *part = smem + (it & 1) * RS * G * B * NM * KW;
 #pragma unroll
-        for (int m = 0; m < NM; ++m)
-#pragma unroll
-            for (int g = 0; g < G; ++g)
+            for (int m = 0; m < NM; ++m)
 #pragma unroll
                 for (int b = 0; b < B; ++b) {
-                    const float v = warp_sum(acc[m][g][b]);
-                    if (lane == 0) part[(((stream * G + g) * B + b) * NM + m) * KW + kw] = v;
+                    const float v = warp_sum(acc[m][b]);
+                    if (lane == 0) pg[((i * B + b) * NM + m) * KW + kw] = v;
                 }
-        __syncthreads();
-        if (ft < fin_slots) {
-            const int row = r0 + (it * RS + f_s) * G + f_g;
-            if (row < r1) {
-                const float *pp = part + ((f_s * G + f_g) * B + f_b) * NM * KW;
-                float s0 = 0.0f;
-                for (int i = 0; i < KW; ++i) s0 += pp[i];
-                float *yo = p.y + (size_t)f_b * p.rows + row;
-                if constexpr (MODE == MV_STORE) {
-                    *yo = s0;
-                } else if constexpr (MODE == MV_ACCUM) {
-                    *yo += s0;
-                } else if constexpr (MODE == MV_SWIGLU) {
-                    float s1 = 0.0f;
-                    for (int i = 0; i < KW; ++i) s1 += pp[KW + i];
-                    *yo = silu_f(s0) * s1;
-                } else {
-                    if (p.y != nullptr) *yo = s0;
-                    // rows arrive in increasing order per thread: strict > keeps the lowest id
-                    if (s0 > best_v[0]) { best_v[0] = s0; best_i[0] = (uint32_t)row; }
-                }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage
+        named_sync(1, ncons);
+        if (ft < fin_slots && f_i < nr) {
+            const int row = row0 + f_i;
+            const float *pp = pg + (f_i * B + f_b) * NM * KW;
+            float s0 = 0.0f;
+            for (int k = 0; k < KW; ++k) s0 += pp[k];
+            float *yo = p.y + (size_t)f_b * p.rows + row;
+            if constexpr (MODE == MV_STORE) {
+                *yo = s0;
+            } else if constexpr (MODE == MV_ACCUM) {
+                *yo += s0;
+            } else if constexpr (MODE == MV_SWIGLU) {
+                float s1 = 0.0f;
+                for (int k = 0; k < KW; ++k) s1 += pp[KW + k];
+                *yo = silu_f(s0) * s1;
+            } else {
+                if (p.y != nullptr) *yo = s0;
+                if (s0 > best_v) { best_v = s0; best_i = (uint32_t)row; }  // rows ascend: keeps lowest id
             }
         }
-        // the double-buffered partials make one barrier per group sufficient
+        // partials are double-buffered by group parity: one barrier per group
     }
 
     if constexpr (MODE == MV_ARGMAX) {
-        // reduce (best_v, best_i) of the finaliser threads per batch row b
-        __syncthreads();
-        float *bv = smem;
-        uint32_t *bi = reinterpret_cast<uint32_t *>(smem + fin_slots);
-        if (ft < fin_slots) { bv[ft] = best_v[0]; bi[ft] = best_i[0]; }
-        __syncthreads();
+        named_sync(1, ncons);
+        float *bv = red;  // fin_slots = G * B <= 32
+        uint32_t *bi = reinterpret_cast<uint32_t *>(red + 32);
+        if (ft < fin_slots) { bv[ft] = best_v; bi[ft] = best_i; }
+        named_sync(1, ncons);
         if (ft < B) {
             float v = -INFINITY;
             uint32_t id = 0xffffffffu;
@@ -283,8 +353,8 @@ __global__ void __launch_bounds__(384) mv_kernel(MvParams p) {
 
 // Final argmax over per-CTA partials; ties resolve to the smallest id
 // (qw35_output.metal:141-182).  One CTA of 256 threads per batch row.
-__global__ void argmax_reduce_kernel(const float *pv, const uint32_t *pi, int n, int B,
-                                     uint32_t *out_tok, float *out_val) {
+__global__ void argmax_reduce_kernel(const float *pv, const uint32_t *pi, int n, int B, uint32_t *out_tok,
+                                     float *out_val) {
     __shared__ float sv[256];
     __shared__ uint32_t si[256];
     const int b = blockIdx.x;
@@ -319,31 +389,39 @@ __global__ void argmax_reduce_kernel(const float *pv, const uint32_t *pi, int n,
 // host-side launch
 // ---------------------------------------------------------------------------
 struct MvGeom {
-    int kw, rs, threads, ctas, rows_per_cta;
+    int kw, rs, G, threads, ctas, rows_per_cta;
+    uint32_t code_row, scale_row, stage_bytes;
     size_t smem;
 };
 
+static void codec_rows(uint32_t type_id, int K, uint32_t &code_row, uint32_t &scale_row) {
+    if (type_id == QW35_GF4_TYPE) { code_row = K / 2; scale_row = 0; }
+    else if (type_id == QW35_Q8_0_TYPE) { code_row = K; scale_row = K / 16; }
+    else { code_row = K / 2; scale_row = K / 16; }
+}
+
 template <int CODEC, int B, int MODE>
 static MvGeom mv_geometry(int rows, int K, const void *kern) {
-    constexpr int G = CodecTraits<CODEC>::G;
     constexpr int NM = MODE == MV_SWIGLU ? 2 : 1;
     MvGeom g;
     const int nchunk = K / 32;
     g.kw = (nchunk + 31) / 32;
     g.rs = g.kw >= 8 ? 1 : 8 / g.kw;
-    g.threads = g.kw * g.rs * 32;
-    const size_t part = (size_t)2 * g.rs * G * B * NM * g.kw;
-    const size_t fin = (size_t)2 * g.rs * G * B;
-    g.smem = (part > fin ? part : fin) * sizeof(float) + 64 * sizeof(float);
+    g.threads = (g.kw * g.rs + 1) * 32;
+    codec_rows(CODEC, K, g.code_row, g.scale_row);
+    const uint32_t rb = g.code_row + g.scale_row;
+    g.G = (int)(20 * 1024 / rb);
+    g.G = g.G < 1 ? 1 : (g.G > 16 ? 16 : g.G);
+    g.stage_bytes = ((uint32_t)g.G * rb + 127u) & ~127u;
+    g.smem = (size_t)NM * kStages * g.stage_bytes + (size_t)2 * g.G * B * NM * g.kw * 4 + 64 * 4 +
+             2 * kStages * 8 + 16;
     int occ = 1;
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, g.threads, g.smem);
     if (occ < 1) occ = 1;
     const int max_ctas = qw35h::sm_count() * occ;
-    const int unit = g.rs * G;
-    const int units = (rows + unit - 1) / unit;
-    int ctas = units < max_ctas ? units : max_ctas;
-    const int units_per_cta = (units + ctas - 1) / ctas;
-    g.rows_per_cta = units_per_cta * unit;
+    const int groups = (rows + g.G - 1) / g.G;
+    const int ctas = groups < max_ctas ? groups : max_ctas;
+    g.rows_per_cta = ((groups + ctas - 1) / ctas) * g.G;
     g.ctas = (rows + g.rows_per_cta - 1) / g.rows_per_cta;
     return g;
 }
@@ -351,15 +429,35 @@ static MvGeom mv_geometry(int rows, int K, const void *kern) {
 template <int CODEC, int B, int MODE, bool EXACT, typename XT>
 static cudaError_t mv_launch(MvParams p, cudaStream_t st, int *ctas_out) {
     auto kern = mv_kernel<CODEC, B, MODE, EXACT, XT>;
+    static bool attr_set = false;  // once per kernel instantiation
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
     MvGeom g = mv_geometry<CODEC, B, MODE>(p.rows, p.K, (const void *)kern);
-    if (g.kw > kMaxKW) return cudaErrorInvalidValue;
-    if (g.smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
+    if (g.kw > 12 || g.smem > 200 * 1024) return cudaErrorInvalidValue;
+    if (MODE == MV_ARGMAX && (p.part_val == nullptr || g.G * B > 32)) return cudaErrorInvalidValue;
     p.kw = g.kw;
+    p.rs = g.rs;
+    p.G = g.G;
     p.rows_per_cta = g.rows_per_cta;
+    p.code_row = g.code_row;
+    p.scale_row = g.scale_row;
+    p.stage_bytes = g.stage_bytes;
     if (ctas_out) *ctas_out = g.ctas;
-    if (MODE == MV_ARGMAX && p.part_val == nullptr) return cudaErrorInvalidValue;
-    kern<<<g.ctas, g.threads, g.smem, st>>>(p);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(g.ctas);
+    cfg.blockDim = dim3(g.threads);
+    cfg.dynamicSmemBytes = g.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    static const bool no_pdl = getenv("QW35_NO_PDL") != nullptr;
+    cfg.attrs = attr;
+    cfg.numAttrs = no_pdl ? 0 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 template <int CODEC, int MODE, bool EXACT, typename XT>
@@ -392,21 +490,26 @@ static cudaError_t mv_dispatch(const MatvecArgs &a, MvParams p, int B, cudaStrea
                  : mv_dispatch_codec<MODE, false, float>(a.type_id, p, B, st, ctas);
 }
 
-// Batch rows beyond the register-resident tile are processed in tiles of
-// two; each tile re-reads the weights (from L2 when they fit).
-cudaError_t matvec_run(const MatvecArgs &a, cudaStream_t st) {
+static MvParams base_params(const MatvecArgs &a, int b0) {
     const size_t xes = a.x_dtype == QW35_F16_TYPE ? 2 : 4;
+    MvParams p{};
+    p.w0 = static_cast<const uint8_t *>(a.w0);
+    p.w1 = static_cast<const uint8_t *>(a.w1);
+    p.x = static_cast<const uint8_t *>(a.x) + (size_t)b0 * a.k * xes;
+    p.norm_w = a.norm_w;
+    p.eps = a.eps;
+    p.y = a.y ? a.y + (size_t)b0 * a.rows : nullptr;
+    p.rows = (int)a.rows;
+    p.K = (int)a.k;
+    return p;
+}
+
+// Batch rows beyond the register-resident tile of two are processed in tiles
+// of two; each tile re-reads the weights (from L2 when they fit).
+cudaError_t matvec_run(const MatvecArgs &a, cudaStream_t st) {
     for (int b0 = 0; b0 < a.batch; b0 += 2) {
         const int nb = a.batch - b0 < 2 ? a.batch - b0 : 2;
-        MvParams p{};
-        p.w0 = static_cast<const uint8_t *>(a.w0);
-        p.w1 = static_cast<const uint8_t *>(a.w1);
-        p.x = static_cast<const uint8_t *>(a.x) + (size_t)b0 * a.k * xes;
-        p.norm_w = a.norm_w;
-        p.eps = a.eps;
-        p.y = a.y ? a.y + (size_t)b0 * a.rows : nullptr;
-        p.rows = (int)a.rows;
-        p.K = (int)a.k;
+        MvParams p = base_params(a, b0);
         cudaError_t e;
         switch (a.mode) {
             case MV_STORE: e = mv_dispatch<MV_STORE>(a, p, nb, st, nullptr); break;
@@ -421,36 +524,36 @@ cudaError_t matvec_run(const MatvecArgs &a, cudaStream_t st) {
 
 size_t argmax_workspace_bytes(uint32_t rows, uint32_t batch) {
     (void)rows;
-    const size_t n = (size_t)qw35h::sm_count() * 16;  // >= any persistent grid
-    return n * 2 * ((batch + 1) / 2 * 2) * sizeof(float) * 2 + 256;
+    (void)batch;
+    const size_t n = (size_t)qw35h::sm_count() * 8;  // >= any persistent grid of the head
+    return 2 * n * 2 * sizeof(float) + 256;          // two halves of [n][2]: values | indices
 }
 
 cudaError_t argmax_head_run(const MatvecArgs &a, uint32_t *tok, float *val, void *ws, size_t ws_bytes,
                             cudaStream_t st) {
     if (ws_bytes < argmax_workspace_bytes(a.rows, a.batch)) return cudaErrorInvalidValue;
-    const size_t xes = a.x_dtype == QW35_F16_TYPE ? 2 : 4;
     const size_t half_ws = ws_bytes / 2;
     for (int b0 = 0; b0 < a.batch; b0 += 2) {
         const int nb = a.batch - b0 < 2 ? a.batch - b0 : 2;
-        MvParams p{};
-        p.w0 = static_cast<const uint8_t *>(a.w0);
-        p.x = static_cast<const uint8_t *>(a.x) + (size_t)b0 * a.k * xes;
-        p.norm_w = a.norm_w;
-        p.eps = a.eps;
-        p.y = a.y ? a.y + (size_t)b0 * a.rows : nullptr;
+        MvParams p = base_params(a, b0);
         p.part_val = static_cast<float *>(ws);
         p.part_idx = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(ws) + half_ws);
-        p.rows = (int)a.rows;
-        p.K = (int)a.k;
         int ctas = 0;
         cudaError_t e = mv_dispatch<MV_ARGMAX>(a, p, nb, st, &ctas);
         if (e != cudaSuccess) return e;
-        argmax_reduce_kernel<<<nb, 256, 0, st>>>(p.part_val, p.part_idx, ctas, nb, tok + b0,
-                                                 val ? val + b0 : nullptr);
+        if ((size_t)ctas * nb * 4 > half_ws) return cudaErrorInvalidValue;
+        argmax_reduce_kernel<<<nb, 256, 0, st>>>(p.part_val, p.part_idx, ctas, nb, tok + b0, val ? val + b0 : nullptr);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+unsigned int device_error_read_and_clear() {
+    unsigned int v = 0, z = 0;
+    cudaMemcpyFromSymbol(&v, g_dev_error, sizeof(v));
+    if (v) cudaMemcpyToSymbol(g_dev_error, &z, sizeof(z));
+    return v;
 }
 
 }  // namespace qw35

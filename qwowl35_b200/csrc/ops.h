@@ -104,6 +104,8 @@ struct AttnArgs {
 size_t attn_workspace_bytes(int n_seq, int max_len);
 cudaError_t attn_decode_run(const AttnArgs &a, cudaStream_t st);
 
+unsigned int device_error_read_and_clear();
+
 cudaError_t rms_norm_run(const float *x, const float *w, float *out, int n, int k, float eps, cudaStream_t st);
 
 }  // namespace qw35

@@ -108,3 +108,72 @@ __device__ __forceinline__ float q4_word_dot(uint32_t w, const float *x) {
 }
 
 }  // namespace qw35
+
+// ---------------------------------------------------------------------------
+// Fast decode for the streaming matvec.  Codes are turned into floats with one
+// LOP3/PRMT each by OR-ing them into the mantissa of 1.0f:
+//     f = 1 + q * 2^(p - 23)        (code q placed at mantissa bit p)
+// so f * xs = xs + q * x when xs = x * 2^(23 - p) (an exact power-of-two
+// scaling of the register-resident activation).  The xs terms of a word or
+// block are summed once per lane (the activation row never changes during a
+// launch) and subtracted once per word/block; p is chosen high in the
+// mantissa (>= 8) so the constant part stays within 2^15 of the code part and
+// fp32 rounding stays ~1e-6 relative.
+// ---------------------------------------------------------------------------
+namespace qw35 {
+
+// GF4: code j of the word is moved to mantissa bit 17 (j even) or 20 (j odd)
+// by one of four shifts of the word; xs_j = x_j * (j even ? 64 : 8).
+// cw = sum_j xs_j + 4 * sum_j x_j (+ x_4 / 2 in metal mode); xh = x_4 / 2.
+template <bool EXACT>
+__device__ __forceinline__ float gf4_word_fast(uint32_t w, const float *xs, float cw, float xh) {
+    const uint32_t s0 = w << 9, s1 = w << 3, s2 = w >> 3, s3 = w >> 9;
+    constexpr uint32_t M17 = 7u << 17, M20 = 7u << 20;
+    constexpr uint32_t X17 = 0x3F800000u | (4u << 17), X20 = 0x3F800000u | (4u << 20);
+    float acc = -cw;
+    acc = fmaf(__uint_as_float((s0 & M17) ^ X17), xs[0], acc);
+    acc = fmaf(__uint_as_float((s0 & M20) ^ X20), xs[1], acc);
+    acc = fmaf(__uint_as_float((s1 & M17) ^ X17), xs[2], acc);
+    acc = fmaf(__uint_as_float((s1 & M20) ^ X20), xs[3], acc);
+    acc = fmaf(__uint_as_float((s2 & M17) ^ X17), xs[4], acc);
+    acc = fmaf(__uint_as_float((s2 & M20) ^ X20), xs[5], acc);
+    acc = fmaf(__uint_as_float((s3 & M17) ^ X17), xs[6], acc);
+    acc = fmaf(__uint_as_float((s3 & M20) ^ X20), xs[7], acc);
+    // metal element-4 junk: bits 11..19 as 1 + junk*2^-12, times x_4/2
+    if (!EXACT) acc = fmaf(__uint_as_float((w & 0x000FF800u) | 0x3F800000u), xh, acc);
+    return acc * (e5m2_to_float(w) * -0.25f);
+}
+
+__device__ __forceinline__ float gf4_xscale(int j) { return (j & 1) ? 8.0f : 64.0f; }
+
+// Q8_0: byte k of a code word (biased to u = q + 128) is placed in bits 8..15:
+// f = 1 + u * 2^-15, xs = x * 2^15.  Block constant c = (2^15 + 128) * sum(x).
+__device__ __forceinline__ float q8_word_fast(uint32_t wd, const float *xs, float acc) {
+    const uint32_t wx = wd ^ 0x80808080u;
+    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x3F800000u, 0x7604u)), xs[0], acc);
+    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x3F800000u, 0x7614u)), xs[1], acc);
+    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x3F800000u, 0x7624u)), xs[2], acc);
+    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x3F800000u, 0x7634u)), xs[3], acc);
+    return acc;
+}
+constexpr float kQ8Scale = 32768.0f;
+constexpr float kQ8Bias = 32768.0f + 128.0f;
+
+// Q4_K (element-contiguous nibbles): nibble n goes to mantissa bit 12 (n even)
+// or 16 (n odd); xs_n = x_n * (n even ? 2^11 : 2^7).
+__device__ __forceinline__ float q4_word_fast(uint32_t w, const float *xs, float acc) {
+    const uint32_t s0 = w << 12, s1 = w << 4, s2 = w >> 4, s3 = w >> 12;
+    constexpr uint32_t M12 = 0xFu << 12, M16 = 0xFu << 16, E = 0x3F800000u;
+    acc = fmaf(__uint_as_float((s0 & M12) | E), xs[0], acc);
+    acc = fmaf(__uint_as_float((s0 & M16) | E), xs[1], acc);
+    acc = fmaf(__uint_as_float((s1 & M12) | E), xs[2], acc);
+    acc = fmaf(__uint_as_float((s1 & M16) | E), xs[3], acc);
+    acc = fmaf(__uint_as_float((s2 & M12) | E), xs[4], acc);
+    acc = fmaf(__uint_as_float((s2 & M16) | E), xs[5], acc);
+    acc = fmaf(__uint_as_float((s3 & M12) | E), xs[6], acc);
+    acc = fmaf(__uint_as_float((s3 & M16) | E), xs[7], acc);
+    return acc;
+}
+__device__ __forceinline__ float q4_xscale(int n) { return (n & 1) ? 128.0f : 2048.0f; }
+
+}  // namespace qw35

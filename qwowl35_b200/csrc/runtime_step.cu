@@ -186,6 +186,8 @@ void rt_release_kv(Runtime *rt, uint32_t slot, size_t keep) {
 void rt_wait(Runtime *rt) {
     cudaError_t e = cudaStreamSynchronize(rt->stream);
     if (e != cudaSuccess) fail("CUDA decode step failed: %s", cudaGetErrorString(e));
+    if (const unsigned code = device_error_read_and_clear())
+        fail("a device pipeline wait timed out (code %u); results of the last step are invalid", code);
 }
 
 void rt_reset_slot(Runtime *rt, uint32_t slot) {

@@ -150,3 +150,9 @@ def test_argmax_ties_resolve_to_lowest_id():
     if lg2[0, 1234] == lg2[0].max():
         assert tok2.tolist() == [1234, 1234]
     assert lg.shape == (2, rows)
+
+
+def test_no_device_wait_timed_out():
+    from qwowl35_b200 import lib
+    torch.cuda.synchronize()
+    assert lib().qw35_cuda_device_error() == 0

@@ -32,7 +32,8 @@ def test_full_logits_match_oracle(small):
         rt.eval_token(tok, pos, LogitsMode.FULL)
         got = rt.copy_logits()
         ref = orc.step(tok, pos)
-        assert relerr(got, ref) < TOL, pos
+        e = relerr(got, ref)
+        assert e < TOL, (pos, e)
     rt.close()
 
 
