@@ -97,12 +97,7 @@ __device__ __forceinline__ void prep_x(float *xs, float *cst) {
             for (int j = 0; j < 8; ++j) xs[8 * wd + j] *= gf4_xscale(j);
         }
     } else if constexpr (CODEC == QW35_Q8_0_TYPE) {
-        float s = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s += xs[i];
-        cst[0] = kQ8Bias * s;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) xs[i] *= kQ8Scale;
+        cst[0] = 0.0f;
     } else {
         float s = 0.0f, sx = 0.0f;
 #pragma unroll
@@ -131,7 +126,7 @@ __device__ __forceinline__ float chunk_fast(const uint8_t *codes, const uint8_t 
         const uint4 a = *reinterpret_cast<const uint4 *>(codes + c * 32);
         const uint4 b = *reinterpret_cast<const uint4 *>(codes + c * 32 + 16);
         const unsigned short sb = *reinterpret_cast<const unsigned short *>(scales + c * 2);
-        float acc = -cst[0];
+        float acc = 0.0f;
         acc = q8_word_fast(a.x, xs + 0, acc);
         acc = q8_word_fast(a.y, xs + 4, acc);
         acc = q8_word_fast(a.z, xs + 8, acc);

@@ -146,24 +146,24 @@ __device__ __forceinline__ float gf4_word_fast(uint32_t w, const float *xs, floa
 
 __device__ __forceinline__ float gf4_xscale(int j) { return (j & 1) ? 8.0f : 64.0f; }
 
-// Q8_0: byte k of a code word (biased to u = q + 128) is placed in bits 8..15:
-// f = 1 + u * 2^-15, xs = x * 2^15.  Block constant c = (2^15 + 128) * sum(x).
-__device__ __forceinline__ float q8_word_fast(uint32_t wd, const float *xs, float acc) {
+// Q8_0: the 1+u*2^-15 form would put the constant 2^15/|q| times above the
+// code term (~1e-4 relative error), so each byte (biased to u = q + 128) is
+// made exact instead: PRMT into the mantissa of 2^23, one FADD of -(2^23+128)
+// gives q as a float, one FMA.
+__device__ __forceinline__ float q8_word_fast(uint32_t wd, const float *x, float acc) {
     const uint32_t wx = wd ^ 0x80808080u;
-    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x3F800000u, 0x7604u)), xs[0], acc);
-    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x3F800000u, 0x7614u)), xs[1], acc);
-    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x3F800000u, 0x7624u)), xs[2], acc);
-    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x3F800000u, 0x7634u)), xs[3], acc);
+    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u)) - 8388736.0f, x[0], acc);
+    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7541u)) - 8388736.0f, x[1], acc);
+    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7542u)) - 8388736.0f, x[2], acc);
+    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7543u)) - 8388736.0f, x[3], acc);
     return acc;
 }
-constexpr float kQ8Scale = 32768.0f;
-constexpr float kQ8Bias = 32768.0f + 128.0f;
 
-// Q4_K (element-contiguous nibbles): nibble n goes to mantissa bit 12 (n even)
-// or 16 (n odd); xs_n = x_n * (n even ? 2^11 : 2^7).
+// Q4_K (element-contiguous nibbles): nibble n goes to mantissa bit 15 (n even)
+// or 19 (n odd); xs_n = x_n * (n even ? 2^8 : 2^4).
 __device__ __forceinline__ float q4_word_fast(uint32_t w, const float *xs, float acc) {
-    const uint32_t s0 = w << 12, s1 = w << 4, s2 = w >> 4, s3 = w >> 12;
-    constexpr uint32_t M12 = 0xFu << 12, M16 = 0xFu << 16, E = 0x3F800000u;
+    const uint32_t s0 = w << 15, s1 = w << 7, s2 = w >> 1, s3 = w >> 9;
+    constexpr uint32_t M12 = 0xFu << 15, M16 = 0xFu << 19, E = 0x3F800000u;
     acc = fmaf(__uint_as_float((s0 & M12) | E), xs[0], acc);
     acc = fmaf(__uint_as_float((s0 & M16) | E), xs[1], acc);
     acc = fmaf(__uint_as_float((s1 & M12) | E), xs[2], acc);
@@ -174,6 +174,6 @@ __device__ __forceinline__ float q4_word_fast(uint32_t w, const float *xs, float
     acc = fmaf(__uint_as_float((s3 & M16) | E), xs[7], acc);
     return acc;
 }
-__device__ __forceinline__ float q4_xscale(int n) { return (n & 1) ? 128.0f : 2048.0f; }
+__device__ __forceinline__ float q4_xscale(int n) { return (n & 1) ? 16.0f : 256.0f; }
 
 }  // namespace qw35
