@@ -119,6 +119,9 @@ int qw35_cuda_runtime_seq_alloc(void *runtime, uint32_t *seq_id, char *err, uint
 int qw35_cuda_runtime_seq_free(void *runtime, uint32_t seq_id, char *err, uintptr_t err_len);
 int qw35_cuda_runtime_seq_reset(void *runtime, uint32_t seq_id, char *err, uintptr_t err_len);
 uint32_t qw35_cuda_runtime_max_seqs(void *runtime);
+// Copy sequence src (recurrent state and KV chunks) into allocated sequence
+// dst; both then continue from the same prefix.  Waits for the device.
+int qw35_cuda_runtime_seq_fork(void *runtime, uint32_t src, uint32_t dst, char *err, uintptr_t err_len);
 // One decode step for n sequences (token ids and positions are host arrays).
 int qw35_cuda_runtime_eval_batch(void *runtime, uint32_t n, const uint32_t *seq_ids, const uint32_t *tokens,
                                  const uint32_t *pos, int logits_mode, char *err, uintptr_t err_len);

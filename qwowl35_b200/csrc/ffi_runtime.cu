@@ -279,6 +279,14 @@ int qw35_cuda_runtime_seq_reset(void *runtime, uint32_t seq_id, char *err, uintp
     });
 }
 
+int qw35_cuda_runtime_seq_fork(void *runtime, uint32_t src, uint32_t dst, char *err, uintptr_t err_len) {
+    return guarded(runtime, err, err_len, [&](Runtime *rt) {
+        if (src >= rt->max_seqs || !rt->slot_used[src] || dst >= rt->max_seqs || !rt->slot_used[dst])
+            qw35::fail("fork needs two allocated sequences");
+        qw35::rt_fork(rt, src, dst);
+    });
+}
+
 uint32_t qw35_cuda_runtime_max_seqs(void *runtime) {
     Runtime *rt = lookup(runtime);
     return rt ? rt->max_seqs : 0;

@@ -91,10 +91,11 @@ __device__ __forceinline__ void prep_x(float *xs, float *cst) {
                 sx += x * gf4_xscale(j);
             }
             const float x4 = xs[8 * wd + 4];
-            cst[wd] = sx + 4.0f * s + (EXACT ? 0.0f : 0.5f * x4);
-            cst[4 + wd] = 0.5f * x4;
+            // everything carries the -0.25 of the GF4 level spacing (exact)
+            cst[wd] = -0.25f * (sx + 4.0f * s + (EXACT ? 0.0f : 0.5f * x4));
+            cst[4 + wd] = -0.125f * x4;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) xs[8 * wd + j] *= gf4_xscale(j);
+            for (int j = 0; j < 8; ++j) xs[8 * wd + j] *= -0.25f * gf4_xscale(j);
         }
     } else if constexpr (CODEC == QW35_Q8_0_TYPE) {
         cst[0] = 0.0f;
@@ -117,10 +118,10 @@ __device__ __forceinline__ float chunk_fast(const uint8_t *codes, const uint8_t 
                                             const float *cst) {
     if constexpr (CODEC == QW35_GF4_TYPE) {
         const uint4 w = *reinterpret_cast<const uint4 *>(codes + c * 16);
-        float r = gf4_word_fast<EXACT>(w.x, xs + 0, cst[0], cst[4]);
-        r += gf4_word_fast<EXACT>(w.y, xs + 8, cst[1], cst[5]);
-        r += gf4_word_fast<EXACT>(w.z, xs + 16, cst[2], cst[6]);
-        r += gf4_word_fast<EXACT>(w.w, xs + 24, cst[3], cst[7]);
+        float r = gf4_word_fast<EXACT>(w.x, xs + 0, cst[0], cst[4], 0.0f);
+        r = gf4_word_fast<EXACT>(w.y, xs + 8, cst[1], cst[5], r);
+        r = gf4_word_fast<EXACT>(w.z, xs + 16, cst[2], cst[6], r);
+        r = gf4_word_fast<EXACT>(w.w, xs + 24, cst[3], cst[7], r);
         return r;
     } else if constexpr (CODEC == QW35_Q8_0_TYPE) {
         const uint4 a = *reinterpret_cast<const uint4 *>(codes + c * 32);
@@ -170,9 +171,13 @@ __global__ void __launch_bounds__(416, 1) mv_kernel(MvParams p) {
     uint64_t *empty = full + kStages;
     volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStages);
 
-    const int r0 = blockIdx.x * p.rows_per_cta;
-    const int r1 = min(p.rows, r0 + p.rows_per_cta);
-    const int ngroups = r1 > r0 ? (r1 - r0 + G - 1) / G : 0;
+    // contiguous, balanced split of the row groups over the grid
+    const int groups_total = (p.rows + G - 1) / G;
+    const int g0 = (int)(((long long)blockIdx.x * groups_total) / gridDim.x);
+    const int g1 = (int)(((long long)(blockIdx.x + 1) * groups_total) / gridDim.x);
+    const int r0 = g0 * G;
+    const int r1 = min(p.rows, g1 * G);
+    const int ngroups = g1 - g0;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -415,9 +420,8 @@ static MvGeom mv_geometry(int rows, int K, const void *kern) {
     if (occ < 1) occ = 1;
     const int max_ctas = qw35h::sm_count() * occ;
     const int groups = (rows + g.G - 1) / g.G;
-    const int ctas = groups < max_ctas ? groups : max_ctas;
-    g.rows_per_cta = ((groups + ctas - 1) / ctas) * g.G;
-    g.ctas = (rows + g.rows_per_cta - 1) / g.rows_per_cta;
+    g.ctas = groups < max_ctas ? groups : max_ctas;
+    g.rows_per_cta = 0;  // the kernel splits the groups evenly over the grid
     return g;
 }
 

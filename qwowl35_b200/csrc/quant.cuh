@@ -126,7 +126,9 @@ namespace qw35 {
 // by one of four shifts of the word; xs_j = x_j * (j even ? 64 : 8).
 // cw = sum_j xs_j + 4 * sum_j x_j (+ x_4 / 2 in metal mode); xh = x_4 / 2.
 template <bool EXACT>
-__device__ __forceinline__ float gf4_word_fast(uint32_t w, const float *xs, float cw, float xh) {
+// xs, cw and xh arrive pre-multiplied by -0.25 (the level spacing); the
+// word's e5m2 scale is applied with one FMA into the running row sum r.
+__device__ __forceinline__ float gf4_word_fast(uint32_t w, const float *xs, float cw, float xh, float r) {
     const uint32_t s0 = w << 9, s1 = w << 3, s2 = w >> 3, s3 = w >> 9;
     constexpr uint32_t M17 = 7u << 17, M20 = 7u << 20;
     constexpr uint32_t X17 = 0x3F800000u | (4u << 17), X20 = 0x3F800000u | (4u << 20);
@@ -141,7 +143,7 @@ __device__ __forceinline__ float gf4_word_fast(uint32_t w, const float *xs, floa
     acc = fmaf(__uint_as_float((s3 & M20) ^ X20), xs[7], acc);
     // metal element-4 junk: bits 11..19 as 1 + junk*2^-12, times x_4/2
     if (!EXACT) acc = fmaf(__uint_as_float((w & 0x000FF800u) | 0x3F800000u), xh, acc);
-    return acc * (e5m2_to_float(w) * -0.25f);
+    return fmaf(acc, e5m2_to_float(w), r);
 }
 
 __device__ __forceinline__ float gf4_xscale(int j) { return (j & 1) ? 8.0f : 64.0f; }

@@ -166,6 +166,7 @@ void rt_release_kv(Runtime *rt, uint32_t slot, size_t keep);
 void rt_ensure_kv(Runtime *rt, uint32_t slot, uint64_t positions);
 void rt_reset_slot(Runtime *rt, uint32_t slot);
 void rt_set_ctx(Runtime *rt, uint32_t ctx);
+void rt_fork(Runtime *rt, uint32_t src, uint32_t dst);
 uint64_t rt_state_size(const Runtime *rt);
 void rt_state_export(Runtime *rt, uint32_t slot, uint8_t *buf, uint64_t len);
 void rt_state_import(Runtime *rt, uint32_t slot, const uint8_t *buf, uint64_t len);

@@ -202,6 +202,26 @@ void rt_reset_slot(Runtime *rt, uint32_t slot) {
     rt_wait(rt);
 }
 
+// Copy sequence `src` (recurrent state and every KV chunk it holds) into `dst`,
+// so both continue from the same prefix (session fork / shared prompt).
+void rt_fork(Runtime *rt, uint32_t src, uint32_t dst) {
+    if (src == dst) fail("fork source and destination are the same sequence");
+    rt_wait(rt);
+    const size_t nd = (size_t)std::max(rt->model->n_delta, 1);
+    ck(cudaMemcpyAsync(rt->conv_state + dst * nd * rt->conv_per_layer, rt->conv_state + src * nd * rt->conv_per_layer,
+                       nd * rt->conv_per_layer * 4, cudaMemcpyDeviceToDevice, rt->stream), "fork state");
+    ck(cudaMemcpyAsync(rt->ssm_state + dst * nd * rt->ssm_per_layer, rt->ssm_state + src * nd * rt->ssm_per_layer,
+                       nd * rt->ssm_per_layer * 4, cudaMemcpyDeviceToDevice, rt->stream), "fork state");
+    const size_t n = rt->seq_chunks[src].size();
+    rt_release_kv(rt, dst, 0);
+    rt_ensure_kv(rt, dst, (uint64_t)n * QW35_KV_CHUNK);
+    for (size_t c = 0; c < n; ++c)
+        ck(cudaMemcpyAsync(reinterpret_cast<void *>(rt->seq_chunks[dst][c]),
+                           reinterpret_cast<const void *>(rt->seq_chunks[src][c]), rt->chunk_bytes,
+                           cudaMemcpyDeviceToDevice, rt->stream), "fork kv");
+    rt_wait(rt);
+}
+
 void rt_set_ctx(Runtime *rt, uint32_t ctx) {
     if (ctx <= rt->ctx) return;
     if (ctx > kMaxCtx) fail("ctx %u exceeds the maximum %u tokens the KV cache can address", ctx, kMaxCtx);

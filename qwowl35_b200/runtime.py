@@ -121,6 +121,9 @@ class Runtime:
     def seq_free(self, seq: int):
         self._call("qw35_cuda_runtime_seq_free", seq)
 
+    def seq_fork(self, src: int, dst: int):
+        self._call("qw35_cuda_runtime_seq_fork", src, dst)
+
     def seq_reset(self, seq: int):
         self._call("qw35_cuda_runtime_seq_reset", seq)
 

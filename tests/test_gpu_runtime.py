@@ -147,3 +147,17 @@ def test_window_and_sink_match_oracle(small):
         ref = orc.step((pos * 7) % 4096, pos)
     assert relerr(rt.copy_logits(), ref) < TOL
     rt.close()
+
+
+def test_seq_fork_continues_identically(small):
+    rt = Runtime(small, ctx=1024, max_seqs=3)
+    b, c = rt.seq_alloc(), rt.seq_alloc()
+    for pos in range(270):  # crosses a 256-position chunk boundary
+        rt.eval_token((pos * 13) % 4096, pos, LogitsMode.NONE)
+    rt.seq_fork(0, b)
+    rt.seq_fork(0, c)
+    rt.eval_batch([0, b, c], [5, 5, 5], [270, 270, 270], LogitsMode.FULL)
+    out = rt.copy_logits_batch(3)
+    np.testing.assert_array_equal(out[0], out[1])
+    np.testing.assert_array_equal(out[0], out[2])
+    rt.close()
