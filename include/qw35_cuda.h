@@ -107,6 +107,23 @@ int qw35_cuda_gqa_decode(uint32_t n_seq, const float *q, const float *gate, cons
                          uint64_t v_off, int32_t window, int32_t sink, float *out, void *workspace,
                          uint64_t workspace_bytes, void *stream, char *err, uintptr_t err_len);
 
+// Allocation-free twin of qw35_cuda_gqa_decode (no counterpart in the
+// reference).  For callers that cannot allocate device memory where they
+// decode (their GPU memory belongs to another allocator, or a cudaMalloc and
+// its implicit synchronisation is not allowed there): the split partials use
+// a static 16 MiB device array inside the library instead of a caller
+// workspace, so this call allocates nothing.  Arguments and results are those
+// of qw35_cuda_gqa_decode without the workspace.  Fails (0 + message) when
+// qw35_cuda_gqa_workspace_bytes(n_seq, max_len) exceeds
+// qw35_cuda_gqa_noalloc_max_bytes().  The first call on a device looks up the
+// array's device address (make it before any stream capture); all calls share
+// the array, so calls that may run concurrently on the GPU must not overlap.
+uint64_t qw35_cuda_gqa_noalloc_max_bytes(void);
+int qw35_cuda_gqa_decode_noalloc(uint32_t n_seq, const float *q, const float *gate, const int32_t *seq_len,
+                                 uint32_t max_len, const uint64_t *chunk_ptrs, uint32_t max_chunks, uint64_t k_off,
+                                 uint64_t v_off, int32_t window, int32_t sink, float *out, void *stream, char *err,
+                                 uintptr_t err_len);
+
 // Batched runtime (extension of Qw35FFI.h) -----------------------------------
 // Sequences live in slots; slot 0 is the one the qw35_metal_* calls use.
 // Same arguments as qw35_metal_runtime_create plus the number of sequence

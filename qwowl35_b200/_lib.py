@@ -88,6 +88,9 @@ _SIGS = {
     "qw35_cuda_gqa_workspace_bytes": (C.c_uint64, [C.c_uint32, C.c_uint32]),
     "qw35_cuda_gqa_decode": (C.c_int, [C.c_uint32, vp, vp, vp, C.c_uint32, vp, C.c_uint32, C.c_uint64,
                                        C.c_uint64, C.c_int32, C.c_int32, vp, vp, C.c_uint64, vp, cp, up]),
+    "qw35_cuda_gqa_noalloc_max_bytes": (C.c_uint64, []),
+    "qw35_cuda_gqa_decode_noalloc": (C.c_int, [C.c_uint32, vp, vp, vp, C.c_uint32, vp, C.c_uint32, C.c_uint64,
+                                               C.c_uint64, C.c_int32, C.c_int32, vp, vp, cp, up]),
     "qw35_cuda_runtime_create": (vp, [vp, C.c_uint64, C.POINTER(TensorDesc), up, C.POINTER(Hparams), C.c_uint32,
                                       C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, cp, up]),
     "qw35_cuda_runtime_seq_alloc": (C.c_int, [vp, u32p, cp, up]),

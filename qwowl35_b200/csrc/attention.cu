@@ -19,6 +19,8 @@
 // 128-bit loads of K/V rows, fp32 dots for the 4 heads, a 31-shuffle
 // transpose-reduction, online softmax per head.  A second kernel merges the
 // splits and applies the sigmoid output gate.
+#include <mutex>
+
 #include "common.cuh"
 #include "ops.h"
 
@@ -303,6 +305,59 @@ cudaError_t attn_decode_run(const AttnArgs &a, cudaStream_t st) {
     dim3 g2(AH, a.n_seq);
     attn_combine_kernel<<<g2, 256, 0, st>>>(a, ns);
     return cudaGetLastError();
+}
+
+}  // namespace qw35
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the split-K decode.
+//
+// Some callers cannot allocate device memory at the point where they decode:
+// an engine whose GPU memory is owned by another allocator and not reachable
+// across the FFI, a host with a fixed memory budget that reserves everything
+// up front, or a latency-critical loop that must not pay cudaMalloc's implicit
+// device synchronisation.  For them the split partials live in one static
+// device array of kNoAllocScratchBytes, held by every GPU that loads this
+// library until the process exits.  The array's host-side symbol is not a
+// device address, so its device address is looked up once per device with
+// cudaGetSymbolAddress (on the first call for that device, with that device
+// current) and handed to the unchanged kernels.  Every call shares the array:
+// calls that overlap on the GPU (different streams, no ordering) race on it.
+// Nothing in it has to start at zero: the split kernel writes every partial
+// the combine kernel reads, in the same call.
+// ---------------------------------------------------------------------------
+namespace qw35 {
+
+constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB
+static __device__ __align__(256) uint8_t g_attn_scratch[kNoAllocScratchBytes];
+
+static cudaError_t noalloc_scratch(void **ptr) {
+    static std::mutex mu;
+    static void *addr[64] = {nullptr};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(mu);
+    if (addr[dev] == nullptr) {
+        void *p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_attn_scratch);
+        if (e != cudaSuccess) return e;
+        addr[dev] = p;
+    }
+    *ptr = addr[dev];
+    return cudaSuccess;
+}
+
+size_t attn_noalloc_limit() { return kNoAllocScratchBytes; }
+
+cudaError_t attn_decode_noalloc_run(AttnArgs a, cudaStream_t st) {
+    void *scratch = nullptr;
+    cudaError_t e = noalloc_scratch(&scratch);
+    if (e != cudaSuccess) return e;
+    a.ws = scratch;
+    a.ws_bytes = kNoAllocScratchBytes;
+    return attn_decode_run(a, st);
 }
 
 }  // namespace qw35

@@ -218,4 +218,32 @@ int qw35_cuda_gqa_decode(uint32_t n_seq, const float *q, const float *gate, cons
     return cuda_ok(qw35::attn_decode_run(a, (cudaStream_t)stream), "gqa_decode", err, err_len);
 }
 
+uint64_t qw35_cuda_gqa_noalloc_max_bytes(void) { return qw35::attn_noalloc_limit(); }
+
+int qw35_cuda_gqa_decode_noalloc(uint32_t n_seq, const float *q, const float *gate, const int32_t *seq_len,
+                                 uint32_t max_len, const uint64_t *chunk_ptrs, uint32_t max_chunks, uint64_t k_off,
+                                 uint64_t v_off, int32_t window, int32_t sink, float *out, void *stream, char *err,
+                                 uintptr_t err_len) {
+    if (n_seq == 0) return 1;
+    if (!q || !seq_len || !chunk_ptrs || !out || max_len == 0 || max_chunks == 0 ||
+        (uint64_t)max_chunks * QW35_KV_CHUNK < max_len || n_seq > 65535 || (k_off % 16) || (v_off % 16)) {
+        set_err(err, err_len, "invalid attention arguments%s", "");
+        return 0;
+    }
+    const size_t need = qw35::attn_workspace_bytes((int)n_seq, (int)max_len);
+    if (need > qw35::attn_noalloc_limit()) {
+        if (err && err_len)
+            snprintf(err, (size_t)err_len,
+                     "allocation-free attention needs %zu bytes of split partials for n_seq=%u, max_len=%u; "
+                     "the static scratch holds %zu (use qw35_cuda_gqa_decode with a workspace)",
+                     need, n_seq, max_len, qw35::attn_noalloc_limit());
+        return 0;
+    }
+    qw35::AttnArgs a;
+    a.n_seq = (int)n_seq; a.q = q; a.gate = gate; a.seq_len = seq_len; a.chunk_ptrs = chunk_ptrs;
+    a.max_chunks = (int)max_chunks; a.k_off = (long long)k_off; a.v_off = (long long)v_off;
+    a.window = window; a.sink = sink < 0 ? 0 : sink; a.max_len = (int)max_len; a.out = out;
+    return cuda_ok(qw35::attn_decode_noalloc_run(a, (cudaStream_t)stream), "gqa_decode_noalloc", err, err_len);
+}
+
 }  // extern "C"

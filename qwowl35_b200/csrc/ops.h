@@ -103,6 +103,8 @@ struct AttnArgs {
 };
 size_t attn_workspace_bytes(int n_seq, int max_len);
 cudaError_t attn_decode_run(const AttnArgs &a, cudaStream_t st);
+size_t attn_noalloc_limit();
+cudaError_t attn_decode_noalloc_run(AttnArgs a, cudaStream_t st);  // ws taken from a static device array
 
 unsigned int device_error_read_and_clear();
 
