@@ -127,8 +127,17 @@ def gf4_dequant_metal(words: np.ndarray) -> np.ndarray:
     return out.reshape(w.shape[0], -1).astype(np.float32)
 
 
-def gf4_dequant(words: np.ndarray, exact: bool = False) -> np.ndarray:
-    return gf4_dequant_exact(words) if exact else gf4_dequant_metal(words)
+def gf4_dequant_metal_half(words: np.ndarray) -> np.ndarray:
+    """The reference's multi-token (tiled) dequant, qw35_dequantize_gf4
+    (qw35_gf4.metal:42-58): the Metal decode values rounded to half (only
+    element 4 of a word is not already exact in half)."""
+    return gf4_dequant_metal(words).astype(np.float16).astype(np.float32)
+
+
+def gf4_dequant(words: np.ndarray, exact: bool = False, half: bool = False) -> np.ndarray:
+    if exact:
+        return gf4_dequant_exact(words)
+    return gf4_dequant_metal_half(words) if half else gf4_dequant_metal(words)
 
 
 # --------------------------------------------------------------------------
@@ -175,9 +184,10 @@ def q4_k_dequant(raw: np.ndarray, rows: int, k: int) -> np.ndarray:
     return out.reshape(rows, k)
 
 
-def dequant(type_id: int, raw: np.ndarray, rows: int, k: int, gf4_exact: bool = False) -> np.ndarray:
+def dequant(type_id: int, raw: np.ndarray, rows: int, k: int, gf4_exact: bool = False,
+            gf4_half: bool = False) -> np.ndarray:
     if type_id == GF4_TYPE:
-        return gf4_dequant(np.asarray(raw).view(np.uint32).reshape(rows, k // 8), exact=gf4_exact)
+        return gf4_dequant(np.asarray(raw).view(np.uint32).reshape(rows, k // 8), exact=gf4_exact, half=gf4_half)
     if type_id == Q8_0_TYPE:
         return q8_0_dequant(raw, rows, k)
     if type_id == Q4_K_TYPE:

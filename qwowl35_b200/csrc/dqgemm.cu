@@ -1,0 +1,720 @@
+// dqgemm.cu -- batched (B >= 16) fused dequantise-and-multiply on the 5th-gen
+// tensor cores (tcgen05, TMEM accumulators, TMA-fed weight stages).
+//
+// Y[b][r] (+)= sum_k W[r][k] * X[b][k] for a decode batch of B sequences.  At
+// B >= 16 the weight stream is shared by B tokens, so the CUDA-core matvec
+// (matvec.cu) becomes FMA-bound; here each weight is decoded ONCE per launch
+// into an f16 tile and multiplied against all B activation rows by
+// tcgen05.mma.  Reference semantics: the reference engine has no batched
+// decode; its multi-token path (qw35_kernel_mul_mm, qw35_tiled_mm.metal:36-255)
+// dequantises weights to half (qw35_dequantize_gf4, qw35_gf4.metal:42-58) and
+// keeps activations in f32 (:197-200).  This kernel does the same: GF4
+// weights become exactly those halves (element 4 of a word rounded to half in
+// the default Metal-compatible mode), and every f32 activation is split into
+// hi + lo halves so the product keeps ~22 bits of the activation.
+//
+// Q8_0 weights are not exact in f16 once multiplied by their block scale, so
+// the int8 codes (exact) go through the tensor core per 32-column block into a
+// rotating set of TMEM accumulators and the epilogue warps apply the f16 block
+// scale in fp32 (acc += d * block_sum): bit-for-bit the reference's
+// per-block arithmetic up to summation order.
+//
+// CTA = 10 warps: 0 TMA producer, 1 MMA issuer (+ TMEM owner), 2-5 decoders,
+// 6-9 epilogue.  Tiles are 128 weight rows x NP batch columns (B padded to a
+// multiple of 16); K streams in 128-column chunks through S shared-memory
+// stages; work units (matrix, row tile, K split) are spread over a persistent
+// grid.  Every wait is bounded (pipe.cuh).  No cluster multicast is used.
+#include <cuda.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <algorithm>
+#include <map>
+#include <tuple>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "ops.h"
+#include "pipe.cuh"
+#include "tc.cuh"
+
+namespace qw35 {
+
+constexpr int TM = 128;     // weight rows per tile (MMA M)
+constexpr int KC = 128;     // K columns per stage
+constexpr int NKB = KC / 8; // 16 k-blocks of 8 per stage
+constexpr int DQ_THREADS = 320;
+
+enum DqMode { DQ_STORE = 0, DQ_ACCUM = 1, DQ_DUAL = 2 };
+
+struct DqParams {
+    const uint8_t *xprep;   // [K/8][NP/8][8][8] f16 hi, then the same for lo
+    const float *rowscale;  // [NP]
+    const uint8_t *sc[2];   // Q8_0 scales planes [rows][K/32] f16
+    float *y[2];
+    int rows, K, B, ksplit, tiles, units;
+    uint32_t wbytes;        // bytes of one weight stage (TMA box)
+};
+
+struct DqSmem {  // offsets into dynamic shared memory
+    uint32_t w, x, a, bar, tmem, abort_;
+    int S;
+};
+
+template <int CODEC, int NP>
+__host__ __device__ constexpr uint32_t dq_wstage() {
+    return CODEC == QW35_GF4_TYPE ? TM * KC / 2 : TM * KC;
+}
+template <int NP>
+__host__ __device__ constexpr uint32_t dq_xstage() { return 2u * NP * KC * 2; }  // hi + lo
+__host__ __device__ constexpr uint32_t dq_astage() { return TM * KC * 2; }
+
+// TMEM columns for the accumulators.
+template <int CODEC, int NP>
+__host__ __device__ constexpr int dq_regions() { return CODEC == QW35_GF4_TYPE ? 2 : (512 / NP < 8 ? 512 / NP : 8); }
+template <int CODEC, int NP>
+__host__ __device__ constexpr uint32_t dq_tmem_cols() {
+    return dq_regions<CODEC, NP>() * NP <= 32 ? 32u
+           : dq_regions<CODEC, NP>() * NP <= 64 ? 64u
+           : dq_regions<CODEC, NP>() * NP <= 128 ? 128u
+           : dq_regions<CODEC, NP>() * NP <= 256 ? 256u : 512u;
+}
+
+// ---- decode of one 16-byte chunk of a weight row into 8 halves --------------------
+// GF4: one word -> 8 halves in k order [0,4,1,5,2,6,3,7] (the activation prep
+// applies the same permutation inside every 8-column group, so the dot is
+// unchanged).  Values: (q_raw - 4) * (-0.25 * s), exact in f16; in metal mode
+// element 4 is half(float(q4 * 8192 + junk) * s * -0.25 * 2^-13), the
+// reference's tiled-path rounding.
+template <bool EXACT>
+__device__ __forceinline__ uint4 gf4_word_to_halves(uint32_t w) {
+    const uint32_t packed = (w & 0xfff00000u) | ((w >> 4) & 0x0000fff0u);  // codes i | i+4 16 bits apart
+    const __half hs = __ushort_as_half((unsigned short)((w & 0xffu) << 8));
+    const __half2 sc2 = __half2half2(__hmul(hs, __float2half_rn(-0.25f)));
+    const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6404));  // 1028
+    uint32_t h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t v = ((packed >> (4 + 3 * i)) & 0x00070007u) ^ 0x64046404u;  // 1024 + q_raw per half
+        __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&v), off);
+        q = __hmul2(q, sc2);
+        h[i] = *reinterpret_cast<const uint32_t *>(&q);
+    }
+    if (!EXACT) {
+        const int qi = ((int)(((w >> 20) & 7u) ^ 4u) - 4) * 8192 + (int)((w >> 11) & 0x1ffu);
+        const float scale = __half2float(hs) * -0.25f * 0.0001220703125f;
+        const __half e4 = __float2half_rn((float)qi * scale);
+        h[0] = (h[0] & 0x0000ffffu) | ((uint32_t)__half_as_ushort(e4) << 16);
+    }
+    return make_uint4(h[0], h[1], h[2], h[3]);
+}
+
+// Q8_0: 8 int8 codes -> 8 exact halves (1024 + (q + 128) - 1152).
+__device__ __forceinline__ uint4 q8_codes_to_halves(uint32_t a, uint32_t b) {
+    const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6480));  // 1152
+    const uint32_t xa = a ^ 0x80808080u, xb = b ^ 0x80808080u;
+    uint32_t r[4];
+    const uint32_t src[4] = {__byte_perm(xa, 0x64646464u, 0x4140u), __byte_perm(xa, 0x64646464u, 0x4342u),
+                             __byte_perm(xb, 0x64646464u, 0x4140u), __byte_perm(xb, 0x64646464u, 0x4342u)};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&src[i]), off);
+        r[i] = *reinterpret_cast<const uint32_t *>(&q);
+    }
+    return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+// Bounded wait with a CTA-wide abort flag: once any wait timed out, later
+// waits are skipped so every role unwinds quickly.
+__device__ __forceinline__ void dq_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag, unsigned code) {
+    if (*abort_flag) return;
+    if (!mbar_wait(bar, parity, code)) *abort_flag = 1;
+}
+
+template <int CODEC, int NP, int MODE, bool EXACT>
+__global__ void __launch_bounds__(DQ_THREADS, 1)
+dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1, DqParams p, int S) {
+    constexpr int R = dq_regions<CODEC, NP>();
+    constexpr uint32_t TCOLS = dq_tmem_cols<CODEC, NP>();
+    constexpr uint32_t XS = dq_xstage<NP>();
+    constexpr uint32_t AS = dq_astage();
+    constexpr uint32_t IDESC = idesc_f16_f32(TM, NP);
+    constexpr bool BLOCKED = CODEC != QW35_GF4_TYPE;
+    extern __shared__ __align__(1024) uint8_t smem[];
+
+    const uint32_t WS = p.wbytes;
+    uint8_t *wst = smem;                            // [S][WS]
+    uint8_t *xst = wst + (size_t)S * WS;            // [S][XS]
+    uint8_t *ast = xst + (size_t)S * XS;            // [S][AS]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ast + (size_t)S * AS);
+    uint64_t *full = bars;                          // [S] producer tx
+    uint64_t *empty_w = full + S;                   // [S] decoders done with raw weights
+    uint64_t *full_a = empty_w + S;                 // [S] decoded tile ready
+    uint64_t *mma_done = full_a + S;                // [S] MMA done with A and X
+    uint64_t *acc_full = mma_done + S;              // [R]
+    uint64_t *acc_empty = acc_full + R;             // [R]
+    uint64_t *drain = acc_empty + R;                // [1] abort-path drain of in-flight MMAs
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nch = p.K / KC;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty_w[s], 4);
+            mbar_init(&full_a[s], 4);
+            mbar_init(&mma_done[s], 1);
+        }
+        for (int r = 0; r < R; ++r) {
+            mbar_init(&acc_full[r], 1);
+            mbar_init(&acc_empty[r], 4);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) tmem_alloc(tmem_slot, TCOLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    pdl_trigger();
+
+    // unit u -> (matrix, tile, split)
+    auto unit_of = [&](int u, int &m, int &tile, int &c0, int &c1) {
+        const int per_m = p.tiles * p.ksplit;
+        m = u / per_m;
+        const int rem = u - m * per_m;
+        tile = rem / p.ksplit;
+        const int s = rem - tile * p.ksplit;
+        c0 = (s * nch) / p.ksplit;
+        c1 = ((s + 1) * nch) / p.ksplit;
+    };
+
+    if (warp == 0) {
+        // ------------------------------- producer -------------------------------
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            pdl_wait();  // the activation prep of this matvec was written by the previous kernel
+            int c = 0;
+            for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
+                int m, tile, c0, c1;
+                unit_of(u, m, tile, c0, c1);
+                for (int kc = c0; kc < c1; ++kc, ++c) {
+                    const int s = c % S, ph = c / S;
+                    if (c >= S) {
+                        dq_wait(&empty_w[s], (ph - 1) & 1, abort_flag, 8u);
+                        dq_wait(&mma_done[s], (ph - 1) & 1, abort_flag, 8u);
+                    }
+                    if (*abort_flag) break;
+                    mbar_arrive_expect_tx(&full[s], WS + XS);
+                    const int xk = CODEC == QW35_GF4_TYPE ? kc * (KC / 8) : kc * KC;  // element coordinate
+                    tma_load_2d(wst + (size_t)s * WS, m ? &map1 : &map0, xk, tile * TM, &full[s], pol);
+                    const size_t xbytes = (size_t)NP * KC * 2;  // one of hi / lo
+                    const uint8_t *xs = p.xprep + (size_t)kc * xbytes;
+                    bulk_g2s(xst + (size_t)s * XS, xs, (uint32_t)xbytes, &full[s], pol);
+                    bulk_g2s(xst + (size_t)s * XS + xbytes, xs + (size_t)p.K * NP * 2, (uint32_t)xbytes, &full[s],
+                             pol);
+                }
+                if (*abort_flag) break;
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------ MMA issuer -------------------------------
+        if (lane == 0) {
+            int c = 0, blk = 0, ul = 0;
+            const uint32_t a_lbo = (TM / 8) * 128, b_lbo = (NP / 8) * 128;
+            for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x, ++ul) {
+                int m, tile, c0, c1;
+                unit_of(u, m, tile, c0, c1);
+                const int ab = ul & 1;
+                if (!BLOCKED && ul >= 2) {
+                    dq_wait(&acc_empty[ab], ((ul >> 1) - 1) & 1, abort_flag, 16u);
+                    tc_fence_after();
+                }
+                for (int kc = c0; kc < c1; ++kc, ++c) {
+                    const int s = c % S, ph = c / S;
+                    dq_wait(&full_a[s], ph & 1, abort_flag, 16u);
+                    if (*abort_flag) break;
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(ast + (size_t)s * AS);
+                    const uint32_t x0 = smem_u32(xst + (size_t)s * XS);
+#pragma unroll
+                    for (int j = 0; j < KC / 16; ++j) {
+                        const uint64_t ad = smem_desc(a0 + j * 2 * a_lbo, a_lbo, 128);
+                        const uint64_t bh = smem_desc(x0 + j * 2 * b_lbo, b_lbo, 128);
+                        const uint64_t bl = smem_desc(x0 + NP * KC * 2 + j * 2 * b_lbo, b_lbo, 128);
+                        if constexpr (!BLOCKED) {
+                            const uint32_t d = tmem + ab * NP;
+                            tc_mma_f16(d, ad, bh, IDESC, (kc > c0 || j > 0) ? 1u : 0u);
+                            tc_mma_f16(d, ad, bl, IDESC, 1u);
+                        } else {
+                            const int r = blk % R;
+                            if ((j & 1) == 0 && blk >= R) {
+                                dq_wait(&acc_empty[r], ((blk / R) - 1) & 1, abort_flag, 16u);
+                                tc_fence_after();
+                            }
+                            const uint32_t d = tmem + r * NP;
+                            tc_mma_f16(d, ad, bh, IDESC, (j & 1) ? 1u : 0u);
+                            tc_mma_f16(d, ad, bl, IDESC, 1u);
+                            if (j & 1) {
+                                tc_commit(&acc_full[r]);
+                                ++blk;
+                            }
+                        }
+                    }
+                    tc_commit(&mma_done[s]);
+                }
+                if constexpr (!BLOCKED) tc_commit(&acc_full[ab]);
+            }
+        }
+    } else if (warp < 6) {
+        // -------------------------------- decoders --------------------------------
+        const int t = threadIdx.x - 64;  // 0..127: one weight row of the tile each
+        int c = 0;
+        for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
+            int m, tile, c0, c1;
+            unit_of(u, m, tile, c0, c1);
+            for (int kc = c0; kc < c1; ++kc, ++c) {
+                const int s = c % S, ph = c / S;
+                dq_wait(&full[s], ph & 1, abort_flag, 32u);
+                if (c >= S) dq_wait(&mma_done[s], (ph - 1) & 1, abort_flag, 32u);
+                if (*abort_flag) break;
+                uint8_t *a = ast + (size_t)s * AS;
+                const uint8_t *wrow = wst + (size_t)s * WS + (size_t)t * (WS / TM);
+                uint8_t *arow = a + (size_t)(t >> 3) * 128 + (size_t)(t & 7) * 16;
+                if constexpr (CODEC == QW35_GF4_TYPE) {
+#pragma unroll
+                    for (int q = 0; q < NKB / 4; ++q) {
+                        const uint4 w4 = *reinterpret_cast<const uint4 *>(wrow + q * 16);
+                        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                        for (int i = 0; i < 4; ++i)
+                            *reinterpret_cast<uint4 *>(arow + (size_t)(4 * q + i) * (TM / 8) * 128) =
+                                gf4_word_to_halves<EXACT>(ws[i]);
+                    }
+                } else {
+#pragma unroll
+                    for (int q = 0; q < NKB / 2; ++q) {
+                        const uint4 w4 = *reinterpret_cast<const uint4 *>(wrow + q * 16);
+                        *reinterpret_cast<uint4 *>(arow + (size_t)(2 * q) * (TM / 8) * 128) =
+                            q8_codes_to_halves(w4.x, w4.y);
+                        *reinterpret_cast<uint4 *>(arow + (size_t)(2 * q + 1) * (TM / 8) * 128) =
+                            q8_codes_to_halves(w4.z, w4.w);
+                    }
+                }
+                fence_async_smem();  // generic-proxy writes -> visible to the tensor core
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&empty_w[s]);
+                    mbar_arrive(&full_a[s]);
+                }
+            }
+        }
+    } else {
+        // -------------------------------- epilogue --------------------------------
+        pdl_wait();  // rowscale / residual y come from earlier kernels
+        const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+        const int row_in_tile = quarter * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+        int blk = 0, ul = 0;
+        for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x, ++ul) {
+            int m, tile, c0, c1;
+            unit_of(u, m, tile, c0, c1);
+            const int row = tile * TM + row_in_tile;
+            float acc[NP];
+#pragma unroll
+            for (int n = 0; n < NP; ++n) acc[n] = 0.0f;
+            if constexpr (!BLOCKED) {
+                const int ab = ul & 1;
+                dq_wait(&acc_full[ab], (ul >> 1) & 1, abort_flag, 64u);
+                tc_fence_after();
+                tmem_ld_np<NP>(tmem + lane_addr + ab * NP, acc);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[ab]);
+            } else {
+                const uint16_t *scl = reinterpret_cast<const uint16_t *>(p.sc[m]) + (size_t)row * (p.K / 32);
+                for (int kc = c0; kc < c1; ++kc) {
+                    uint2 dpk = make_uint2(0, 0);
+                    if (row < p.rows) dpk = *reinterpret_cast<const uint2 *>(scl + kc * 4);
+                    const uint32_t dw[2] = {dpk.x, dpk.y};
+#pragma unroll
+                    for (int b4 = 0; b4 < 4; ++b4, ++blk) {
+                        const int r = blk % R;
+                        dq_wait(&acc_full[r], (blk / R) & 1, abort_flag, 64u);
+                        tc_fence_after();
+                        float tv[NP];
+                        tmem_ld_np<NP>(tmem + lane_addr + r * NP, tv);
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[r]);
+                        const float d =
+                            __half2float(__ushort_as_half((unsigned short)((dw[b4 >> 1] >> (16 * (b4 & 1))) & 0xffffu)));
+#pragma unroll
+                        for (int n = 0; n < NP; ++n) acc[n] = fmaf(d, tv[n], acc[n]);
+                    }
+                }
+            }
+            if (row < p.rows && !*abort_flag) {
+                float *y = p.y[MODE == DQ_DUAL ? m : 0];
+                const bool atomic = MODE == DQ_ACCUM || p.ksplit > 1;
+                for (int n = 0; n < p.B; ++n) {
+                    const float v = acc[n] * p.rowscale[n];
+                    float *dst = y + (size_t)n * p.rows + row;
+                    if (atomic) atomicAdd(dst, v);
+                    else *dst = v;
+                }
+            }
+        }
+    }
+
+    // ---- teardown: nothing of ours may be in flight when TMEM is released ----
+    if (threadIdx.x == 32 && *abort_flag) {
+        // the MMA issuer drains its own tensor-core work (bounded) before TMEM goes
+        tc_commit(drain);
+        mbar_wait(drain, 0, 128u);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, TCOLS);
+}
+
+// ---------------------------------------------------------------------------
+// activation prep: RMS norm (optional), per-row power-of-two scale, f32 ->
+// hi + lo halves in the MMA's K-major core-matrix layout (one CTA per padded
+// batch row); zeroes the outputs that split-K accumulates into.
+// ---------------------------------------------------------------------------
+template <typename XT>
+__global__ void __launch_bounds__(256) dq_prep_kernel(const XT *x, const float *norm_w, float eps, int K, int B, int NP,
+                                                      int gf4_perm, __half *xh, __half *xl, float *rowscale,
+                                                      float *zero0, float *zero1, int zero_rows) {
+    __shared__ float red[32];
+    const int n = blockIdx.x;
+    const XT *xr = x + (size_t)(n < B ? n : 0) * K;
+    float inv = 1.0f, e2 = 1.0f;
+    if (n < B) {
+        float ss = 0.0f;
+        if (norm_w) {
+            for (int k = threadIdx.x; k < K; k += 256) {
+                const float v = to_f32(xr[k]);
+                ss = fmaf(v, v, ss);
+            }
+            ss = block_sum(ss, red);
+            inv = rsqrtf(ss / (float)K + eps);
+        }
+        float mx = 0.0f;
+        for (int k = threadIdx.x; k < K; k += 256) {
+            const float v = norm_w ? to_f32(xr[k]) * inv * norm_w[k] : to_f32(xr[k]);
+            mx = fmaxf(mx, fabsf(v));
+        }
+        mx = warp_max(mx);
+        __syncthreads();
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+        __syncthreads();
+        mx = 0.0f;
+        for (int i = 0; i < 8; ++i) mx = fmaxf(mx, red[i]);
+        int ex = 0;
+        if (mx > 0.0f && isfinite(mx)) {
+            frexpf(mx, &ex);
+            ex -= 15;  // max |v| * 2^-ex in [2^14, 2^15)
+        }
+        e2 = ldexpf(1.0f, ex);
+        if (threadIdx.x == 0) rowscale[n] = e2;
+        if (zero0)
+            for (int r = threadIdx.x; r < zero_rows; r += 256) zero0[(size_t)n * zero_rows + r] = 0.0f;
+        if (zero1)
+            for (int r = threadIdx.x; r < zero_rows; r += 256) zero1[(size_t)n * zero_rows + r] = 0.0f;
+    } else if (threadIdx.x == 0) {
+        rowscale[n] = 1.0f;
+    }
+    const float rs = 1.0f / e2;  // exact power of two
+    for (int k = threadIdx.x; k < K; k += 256) {
+        float v = 0.0f;
+        if (n < B) v = (norm_w ? to_f32(xr[k]) * inv * norm_w[k] : to_f32(xr[k])) * rs;
+        const __half hi = __float2half_rn(v);
+        const __half lo = __float2half_rn(v - __half2float(hi));
+        const int i = k & 7, kb = k >> 3;
+        const int slot = gf4_perm ? (i < 4 ? 2 * i : 2 * (i - 4) + 1) : i;
+        const size_t off = ((size_t)(kb * (NP / 8) + (n >> 3)) * 8 + (n & 7)) * 8 + slot;
+        xh[off] = hi;
+        xl[off] = lo;
+    }
+}
+
+// h = silu(gate) * up over [B][rows]
+__global__ void dq_swiglu_kernel(const float *g, const float *u, float *h, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        h[i] = silu_f(g[i]) * u[i];
+}
+
+// lowest-id argmax of each logits row (one CTA of 1024 threads per row)
+__global__ void __launch_bounds__(1024) dq_argmax_rows_kernel(const float *logits, int V, uint32_t *tok, float *val) {
+    __shared__ float sv[32];
+    __shared__ uint32_t si[32];
+    const float *l = logits + (size_t)blockIdx.x * V;
+    float bv = -INFINITY;
+    uint32_t bi = 0xffffffffu;
+    for (int i = threadIdx.x; i < V; i += 1024) {
+        const float v = l[i];
+        if (v > bv) { bv = v; bi = (uint32_t)i; }  // ascending i per thread: keeps the lowest id
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        bv = sv[threadIdx.x];
+        bi = si[threadIdx.x];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (threadIdx.x == 0) {
+            tok[blockIdx.x] = bi;
+            if (val) val[blockIdx.x] = bv;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// Tensor map over the codes plane of a device-layout weight (cached: weights are immutable).
+bool weight_map(uint32_t type_id, const void *w, uint32_t rows, uint32_t k, CUtensorMap *out) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void *, uint32_t, uint32_t, uint32_t>, CUtensorMap> cache;
+    std::lock_guard<std::mutex> g(mu);
+    auto key = std::make_tuple(w, type_id, rows, k);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return true;
+    }
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    CUtensorMap m;
+    cuuint64_t dims[2], strides[1];
+    cuuint32_t box[2], estr[2] = {1, 1};
+    CUtensorMapDataType dt;
+    if (type_id == QW35_GF4_TYPE) {
+        dt = CU_TENSOR_MAP_DATA_TYPE_UINT32;
+        dims[0] = k / 8; dims[1] = rows; strides[0] = (cuuint64_t)k / 2;
+        box[0] = KC / 8; box[1] = TM;
+    } else {
+        dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+        dims[0] = k; dims[1] = rows; strides[0] = k;
+        box[0] = KC; box[1] = TM;
+    }
+    if (fn(&m, dt, 2, const_cast<void *>(w), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+        return false;
+    cache[key] = m;
+    *out = m;
+    return true;
+}
+
+// Per-device scratch for the activation prep and the two-pass epilogues.
+// Grows only outside stream capture (the runtime reserves it up front).
+struct Scratch {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+};
+std::mutex g_scratch_mu;
+Scratch g_scratch[64];
+
+cudaError_t scratch_get(size_t bytes, void **out, cudaStream_t st) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(g_scratch_mu);
+    Scratch &s = g_scratch[dev];
+    if (s.bytes < bytes) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        if (st) cudaStreamIsCapturing(st, &cs);
+        if (cs != cudaStreamCaptureStatusNone) return cudaErrorStreamCaptureUnsupported;
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) return e;
+        if (s.ptr) cudaFree(s.ptr);
+        s.ptr = nullptr;
+        s.bytes = 0;
+        e = cudaMalloc(&s.ptr, bytes);
+        if (e != cudaSuccess) return e;
+        s.bytes = bytes;
+    }
+    *out = s.ptr;
+    return cudaSuccess;
+}
+
+int dq_np(int B) { return B <= 16 ? 16 : (B <= 32 ? 32 : 64); }
+
+}  // namespace
+
+bool dq_supported(const MatvecArgs &a) {
+    return a.batch >= 16 && a.batch <= 64 && (a.type_id == QW35_GF4_TYPE || a.type_id == QW35_Q8_0_TYPE) &&
+           a.k % KC == 0 && encode_fn() != nullptr && !getenv("QW35_NO_TCGEN05");
+}
+
+size_t dq_scratch_bytes(int B, uint32_t k, uint32_t rows_out) {
+    const int NP = dq_np(B);
+    return (size_t)2 * NP * k * 2 + 256 + (size_t)2 * B * rows_out * 4 + 256;
+}
+
+cudaError_t dq_reserve(int max_batch, uint32_t max_k, uint32_t max_rows_out) {
+    void *p = nullptr;
+    return scratch_get(dq_scratch_bytes(max_batch, max_k, max_rows_out), &p, nullptr);
+}
+
+template <int CODEC, int NP, int MODE, bool EXACT>
+static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, DqParams p, cudaStream_t st) {
+    auto kern = dq_kernel<CODEC, NP, MODE, EXACT>;
+    constexpr uint32_t stage = dq_wstage<CODEC, NP>() + dq_xstage<NP>() + dq_astage();
+    const int S = (int)std::min<uint32_t>(4u, (200u * 1024u) / stage);
+    const size_t smem = (size_t)S * stage + (4 * S + 2 * dq_regions<CODEC, NP>() + 1) * 8 + 16;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    p.wbytes = dq_wstage<CODEC, NP>();
+    const int grid = std::min(p.units, qw35h::sm_count());
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(DQ_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[1];
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = getenv("QW35_NO_PDL") ? 0 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, m0, m1, p, S);
+}
+
+template <int CODEC, int NP>
+static cudaError_t dq_dispatch_mode(int mode, bool exact, const CUtensorMap &m0, const CUtensorMap &m1,
+                                    const DqParams &p, cudaStream_t st) {
+    if (CODEC == QW35_GF4_TYPE && !exact) {
+        if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, false>(m0, m1, p, st);
+        if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, false>(m0, m1, p, st);
+        return dq_launch<CODEC, NP, DQ_DUAL, false>(m0, m1, p, st);
+    }
+    if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, true>(m0, m1, p, st);
+    if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, true>(m0, m1, p, st);
+    return dq_launch<CODEC, NP, DQ_DUAL, true>(m0, m1, p, st);
+}
+
+// mode: 0 store, 1 accumulate, 2 swiglu pair, 3 logits for the argmax head
+cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cudaStream_t st) {
+    const int B = a.batch, NP = dq_np(B);
+    const int K = (int)a.k, rows = (int)a.rows;
+    const bool dual = mode == 2;
+    CUtensorMap m0, m1;
+    if (!weight_map(a.type_id, a.w0, a.rows, a.k, &m0)) return cudaErrorInvalidValue;
+    if (dual && !weight_map(a.type_id, a.w1, a.rows, a.k, &m1)) return cudaErrorInvalidValue;
+    if (!dual) m1 = m0;
+    // scratch: [xh | xl] halves, rowscale, then (swiglu) gate|up or (head) logits
+    const size_t xbytes = (size_t)NP * K * 2;
+    const size_t extra = (mode == 2) ? (size_t)2 * B * rows * 4 : (mode == 3 && !a.y) ? (size_t)B * rows * 4 : 0;
+    void *scr = nullptr;
+    cudaError_t e = scratch_get(2 * xbytes + 256 + extra + 256, &scr, st);
+    if (e != cudaSuccess) return e;
+    uint8_t *base = static_cast<uint8_t *>(scr);
+    __half *xh = reinterpret_cast<__half *>(base);
+    __half *xl = reinterpret_cast<__half *>(base + xbytes);
+    float *rowscale = reinterpret_cast<float *>(base + 2 * xbytes);
+    float *ext = reinterpret_cast<float *>(base + 2 * xbytes + 256);
+
+    const int tiles = (rows + TM - 1) / TM;
+    const int nch = K / KC;
+    const int sms = qw35h::sm_count();
+    const int per_m_tiles = tiles * (dual ? 2 : 1);
+    int ksplit = (3 * sms + per_m_tiles - 1) / per_m_tiles;
+    ksplit = std::max(1, std::min(ksplit, nch / 4 > 0 ? nch / 4 : 1));
+    if (mode == 3) ksplit = 1;  // logits: plain stores, no atomics
+
+    DqParams p{};
+    p.xprep = base;
+    p.rowscale = rowscale;
+    p.rows = rows;
+    p.K = K;
+    p.B = B;
+    p.ksplit = ksplit;
+    p.tiles = tiles;
+    p.units = tiles * ksplit * (dual ? 2 : 1);
+    float *y0, *y1 = nullptr;
+    int dmode;
+    if (mode == 2) { y0 = ext; y1 = ext + (size_t)B * rows; dmode = DQ_DUAL; }
+    else if (mode == 3) { y0 = a.y ? a.y : ext; dmode = DQ_STORE; }
+    else { y0 = a.y; dmode = mode == 1 ? DQ_ACCUM : DQ_STORE; }
+    p.y[0] = y0;
+    p.y[1] = y1;
+    if (a.type_id == QW35_Q8_0_TYPE) {
+        p.sc[0] = static_cast<const uint8_t *>(a.w0) + (size_t)rows * K;
+        p.sc[1] = dual ? static_cast<const uint8_t *>(a.w1) + (size_t)rows * K : p.sc[0];
+    }
+    // prep (+ zeroing of split-K outputs)
+    const bool zero = dmode != DQ_ACCUM && ksplit > 1;
+    const bool gperm = a.type_id == QW35_GF4_TYPE;
+    if (a.x_dtype == QW35_F16_TYPE)
+        dq_prep_kernel<__half><<<NP, 256, 0, st>>>(static_cast<const __half *>(a.x), a.norm_w, a.eps, K, B, NP, gperm,
+                                                  xh, xl, rowscale, zero ? y0 : nullptr, zero ? y1 : nullptr, rows);
+    else
+        dq_prep_kernel<float><<<NP, 256, 0, st>>>(static_cast<const float *>(a.x), a.norm_w, a.eps, K, B, NP, gperm,
+                                                 xh, xl, rowscale, zero ? y0 : nullptr, zero ? y1 : nullptr, rows);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const bool exact = (a.flags & QW35_MV_GF4_EXACT) != 0;
+    if (a.type_id == QW35_GF4_TYPE) {
+        if (NP == 16) e = dq_dispatch_mode<QW35_GF4_TYPE, 16>(dmode, exact, m0, m1, p, st);
+        else if (NP == 32) e = dq_dispatch_mode<QW35_GF4_TYPE, 32>(dmode, exact, m0, m1, p, st);
+        else e = dq_dispatch_mode<QW35_GF4_TYPE, 64>(dmode, exact, m0, m1, p, st);
+    } else {
+        if (NP == 16) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 16>(dmode, true, m0, m1, p, st);
+        else if (NP == 32) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 32>(dmode, true, m0, m1, p, st);
+        else e = dq_dispatch_mode<QW35_Q8_0_TYPE, 64>(dmode, true, m0, m1, p, st);
+    }
+    if (e != cudaSuccess) return e;
+    if (mode == 2) {
+        const size_t n = (size_t)B * rows;
+        dq_swiglu_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256, 0, st>>>(y0, y1, a.y, n);
+        e = cudaGetLastError();
+    } else if (mode == 3) {
+        dq_argmax_rows_kernel<<<B, 1024, 0, st>>>(y0, rows, tok, val);
+        e = cudaGetLastError();
+    }
+    return e;
+}
+
+}  // namespace qw35

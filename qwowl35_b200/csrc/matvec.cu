@@ -506,6 +506,7 @@ static MvParams base_params(const MatvecArgs &a, int b0) {
 // Batch rows beyond the register-resident tile of two are processed in tiles
 // of two; each tile re-reads the weights (from L2 when they fit).
 cudaError_t matvec_run(const MatvecArgs &a, cudaStream_t st) {
+    if (dq_supported(a)) return dq_run(a, a.mode, nullptr, nullptr, st);  // tensor-core path, B >= 16
     for (int b0 = 0; b0 < a.batch; b0 += 2) {
         const int nb = a.batch - b0 < 2 ? a.batch - b0 : 2;
         MvParams p = base_params(a, b0);
@@ -531,6 +532,7 @@ size_t argmax_workspace_bytes(uint32_t rows, uint32_t batch) {
 cudaError_t argmax_head_run(const MatvecArgs &a, uint32_t *tok, float *val, void *ws, size_t ws_bytes,
                             cudaStream_t st) {
     if (ws_bytes < argmax_workspace_bytes(a.rows, a.batch)) return cudaErrorInvalidValue;
+    if (dq_supported(a)) return dq_run(a, 3, tok, val, st);  // tensor-core path, B >= 16
     const size_t half_ws = ws_bytes / 2;
     for (int b0 = 0; b0 < a.batch; b0 += 2) {
         const int nb = a.batch - b0 < 2 ? a.batch - b0 : 2;

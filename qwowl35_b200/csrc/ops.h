@@ -30,6 +30,12 @@ size_t argmax_workspace_bytes(uint32_t rows, uint32_t batch);
 cudaError_t argmax_head_run(const MatvecArgs &a, uint32_t *tok, float *val, void *ws, size_t ws_bytes,
                             cudaStream_t st);
 
+// tcgen05 batched path (dqgemm.cu): B >= 16, GF4 / Q8_0, k % 128 == 0.
+bool dq_supported(const MatvecArgs &a);
+cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cudaStream_t st);
+size_t dq_scratch_bytes(int B, uint32_t k, uint32_t rows_out);
+cudaError_t dq_reserve(int max_batch, uint32_t max_k, uint32_t max_rows_out);
+
 cudaError_t weight_repack(uint32_t type_id, const void *src, void *dst, uint32_t rows, uint32_t k,
                           cudaStream_t st);
 cudaError_t weight_dequant(uint32_t type_id, const void *w, float *out, uint32_t rows, uint32_t k,

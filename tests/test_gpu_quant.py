@@ -156,3 +156,53 @@ def test_no_device_wait_timed_out():
     from qwowl35_b200 import lib
     torch.cuda.synchronize()
     assert lib().qw35_cuda_device_error() == 0
+
+
+# ---- batched (B >= 16) tensor-core path -----------------------------------------
+@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE])
+@pytest.mark.parametrize("b", [16, 32, 64, 20])
+@pytest.mark.parametrize("shape", [(12288, 4096), (4096, 12288), (333, 1280)])
+def test_batched_matvec_parity(t, b, shape):
+    rows, k = shape
+    raw, w = make(t, rows, k, 20)
+    x = np.random.default_rng(21).standard_normal((b, k)).astype(np.float32)
+    y = ops.matvec(t, w, torch.from_numpy(x).cuda(), rows, k).cpu().numpy()
+    ref = O.matvec(Q.dequant(t, raw, rows, k, gf4_half=True), x)
+    assert relerr(y, ref) < TOL
+    if t == Q.GF4_TYPE:  # exact mode too
+        ye = ops.matvec(t, w, torch.from_numpy(x).cuda(), rows, k, exact=True).cpu().numpy()
+        assert relerr(ye, O.matvec(Q.dequant(t, raw, rows, k, gf4_exact=True), x)) < TOL
+
+
+@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE])
+def test_batched_accumulate_swiglu_and_head(t):
+    rows, k, b = 4096, 4096, 32
+    raw, w = make(t, rows, k, 22)
+    rng = np.random.default_rng(23)
+    x = rng.standard_normal((b, k)).astype(np.float32)
+    base = rng.standard_normal((b, rows)).astype(np.float32)
+    y = torch.from_numpy(base.copy()).cuda()
+    ops.matvec(t, w, torch.from_numpy(x).cuda(), rows, k, y=y, accumulate=True)
+    deq = Q.dequant(t, raw, rows, k, gf4_half=True)
+    assert relerr(y.cpu().numpy(), base + O.matvec(deq, x)) < TOL
+    raw2, w2 = make(t, rows, k, 24)
+    h = ops.gate_up_swiglu(t, w, w2, torch.from_numpy(x).cuda(), rows, k).cpu().numpy()
+    assert relerr(h, O.gate_up_swiglu(deq, Q.dequant(t, raw2, rows, k, gf4_half=True), x)) < TOL
+    tok, val, logits = ops.argmax_head(t, w, torch.from_numpy(x).cuda(), rows, k, want_logits=True)
+    lg = logits.cpu().numpy()
+    assert relerr(lg, O.matvec(deq, x)) < TOL
+    for i in range(b):
+        rid, rv = O.argmax_lowest(lg[i])
+        assert int(tok[i]) == rid and float(val[i]) == rv
+
+
+def test_batched_and_single_paths_agree():
+    rows, k = 4096, 4096
+    raw, w = make(Q.Q8_0_TYPE, rows, k, 25)
+    x = torch.from_numpy(np.random.default_rng(26).standard_normal((32, k)).astype(np.float32)).cuda()
+    yb = ops.matvec(Q.Q8_0_TYPE, w, x, rows, k).cpu().numpy()
+    ys = np.concatenate([ops.matvec(Q.Q8_0_TYPE, w, x[i:i + 1], rows, k).cpu().numpy() for i in range(32)])
+    assert relerr(yb, ys.astype(np.float64)) < 1e-5
+    from qwowl35_b200 import lib
+    torch.cuda.synchronize()
+    assert lib().qw35_cuda_device_error() == 0

@@ -92,3 +92,13 @@ def test_generators_row_bytes(t):
     raw = Q.gen_weight(rng, t, 8, 512)
     assert raw.dtype == np.uint8 and raw.size == 8 * Q.row_bytes(t, 512)
     assert np.isfinite(Q.dequant(t, raw, 8, 512)).all()
+
+
+def test_gf4_metal_half_rounds_only_element4():
+    g = load("gf4.npz")
+    words = g["words"][:48]
+    me = Q.gf4_dequant_metal(words).reshape(48, -1, 8)
+    mh = Q.gf4_dequant_metal_half(words).reshape(48, -1, 8)
+    keep = [0, 1, 2, 3, 5, 6, 7]
+    np.testing.assert_array_equal(me[..., keep], mh[..., keep])
+    assert np.max(np.abs(mh[..., 4] - me[..., 4]) / (np.abs(me[..., 4]) + 1e-30)) <= 2.0 ** -11
