@@ -19,8 +19,8 @@
 // scale in fp32 (acc += d * block_sum): bit-for-bit the reference's
 // per-block arithmetic up to summation order.
 //
-// CTA = 10 warps: 0 TMA producer, 1 MMA issuer (+ TMEM owner), 2-5 decoders,
-// 6-9 epilogue.  Tiles are 128 weight rows x NP batch columns (B padded to a
+// CTA: warp 0 TMA producer, warp 1 MMA issuer (+ TMEM owner), then decode
+// warps, then epilogue warps (counts per codec in DqWarps).  Tiles are 128 weight rows x NP batch columns (B padded to a
 // multiple of 16); K streams in 128-column chunks through S shared-memory
 // stages; work units (matrix, row tile, K split) are spread over a persistent
 // grid.  Every wait is bounded (pipe.cuh).  No cluster multicast is used.
@@ -44,18 +44,30 @@ namespace qw35 {
 constexpr int TM = 128;     // weight rows per tile (MMA M)
 constexpr int KC = 128;     // K columns per stage
 constexpr int NKB = KC / 8; // 16 k-blocks of 8 per stage
-constexpr int DQ_THREADS = 320;
+// warp roles per codec: GF4 decode is the bottleneck (16 decode warps, the
+// once-per-unit epilogue needs 4); Q8_0 decodes cheaply but scales every
+// 32-column block in the epilogue (8 + 8).
+template <int CODEC> struct DqWarps {
+    static constexpr int DEC = CODEC == QW35_GF4_TYPE ? 16 : 8;
+    static constexpr int EPI = CODEC == QW35_GF4_TYPE ? 4 : 8;
+    static constexpr int THREADS = (2 + DEC + EPI) * 32;
+};
 
 enum DqMode { DQ_STORE = 0, DQ_ACCUM = 1, DQ_DUAL = 2 };
 
 struct DqParams {
-    const uint8_t *xprep;   // [K/8][NP/8][8][8] f16 hi, then the same for lo
+    const uint8_t *xprep;   // per 128-column chunk [2 k-atoms][2*NP rows (hi | lo)][128 B swizzled] f16
     const float *rowscale;  // [NP]
     const uint8_t *sc[2];   // Q8_0 scales planes [rows][K/32] f16
     float *y[2];
     int rows, K, B, ksplit, tiles, units;
     uint32_t wbytes;        // bytes of one weight stage (TMA box)
+    unsigned long long *trace;  // debug: per-chunk event stamps of CTA 0 (QW35_DQ_TRACE), or null
 };
+// trace layout: [chunk][6] = producer issue, decoder sees full, decoder done,
+// mma sees full_a, mma committed, (unused)
+#define DQ_TRACE(c, slot) \
+    do { if (p.trace && blockIdx.x == 0 && (c) < 256) p.trace[(c) * 6 + (slot)] = globaltimer(); } while (0)
 
 struct DqSmem {  // offsets into dynamic shared memory
     uint32_t w, x, a, bar, tmem, abort_;
@@ -71,14 +83,21 @@ __host__ __device__ constexpr uint32_t dq_xstage() { return 2u * NP * KC * 2; } 
 __host__ __device__ constexpr uint32_t dq_astage() { return TM * KC * 2; }
 
 // TMEM columns for the accumulators.
+// GF4: 2 unit buffers x 4 independent accumulators (hi/lo x even/odd k-step),
+// so consecutive MMAs never wait on each other's accumulator.  Q8_0: rotating
+// per-block regions (consecutive blocks already use different regions).
+constexpr int GF4_NACC = 1;
 template <int CODEC, int NP>
-__host__ __device__ constexpr int dq_regions() { return CODEC == QW35_GF4_TYPE ? 2 : (512 / NP < 8 ? 512 / NP : 8); }
+__host__ __device__ constexpr int dq_regions() {
+    return CODEC == QW35_GF4_TYPE ? 2 : (512 / (2 * NP) < 8 ? 512 / (2 * NP) : 8);
+}
+// one accumulator = 2*NP columns: [hi-activation products | lo-activation products]
+template <int CODEC, int NP>
+__host__ __device__ constexpr int dq_region_cols() { return CODEC == QW35_GF4_TYPE ? GF4_NACC * 2 * NP : 2 * NP; }
 template <int CODEC, int NP>
 __host__ __device__ constexpr uint32_t dq_tmem_cols() {
-    return dq_regions<CODEC, NP>() * NP <= 32 ? 32u
-           : dq_regions<CODEC, NP>() * NP <= 64 ? 64u
-           : dq_regions<CODEC, NP>() * NP <= 128 ? 128u
-           : dq_regions<CODEC, NP>() * NP <= 256 ? 256u : 512u;
+    constexpr int cols = dq_regions<CODEC, NP>() * dq_region_cols<CODEC, NP>();
+    return cols <= 32 ? 32u : cols <= 64 ? 64u : cols <= 128 ? 128u : cols <= 256 ? 256u : 512u;
 }
 
 // ---- decode of one 16-byte chunk of a weight row into 8 halves --------------------
@@ -91,20 +110,34 @@ template <bool EXACT>
 __device__ __forceinline__ uint4 gf4_word_to_halves(uint32_t w) {
     const uint32_t packed = (w & 0xfff00000u) | ((w >> 4) & 0x0000fff0u);  // codes i | i+4 16 bits apart
     const __half hs = __ushort_as_half((unsigned short)((w & 0xffu) << 8));
-    const __half2 sc2 = __half2half2(__hmul(hs, __float2half_rn(-0.25f)));
-    const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6404));  // 1028
+    const __half sc = __hmul(hs, __ushort_as_half((unsigned short)0xB400));  // s * -0.25 (exact)
+    const __half2 sc2 = __half2half2(sc);
     uint32_t h[4];
+    if (fabsf(__half2float(sc)) <= 63.0f) {
+        // (1024 + q) * sc - 1028 * sc in one FMA: the exact result (q - 4) * sc
+        // and 1028 * sc (<= 11 significant bits) are both representable, so the
+        // single rounding is exact.
+        const __half2 c2 = __hmul2(sc2, __half2half2(__ushort_as_half((unsigned short)0xE404)));  // -1028 * sc
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const uint32_t v = ((packed >> (4 + 3 * i)) & 0x00070007u) ^ 0x64046404u;  // 1024 + q_raw per half
-        __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&v), off);
-        q = __hmul2(q, sc2);
-        h[i] = *reinterpret_cast<const uint32_t *>(&q);
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t v = ((packed >> (4 + 3 * i)) & 0x00070007u) ^ 0x64046404u;  // 1024 + q_raw per half
+            const __half2 q = __hfma2(*reinterpret_cast<const __half2 *>(&v), sc2, c2);
+            h[i] = *reinterpret_cast<const uint32_t *>(&q);
+        }
+    } else {  // very large scales: subtract first (1028 * sc would overflow half)
+        const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6404));  // 1028
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t v = ((packed >> (4 + 3 * i)) & 0x00070007u) ^ 0x64046404u;
+            const __half2 q = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&v), off), sc2);
+            h[i] = *reinterpret_cast<const uint32_t *>(&q);
+        }
     }
     if (!EXACT) {
-        const int qi = ((int)(((w >> 20) & 7u) ^ 4u) - 4) * 8192 + (int)((w >> 11) & 0x1ffu);
-        const float scale = __half2float(hs) * -0.25f * 0.0001220703125f;
-        const __half e4 = __float2half_rn((float)qi * scale);
+        // element 4 = half((q4 - 4) * sc + junk * sc * 2^-13): the exact f32 value rounded once
+        const float junk = __uint_as_float(((w >> 11) & 0x1ffu) | 0x4B000000u) - 8388608.0f;
+        const float h4 = __half2float(__ushort_as_half((unsigned short)(h[0] >> 16)));
+        const __half e4 = __float2half_rn(fmaf(junk, __half2float(sc) * 0.0001220703125f, h4));
         h[0] = (h[0] & 0x0000ffffu) | ((uint32_t)__half_as_ushort(e4) << 16);
     }
     return make_uint4(h[0], h[1], h[2], h[3]);
@@ -133,18 +166,22 @@ __device__ __forceinline__ void dq_wait(uint64_t *bar, uint32_t parity, volatile
 }
 
 template <int CODEC, int NP, int MODE, bool EXACT>
-__global__ void __launch_bounds__(DQ_THREADS, 1)
+__global__ void __launch_bounds__(DqWarps<CODEC>::THREADS, 1)
 dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1, DqParams p, int S) {
     constexpr int R = dq_regions<CODEC, NP>();
     constexpr uint32_t TCOLS = dq_tmem_cols<CODEC, NP>();
     constexpr uint32_t XS = dq_xstage<NP>();
     constexpr uint32_t AS = dq_astage();
-    constexpr uint32_t IDESC = idesc_f16_f32(TM, NP);
+    constexpr uint32_t IDESC = idesc_f16_f32(TM, 2 * NP);  // B = [x_hi rows ; x_lo rows]
+    constexpr int RC = dq_region_cols<CODEC, NP>();
     constexpr bool BLOCKED = CODEC != QW35_GF4_TYPE;
+    constexpr int DQ_DEC_WARPS = DqWarps<CODEC>::DEC;
+    constexpr int DQ_EPI_WARPS = DqWarps<CODEC>::EPI;
     extern __shared__ __align__(1024) uint8_t smem[];
 
     const uint32_t WS = p.wbytes;
-    uint8_t *wst = smem;                            // [S][WS]
+    // 1024-byte aligned base (128B-swizzle atoms need it)
+    uint8_t *wst = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);  // [S][WS]
     uint8_t *xst = wst + (size_t)S * WS;            // [S][XS]
     uint8_t *ast = xst + (size_t)S * XS;            // [S][AS]
     uint64_t *bars = reinterpret_cast<uint64_t *>(ast + (size_t)S * AS);
@@ -164,13 +201,13 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty_w[s], 4);
-            mbar_init(&full_a[s], 4);
+            mbar_init(&empty_w[s], DQ_DEC_WARPS);
+            mbar_init(&full_a[s], DQ_DEC_WARPS);
             mbar_init(&mma_done[s], 1);
         }
         for (int r = 0; r < R; ++r) {
             mbar_init(&acc_full[r], 1);
-            mbar_init(&acc_empty[r], 4);
+            mbar_init(&acc_empty[r], DQ_EPI_WARPS);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -210,14 +247,11 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                         dq_wait(&mma_done[s], (ph - 1) & 1, abort_flag, 8u);
                     }
                     if (*abort_flag) break;
+                    DQ_TRACE(c, 0);
                     mbar_arrive_expect_tx(&full[s], WS + XS);
                     const int xk = CODEC == QW35_GF4_TYPE ? kc * (KC / 8) : kc * KC;  // element coordinate
                     tma_load_2d(wst + (size_t)s * WS, m ? &map1 : &map0, xk, tile * TM, &full[s], pol);
-                    const size_t xbytes = (size_t)NP * KC * 2;  // one of hi / lo
-                    const uint8_t *xs = p.xprep + (size_t)kc * xbytes;
-                    bulk_g2s(xst + (size_t)s * XS, xs, (uint32_t)xbytes, &full[s], pol);
-                    bulk_g2s(xst + (size_t)s * XS + xbytes, xs + (size_t)p.K * NP * 2, (uint32_t)xbytes, &full[s],
-                             pol);
+                    bulk_g2s(xst + (size_t)s * XS, p.xprep + (size_t)kc * XS, XS, &full[s], pol);
                 }
                 if (*abort_flag) break;
             }
@@ -226,7 +260,6 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
         // ------------------------------ MMA issuer -------------------------------
         if (lane == 0) {
             int c = 0, blk = 0, ul = 0;
-            const uint32_t a_lbo = (TM / 8) * 128, b_lbo = (NP / 8) * 128;
             for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x, ++ul) {
                 int m, tile, c0, c1;
                 unit_of(u, m, tile, c0, c1);
@@ -239,27 +272,27 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                     const int s = c % S, ph = c / S;
                     dq_wait(&full_a[s], ph & 1, abort_flag, 16u);
                     if (*abort_flag) break;
+                    DQ_TRACE(c, 3);
                     tc_fence_after();
                     const uint32_t a0 = smem_u32(ast + (size_t)s * AS);
                     const uint32_t x0 = smem_u32(xst + (size_t)s * XS);
 #pragma unroll
                     for (int j = 0; j < KC / 16; ++j) {
-                        const uint64_t ad = smem_desc(a0 + j * 2 * a_lbo, a_lbo, 128);
-                        const uint64_t bh = smem_desc(x0 + j * 2 * b_lbo, b_lbo, 128);
-                        const uint64_t bl = smem_desc(x0 + NP * KC * 2 + j * 2 * b_lbo, b_lbo, 128);
+                        // operands: [k-atom of 64][rows][128 B swizzled]; k-step j = 16 columns
+                        const uint32_t ka = j >> 2, kofs = (j & 3) * 32;
+                        const uint64_t ad = smem_desc_sw128(a0 + ka * (TM * 128) + kofs);
+                        const uint64_t bd = smem_desc_sw128(x0 + ka * (2 * NP * 128) + kofs);
                         if constexpr (!BLOCKED) {
-                            const uint32_t d = tmem + ab * NP;
-                            tc_mma_f16(d, ad, bh, IDESC, (kc > c0 || j > 0) ? 1u : 0u);
-                            tc_mma_f16(d, ad, bl, IDESC, 1u);
+                            const uint32_t d = tmem + ab * RC;
+                            tc_mma_f16(d, ad, bd, IDESC, (kc > c0 || j > 0) ? 1u : 0u);
                         } else {
                             const int r = blk % R;
                             if ((j & 1) == 0 && blk >= R) {
                                 dq_wait(&acc_empty[r], ((blk / R) - 1) & 1, abort_flag, 16u);
                                 tc_fence_after();
                             }
-                            const uint32_t d = tmem + r * NP;
-                            tc_mma_f16(d, ad, bh, IDESC, (j & 1) ? 1u : 0u);
-                            tc_mma_f16(d, ad, bl, IDESC, 1u);
+                            const uint32_t d = tmem + r * RC;
+                            tc_mma_f16(d, ad, bd, IDESC, (j & 1) ? 1u : 0u);
                             if (j & 1) {
                                 tc_commit(&acc_full[r]);
                                 ++blk;
@@ -267,13 +300,18 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                         }
                     }
                     tc_commit(&mma_done[s]);
+                    DQ_TRACE(c, 4);
                 }
                 if constexpr (!BLOCKED) tc_commit(&acc_full[ab]);
             }
         }
-    } else if (warp < 6) {
+    } else if (warp < 2 + DQ_DEC_WARPS) {
         // -------------------------------- decoders --------------------------------
-        const int t = threadIdx.x - 64;  // 0..127: one weight row of the tile each
+        // items (row, 16-byte piece of the row): consecutive threads take
+        // consecutive pieces, so every quarter-warp reads 128 contiguous bytes
+        constexpr int QPR = CODEC == QW35_GF4_TYPE ? 4 : 8;   // 16-byte pieces per row
+        constexpr int NT = DQ_DEC_WARPS * 32;
+        const int t = threadIdx.x - 64;
         int c = 0;
         for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
             int m, tile, c0, c1;
@@ -281,33 +319,31 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
             for (int kc = c0; kc < c1; ++kc, ++c) {
                 const int s = c % S, ph = c / S;
                 dq_wait(&full[s], ph & 1, abort_flag, 32u);
+                if (t == 0) DQ_TRACE(c, 1);
                 if (c >= S) dq_wait(&mma_done[s], (ph - 1) & 1, abort_flag, 32u);
                 if (*abort_flag) break;
                 uint8_t *a = ast + (size_t)s * AS;
-                const uint8_t *wrow = wst + (size_t)s * WS + (size_t)t * (WS / TM);
-                uint8_t *arow = a + (size_t)(t >> 3) * 128 + (size_t)(t & 7) * 16;
-                if constexpr (CODEC == QW35_GF4_TYPE) {
+                const uint8_t *wst_s = wst + (size_t)s * WS;
 #pragma unroll
-                    for (int q = 0; q < NKB / 4; ++q) {
-                        const uint4 w4 = *reinterpret_cast<const uint4 *>(wrow + q * 16);
+                for (int it = t; it < TM * QPR; it += NT) {
+                    const int r = it / QPR, q = it % QPR;
+                    const uint4 w4 = *reinterpret_cast<const uint4 *>(wst_s + (size_t)r * (WS / TM) + q * 16);
+                    // k-block kb (8 columns) -> atom kb / 8, chunk kb % 8 of row r
+                    auto aslot = [&](int kb) -> uint4 * {
+                        return reinterpret_cast<uint4 *>(a + (size_t)(kb >> 3) * (TM * 128) + sw128_off(r, kb & 7));
+                    };
+                    if constexpr (CODEC == QW35_GF4_TYPE) {
                         const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            *reinterpret_cast<uint4 *>(arow + (size_t)(4 * q + i) * (TM / 8) * 128) =
-                                gf4_word_to_halves<EXACT>(ws[i]);
-                    }
-                } else {
-#pragma unroll
-                    for (int q = 0; q < NKB / 2; ++q) {
-                        const uint4 w4 = *reinterpret_cast<const uint4 *>(wrow + q * 16);
-                        *reinterpret_cast<uint4 *>(arow + (size_t)(2 * q) * (TM / 8) * 128) =
-                            q8_codes_to_halves(w4.x, w4.y);
-                        *reinterpret_cast<uint4 *>(arow + (size_t)(2 * q + 1) * (TM / 8) * 128) =
-                            q8_codes_to_halves(w4.z, w4.w);
+                        for (int i = 0; i < 4; ++i) *aslot(4 * q + i) = gf4_word_to_halves<EXACT>(ws[i]);
+                    } else {
+                        *aslot(2 * q) = q8_codes_to_halves(w4.x, w4.y);
+                        *aslot(2 * q + 1) = q8_codes_to_halves(w4.z, w4.w);
                     }
                 }
                 fence_async_smem();  // generic-proxy writes -> visible to the tensor core
                 __syncwarp();
+                if (t == 0) DQ_TRACE(c, 2);
                 if (lane == 0) {
                     mbar_arrive(&empty_w[s]);
                     mbar_arrive(&full_a[s]);
@@ -316,8 +352,12 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
         }
     } else {
         // -------------------------------- epilogue --------------------------------
+        // EPI/4 warps per TMEM lane quarter, each owning NP/(EPI/4) columns
         pdl_wait();  // rowscale / residual y come from earlier kernels
-        const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+        constexpr int NH = NP / (DQ_EPI_WARPS / 4);
+        const int ew = warp - 2 - DQ_DEC_WARPS;
+        const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+        const int n0 = (ew >> 2) * NH;
         const int row_in_tile = quarter * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
         int blk = 0, ul = 0;
@@ -325,14 +365,20 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
             int m, tile, c0, c1;
             unit_of(u, m, tile, c0, c1);
             const int row = tile * TM + row_in_tile;
-            float acc[NP];
+            float acc[NH];
 #pragma unroll
-            for (int n = 0; n < NP; ++n) acc[n] = 0.0f;
+            for (int n = 0; n < NH; ++n) acc[n] = 0.0f;
             if constexpr (!BLOCKED) {
                 const int ab = ul & 1;
                 dq_wait(&acc_full[ab], (ul >> 1) & 1, abort_flag, 64u);
                 tc_fence_after();
-                tmem_ld_np<NP>(tmem + lane_addr + ab * NP, acc);
+#pragma unroll
+                for (int part = 0; part < 2; ++part) {  // hi and lo activation products
+                    float tv[NH];
+                    tmem_ld_cols<NH>(tmem + lane_addr + ab * RC + part * NP + n0, tv);
+#pragma unroll
+                    for (int n = 0; n < NH; ++n) acc[n] += tv[n];
+                }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[ab]);
@@ -344,29 +390,35 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                     const uint32_t dw[2] = {dpk.x, dpk.y};
 #pragma unroll
                     for (int b4 = 0; b4 < 4; ++b4, ++blk) {
-                        const int r = blk % R;
-                        dq_wait(&acc_full[r], (blk / R) & 1, abort_flag, 64u);
+                        const int rg = blk % R;
+                        dq_wait(&acc_full[rg], (blk / R) & 1, abort_flag, 64u);
                         tc_fence_after();
-                        float tv[NP];
-                        tmem_ld_np<NP>(tmem + lane_addr + r * NP, tv);
+                        float tv[NH], tl[NH];
+                        tmem_ld_cols<NH>(tmem + lane_addr + rg * RC + n0, tv);
+                        tmem_ld_cols<NH>(tmem + lane_addr + rg * RC + NP + n0, tl);
+#pragma unroll
+                        for (int n = 0; n < NH; ++n) tv[n] += tl[n];
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&acc_empty[r]);
+                        if (lane == 0) mbar_arrive(&acc_empty[rg]);
                         const float d =
                             __half2float(__ushort_as_half((unsigned short)((dw[b4 >> 1] >> (16 * (b4 & 1))) & 0xffffu)));
 #pragma unroll
-                        for (int n = 0; n < NP; ++n) acc[n] = fmaf(d, tv[n], acc[n]);
+                        for (int n = 0; n < NH; ++n) acc[n] = fmaf(d, tv[n], acc[n]);
                     }
                 }
             }
             if (row < p.rows && !*abort_flag) {
                 float *y = p.y[MODE == DQ_DUAL ? m : 0];
                 const bool atomic = MODE == DQ_ACCUM || p.ksplit > 1;
-                for (int n = 0; n < p.B; ++n) {
-                    const float v = acc[n] * p.rowscale[n];
-                    float *dst = y + (size_t)n * p.rows + row;
-                    if (atomic) atomicAdd(dst, v);
-                    else *dst = v;
+#pragma unroll
+                for (int n = 0; n < NH; ++n) {
+                    if (n0 + n < p.B) {
+                        const float v = acc[n] * p.rowscale[n0 + n];
+                        float *dst = y + (size_t)(n0 + n) * p.rows + row;
+                        if (atomic) atomicAdd(dst, v);
+                        else *dst = v;
+                    }
                 }
             }
         }
@@ -438,11 +490,13 @@ __global__ void __launch_bounds__(256) dq_prep_kernel(const XT *x, const float *
         if (n < B) v = (norm_w ? to_f32(xr[k]) * inv * norm_w[k] : to_f32(xr[k])) * rs;
         const __half hi = __float2half_rn(v);
         const __half lo = __float2half_rn(v - __half2float(hi));
-        const int i = k & 7, kb = k >> 3;
+        // per 128-column chunk: [k-atom of 64][2*NP rows: hi rows, then lo rows][128 B swizzled]
+        const int i = k & 7, kl = k & 127;
         const int slot = gf4_perm ? (i < 4 ? 2 * i : 2 * (i - 4) + 1) : i;
-        const size_t off = ((size_t)(kb * (NP / 8) + (n >> 3)) * 8 + (n & 7)) * 8 + slot;
-        xh[off] = hi;
-        xl[off] = lo;
+        const size_t base = (size_t)(k >> 7) * (2 * NP) * 128 + (size_t)(kl >> 6) * (2 * NP) * 64 + slot;
+        const uint32_t c = (uint32_t)((kl & 63) >> 3);
+        xh[base + sw128_off((uint32_t)n, c) / 2] = hi;
+        xh[base + sw128_off((uint32_t)(NP + n), c) / 2] = lo;
     }
 }
 
@@ -599,8 +653,8 @@ template <int CODEC, int NP, int MODE, bool EXACT>
 static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, DqParams p, cudaStream_t st) {
     auto kern = dq_kernel<CODEC, NP, MODE, EXACT>;
     constexpr uint32_t stage = dq_wstage<CODEC, NP>() + dq_xstage<NP>() + dq_astage();
-    const int S = (int)std::min<uint32_t>(4u, (200u * 1024u) / stage);
-    const size_t smem = (size_t)S * stage + (4 * S + 2 * dq_regions<CODEC, NP>() + 1) * 8 + 16;
+    const int S = (int)std::min<uint32_t>(4u, (198u * 1024u) / stage);
+    const size_t smem = 1024 + (size_t)S * stage + (4 * S + 2 * dq_regions<CODEC, NP>() + 1) * 8 + 16;
     static bool attr = false;
     if (!attr) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024);
@@ -608,10 +662,16 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, DqPar
         attr = true;
     }
     p.wbytes = dq_wstage<CODEC, NP>();
+    static unsigned long long *trace = nullptr;
+    if (getenv("QW35_DQ_TRACE")) {
+        if (!trace) cudaMalloc(&trace, 256 * 6 * 8);
+        cudaMemsetAsync(trace, 0, 256 * 6 * 8, st);
+        p.trace = trace;
+    }
     const int grid = std::min(p.units, qw35h::sm_count());
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(DQ_THREADS);
+    cfg.blockDim = dim3(DqWarps<CODEC>::THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attrs[1];
@@ -619,7 +679,18 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, DqPar
     attrs[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = getenv("QW35_NO_PDL") ? 0 : 1;
-    return cudaLaunchKernelEx(&cfg, kern, m0, m1, p, S);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m0, m1, p, S);
+    if (p.trace) {
+        unsigned long long h[256 * 6];
+        cudaMemcpy(h, trace, sizeof(h), cudaMemcpyDeviceToHost);
+        const unsigned long long t0 = h[0];
+        fprintf(stderr, "dq trace units=%d grid=%d S=%d ksplit=%d (ns from first issue)\n", p.units, grid, S, p.ksplit);
+        for (int c = 0; c < 256 && h[c * 6]; ++c)
+            fprintf(stderr, "c%3d issue %7lld full %7lld dec %7lld mma %7lld done %7lld\n", c, (long long)(h[c * 6] - t0),
+                    (long long)(h[c * 6 + 1] - t0), (long long)(h[c * 6 + 2] - t0), (long long)(h[c * 6 + 3] - t0),
+                    (long long)(h[c * 6 + 4] - t0));
+    }
+    return e;
 }
 
 template <int CODEC, int NP>

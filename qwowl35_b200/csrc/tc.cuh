@@ -26,6 +26,25 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
     return d;
 }
 
+// K-major operand in the 128-byte swizzled canonical layout: rows of 128 bytes
+// (64 f16 of K), 16-byte chunk c of row r stored at chunk c ^ (r % 8); 8-row
+// groups 1024 bytes apart (SBO); LBO unused (1).  The 1024-byte atom must be
+// 1024-aligned; a k-step inside the atom advances the start address by 32 B.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;             // LBO (ignored for swizzled K-major)
+    d |= (uint64_t)(1024u >> 4) << 32;   // SBO
+    d |= (uint64_t)1u << 46;             // version
+    d |= (uint64_t)2u << 61;             // SWIZZLE_128B
+    return d;
+}
+
+// byte offset of (row r, 16-byte chunk c in [0,8)) inside a 128B-swizzled K-major atom column
+__host__ __device__ __forceinline__ uint32_t sw128_off(uint32_t r, uint32_t c) {
+    return (r >> 3) * 1024u + (r & 7u) * 128u + ((c ^ (r & 7u)) << 4);
+}
+
 // Instruction descriptor for kind::f16: D f32, A/B f16, both K-major.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
@@ -92,6 +111,27 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float *v) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// NC (8, 16 or a multiple of 32) consecutive columns of this warp's 32 lanes.
+template <int NC>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float *v) {
+    if constexpr (NC == 8) tmem_ld8(taddr, v);
+    else if constexpr (NC == 16) tmem_ld16(taddr, v);
+    else {
+#pragma unroll
+        for (int c = 0; c < NC; c += 32) tmem_ld32(taddr + c, v + c);
+    }
 }
 
 // NP (16, 32 or 64) consecutive columns of this warp's 32 lanes.
