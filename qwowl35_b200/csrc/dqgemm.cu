@@ -106,14 +106,17 @@ __host__ __device__ constexpr uint32_t dq_tmem_cols() {
 // unchanged).  Values: (q_raw - 4) * (-0.25 * s), exact in f16; in metal mode
 // element 4 is half(float(q4 * 8192 + junk) * s * -0.25 * 2^-13), the
 // reference's tiled-path rounding.
-template <bool EXACT>
-__device__ __forceinline__ uint4 gf4_word_to_halves(uint32_t w) {
+// Halves of one word, without the Metal element-4 junk (that is added by
+// gf4_pair_to_halves below, two words at a time).  No conversion-unit (XU)
+// instructions: the range check is an integer compare on the half bits.
+__device__ __forceinline__ uint4 gf4_word_levels(uint32_t w, uint32_t &scbits) {
     const uint32_t packed = (w & 0xfff00000u) | ((w >> 4) & 0x0000fff0u);  // codes i | i+4 16 bits apart
     const __half hs = __ushort_as_half((unsigned short)((w & 0xffu) << 8));
     const __half sc = __hmul(hs, __ushort_as_half((unsigned short)0xB400));  // s * -0.25 (exact)
+    scbits = __half_as_ushort(sc);
     const __half2 sc2 = __half2half2(sc);
     uint32_t h[4];
-    if (fabsf(__half2float(sc)) <= 63.0f) {
+    if ((scbits & 0x7fffu) <= 0x53E0u) {  // |sc| <= 63
         // (1024 + q) * sc - 1028 * sc in one FMA: the exact result (q - 4) * sc
         // and 1028 * sc (<= 11 significant bits) are both representable, so the
         // single rounding is exact.
@@ -133,14 +136,31 @@ __device__ __forceinline__ uint4 gf4_word_to_halves(uint32_t w) {
             h[i] = *reinterpret_cast<const uint32_t *>(&q);
         }
     }
-    if (!EXACT) {
-        // element 4 = half((q4 - 4) * sc + junk * sc * 2^-13): the exact f32 value rounded once
-        const float junk = __uint_as_float(((w >> 11) & 0x1ffu) | 0x4B000000u) - 8388608.0f;
-        const float h4 = __half2float(__ushort_as_half((unsigned short)(h[0] >> 16)));
-        const __half e4 = __float2half_rn(fmaf(junk, __half2float(sc) * 0.0001220703125f, h4));
-        h[0] = (h[0] & 0x0000ffffu) | ((uint32_t)__half_as_ushort(e4) << 16);
-    }
     return make_uint4(h[0], h[1], h[2], h[3]);
+}
+
+// Metal element 4 = half((q4 - 4) * sc + junk * sc * 2^-13), the exact value
+// rounded once.  Built in fp32 from the word's bits (e5m2 -> f32 by moving the
+// bits and scaling by 2^112, exact for every finite e5m2).
+__device__ __forceinline__ float gf4_elem4_f32(uint32_t w) {
+    const float sraw = __uint_as_float(((w & 0x7fu) << 21) | ((w & 0x80u) << 24));  // s * 2^-112
+    const float q4 = __uint_as_float((((w >> 20) & 7u) ^ 4u) | 0x4B000000u) - 8388612.0f;  // q_raw - 4
+    const float junk = __uint_as_float(((w >> 11) & 0x1ffu) | 0x4B000000u) - 8388608.0f;
+    // s * -0.25 = sraw * -2^110 ; s * -0.25 * 2^-13 = sraw * -2^97
+    return fmaf(junk, sraw * -1.5845632502852868e29f, q4 * (sraw * -1.2980742146337069e33f));
+}
+
+template <bool EXACT>
+__device__ __forceinline__ void gf4_pair_to_halves(uint32_t w0, uint32_t w1, uint4 &o0, uint4 &o1) {
+    uint32_t s0, s1;
+    o0 = gf4_word_levels(w0, s0);
+    o1 = gf4_word_levels(w1, s1);
+    if (!EXACT) {
+        const __half2 e = __floats2half2_rn(gf4_elem4_f32(w0), gf4_elem4_f32(w1));  // one packed conversion
+        const uint32_t eb = *reinterpret_cast<const uint32_t *>(&e);
+        o0.x = __byte_perm(o0.x, eb, 0x5410);  // element 4 is the high half of the first pair
+        o1.x = __byte_perm(o1.x, eb, 0x7610);
+    }
 }
 
 // Q8_0: 8 int8 codes -> 8 exact halves (1024 + (q + 128) - 1152).
@@ -326,16 +346,33 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                 const uint8_t *wst_s = wst + (size_t)s * WS;
 #pragma unroll
                 for (int it = t; it < TM * QPR; it += NT) {
-                    const int r = it / QPR, q = it % QPR;
+                    // 16-item groups, each 8-lane phase conflict-free both on the
+                    // staged-weight read (bank group of row*WS/TM + q*16) and on the
+                    // swizzled store (chunk ^ row%8): GF4 covers rows 4g..4g+3 with
+                    // row bit 1 = q bit 1 ^ phase; Q8_0 rows 2g..2g+1 with row bit 0 =
+                    // q bit 2 ^ phase.
+                    const int l = it & 15, ph8 = (l >> 3) & 1;
+                    int r, q;
+                    if constexpr (CODEC == QW35_GF4_TYPE) {
+                        q = l & 3;
+                        r = (it >> 4) * 4 + ((l >> 2) & 1) + 2 * ((q >> 1) ^ ph8);
+                    } else {
+                        q = l & 7;
+                        r = (it >> 4) * 2 + ((q >> 2) ^ ph8);
+                    }
                     const uint4 w4 = *reinterpret_cast<const uint4 *>(wst_s + (size_t)r * (WS / TM) + q * 16);
                     // k-block kb (8 columns) -> atom kb / 8, chunk kb % 8 of row r
                     auto aslot = [&](int kb) -> uint4 * {
                         return reinterpret_cast<uint4 *>(a + (size_t)(kb >> 3) * (TM * 128) + sw128_off(r, kb & 7));
                     };
                     if constexpr (CODEC == QW35_GF4_TYPE) {
-                        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) *aslot(4 * q + i) = gf4_word_to_halves<EXACT>(ws[i]);
+                        uint4 o0, o1, o2, o3;
+                        gf4_pair_to_halves<EXACT>(w4.x, w4.y, o0, o1);
+                        gf4_pair_to_halves<EXACT>(w4.z, w4.w, o2, o3);
+                        *aslot(4 * q + 0) = o0;
+                        *aslot(4 * q + 1) = o1;
+                        *aslot(4 * q + 2) = o2;
+                        *aslot(4 * q + 3) = o3;
                     } else {
                         *aslot(2 * q) = q8_codes_to_halves(w4.x, w4.y);
                         *aslot(2 * q + 1) = q8_codes_to_halves(w4.z, w4.w);
