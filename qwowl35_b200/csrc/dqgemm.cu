@@ -19,11 +19,14 @@
 // scale in fp32 (acc += d * block_sum): bit-for-bit the reference's
 // per-block arithmetic up to summation order.
 //
-// CTA: warp 0 TMA producer, warp 1 MMA issuer (+ TMEM owner), then decode
-// warps, then epilogue warps (counts per codec in DqWarps).  Tiles are 128 weight rows x NP batch columns (B padded to a
-// multiple of 16); K streams in 128-column chunks through S shared-memory
-// stages; work units (matrix, row tile, K split) are spread over a persistent
-// grid.  Every wait is bounded (pipe.cuh).  No cluster multicast is used.
+// CTA: warp 0 weight TMA producer, warp 1 MMA issuer (+ TMEM owner), warp 2
+// activation producer, then decode warps (thread = weight row, writing the
+// decoded f16 tile into TMEM with tcgen05.st), then epilogue warps.  Tiles are
+// 128 weight rows x NP batch columns (B padded to 16/32/64); K streams in
+// chunks of one 16 KB weight box (256 GF4 / 128 Q8_0 columns).  The sequence of
+// (matrix, tile, chunk) is split evenly over a persistent grid (stream-K:
+// partial tiles accumulate atomically).  Every wait is bounded (pipe.cuh).  No
+// cluster multicast is used.
 #include <cuda.h>
 
 #include <cstdio>
@@ -41,16 +44,23 @@
 
 namespace qw35 {
 
-constexpr int TM = 128;     // weight rows per tile (MMA M)
-constexpr int KC = 128;     // K columns per stage
-constexpr int NKB = KC / 8; // 16 k-blocks of 8 per stage
-// warp roles per codec: GF4 decode is the bottleneck (16 decode warps, the
-// once-per-unit epilogue needs 4); Q8_0 decodes cheaply but scales every
-// 32-column block in the epilogue (8 + 8).
-template <int CODEC> struct DqWarps {
-    static constexpr int DEC = CODEC == QW35_GF4_TYPE ? 16 : 8;
-    static constexpr int EPI = CODEC == QW35_GF4_TYPE ? 4 : 8;
-    static constexpr int THREADS = (2 + DEC + EPI) * 32;
+constexpr int TM = 128;  // weight rows per tile (MMA M = TMEM lanes)
+constexpr int XKC = 128; // K columns per chunk of the activation prep layout
+
+// Per-codec geometry.  A weight chunk is 128 rows x 128 bytes (one 16 KB TMA
+// box, 128B-swizzled): 256 K columns of GF4 or 128 of Q8_0.  Its decoded f16
+// tile lives in TMEM (128 lanes x KC/2 32-bit columns) and feeds tcgen05.mma
+// as operand A.  Decode warps come in groups of four (one per TMEM lane
+// quarter); the groups split a chunk's K range.
+template <int CODEC> struct DqGeo {
+    static constexpr int KC = CODEC == QW35_GF4_TYPE ? 256 : 128;
+    static constexpr int DEC = CODEC == QW35_GF4_TYPE ? 16 : 8;  // decode warps
+    static constexpr int EPI = CODEC == QW35_GF4_TYPE ? 4 : 8;   // epilogue warps
+    static constexpr int THREADS = (3 + DEC + EPI) * 32;
+    static constexpr int NG = DEC / 4;                            // decode groups
+    static constexpr int GK = KC / NG;                            // K columns per group (64)
+    static constexpr int ACOLS = KC / 2;                          // TMEM columns of one A tile
+    static constexpr uint32_t WS = 128u * 128u;                   // weight stage bytes
 };
 
 enum DqMode { DQ_STORE = 0, DQ_ACCUM = 1, DQ_DUAL = 2 };
@@ -60,45 +70,39 @@ struct DqParams {
     const float *rowscale;  // [NP]
     const uint8_t *sc[2];   // Q8_0 scales planes [rows][K/32] f16
     float *y[2];
-    int rows, K, B, ksplit, tiles, units;
-    uint32_t wbytes;        // bytes of one weight stage (TMA box)
+    int rows, K, B, tiles;
+    int gran, granules;     // schedule: granules of `gran` k-chunks spread over the grid
     unsigned long long *trace;  // debug: per-chunk event stamps of CTA 0 (QW35_DQ_TRACE), or null
 };
-// trace layout: [chunk][6] = producer issue, decoder sees full, decoder done,
-// mma sees full_a, mma committed, (unused)
+// trace layout: [chunk][10] = weight issue, decoder sees full_w, decoder done,
+// mma sees full_a, mma committed, activation issue, mma sees full_x, last
+// decoder warp done, MMA loop SM cycles, (unused)
 #define DQ_TRACE(c, slot) \
-    do { if (p.trace && blockIdx.x == 0 && (c) < 256) p.trace[(c) * 6 + (slot)] = globaltimer(); } while (0)
+    do { if (p.trace && blockIdx.x == 0 && (c) < 255) p.trace[(c) * 10 + (slot)] = globaltimer(); } while (0)
+// kernel-level stamps live in row 255: 0 entry, 1 setup done, 2 activations
+// released (PDL), 3 last epilogue write, 4 max exit over CTAs, 5 ~min entry over CTAs
+#define DQ_STAMP(slot) \
+    do { if (p.trace && blockIdx.x == 0) p.trace[255 * 10 + (slot)] = globaltimer(); } while (0)
+#define DQ_TRACE_MAX(c, slot) \
+    do { if (p.trace && blockIdx.x == 0 && (c) < 255) atomicMax(&p.trace[(c) * 10 + (slot)], globaltimer()); } while (0)
 
-struct DqSmem {  // offsets into dynamic shared memory
-    uint32_t w, x, a, bar, tmem, abort_;
-    int S;
+// activation stage: the chunk's 2*NP rows (hi | lo) x KC columns of f16
+template <int CODEC, int NP>
+__host__ __device__ constexpr uint32_t dq_xstage() { return 2u * NP * DqGeo<CODEC>::KC * 2; }
+
+// TMEM plan (512 columns): accumulators first, then SA decoded A tiles.
+// GF4: two segment accumulators of 2*NP columns [hi products | lo products].
+// Q8_0: R rotating per-32-column-block accumulators (the f16 block scale is
+// applied by the epilogue).
+template <int CODEC, int NP> struct DqTmem {
+    static constexpr int RC = 2 * NP;  // columns of one accumulator
+    static constexpr int SA = CODEC == QW35_GF4_TYPE ? (NP == 64 ? 2 : 3) : 3;
+    static constexpr int ACC_COLS = 512 - SA * DqGeo<CODEC>::ACOLS;
+    static constexpr int R = CODEC == QW35_GF4_TYPE ? 2 : (ACC_COLS / RC < 8 ? ACC_COLS / RC : 8);
+    static constexpr int A0 = ACC_COLS;  // first A column
+    static_assert(R * RC <= ACC_COLS, "TMEM plan");
+    static_assert(CODEC != QW35_GF4_TYPE || R == 2, "GF4 double-buffers its accumulator");
 };
-
-template <int CODEC, int NP>
-__host__ __device__ constexpr uint32_t dq_wstage() {
-    return CODEC == QW35_GF4_TYPE ? TM * KC / 2 : TM * KC;
-}
-template <int NP>
-__host__ __device__ constexpr uint32_t dq_xstage() { return 2u * NP * KC * 2; }  // hi + lo
-__host__ __device__ constexpr uint32_t dq_astage() { return TM * KC * 2; }
-
-// TMEM columns for the accumulators.
-// GF4: 2 unit buffers x 4 independent accumulators (hi/lo x even/odd k-step),
-// so consecutive MMAs never wait on each other's accumulator.  Q8_0: rotating
-// per-block regions (consecutive blocks already use different regions).
-constexpr int GF4_NACC = 1;
-template <int CODEC, int NP>
-__host__ __device__ constexpr int dq_regions() {
-    return CODEC == QW35_GF4_TYPE ? 2 : (512 / (2 * NP) < 8 ? 512 / (2 * NP) : 8);
-}
-// one accumulator = 2*NP columns: [hi-activation products | lo-activation products]
-template <int CODEC, int NP>
-__host__ __device__ constexpr int dq_region_cols() { return CODEC == QW35_GF4_TYPE ? GF4_NACC * 2 * NP : 2 * NP; }
-template <int CODEC, int NP>
-__host__ __device__ constexpr uint32_t dq_tmem_cols() {
-    constexpr int cols = dq_regions<CODEC, NP>() * dq_region_cols<CODEC, NP>();
-    return cols <= 32 ? 32u : cols <= 64 ? 64u : cols <= 128 ? 128u : cols <= 256 ? 256u : 512u;
-}
 
 // ---- decode of one 16-byte chunk of a weight row into 8 halves --------------------
 // GF4: one word -> 8 halves in k order [0,4,1,5,2,6,3,7] (the activation prep
@@ -163,6 +167,67 @@ __device__ __forceinline__ void gf4_pair_to_halves(uint32_t w0, uint32_t w1, uin
     }
 }
 
+// Fast path for one word whose |s| <= 252: {s, s} straight from the scale byte,
+// each pair (1024 + q_raw) * (-0.25 s) + 257 s in one HFMA2 -- exact, since
+// 257 s (9 x 3 significant bits) and the result (q_raw - 4) * -0.25 s are
+// representable.  Also returns {sc, sc} for the element-4 fix.
+__device__ __forceinline__ uint4 gf4_word_fast_levels(uint32_t w, uint32_t &sc2bits) {
+    const uint32_t packed = (w & 0xfff00000u) | ((w >> 4) & 0x0000fff0u);  // codes i | i+4 16 bits apart
+    const uint32_t hs = __byte_perm(w, 0u, 0x0404u);                         // {s, s} as half2
+    const __half2 s2 = *reinterpret_cast<const __half2 *>(&hs);
+    const __half2 sc2 = __hmul2(s2, __half2half2(__ushort_as_half((unsigned short)0xB400)));  // -0.25 s
+    const __half2 c2 = __hmul2(s2, __half2half2(__ushort_as_half((unsigned short)0x5C04)));   // 257 s
+    sc2bits = *reinterpret_cast<const uint32_t *>(&sc2);
+    uint32_t h[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t v = ((packed >> (4 + 3 * i)) & 0x00070007u) ^ 0x64046404u;  // 1024 + q_raw per half
+        const __half2 q = __hfma2(*reinterpret_cast<const __half2 *>(&v), sc2, c2);
+        h[i] = *reinterpret_cast<const uint32_t *>(&q);
+    }
+    return make_uint4(h[0], h[1], h[2], h[3]);
+}
+
+// Metal element 4 of two words in one HFMA2: junk * 2^-13 is exact as
+// (0x3000 | junk) - 0.125, so junk * 2^-13 * sc + level4 is formed exactly
+// and rounded once -- the reference's half(float(int16 * s')) (no overflow:
+// |s| <= 252 on this path).
+__device__ __forceinline__ void gf4_elem4_fast(uint32_t w0, uint32_t w1, uint32_t sc0, uint32_t sc1, uint4 &o0,
+                                               uint4 &o1) {
+    const uint32_t jb = ((w0 >> 11) & 0x1ffu) | ((w1 << 5) & 0x01ff0000u) | 0x30003000u;
+    const __half2 j = __hsub2(*reinterpret_cast<const __half2 *>(&jb),
+                              __half2half2(__ushort_as_half((unsigned short)0x3000)));  // junk * 2^-13
+    const uint32_t scp = __byte_perm(sc0, sc1, 0x7610);       // {sc0, sc1}
+    const uint32_t lv = __byte_perm(o0.x, o1.x, 0x7632);      // {level4(w0), level4(w1)}
+    const __half2 e = __hfma2(j, *reinterpret_cast<const __half2 *>(&scp), *reinterpret_cast<const __half2 *>(&lv));
+    const uint32_t eb = *reinterpret_cast<const uint32_t *>(&e);
+    o0.x = __byte_perm(o0.x, eb, 0x5410);  // element 4 is the high half of the first pair
+    o1.x = __byte_perm(o1.x, eb, 0x7610);
+}
+
+// Four words (one 16-byte piece of a weight row) -> four 8-half outputs.  The
+// fast path is taken when all four scales have |s| <= 252 (byte & 0x7f <=
+// 0x5B), checked at once: adding 0x24 to each byte sets its top bit exactly
+// when the byte exceeds 0x5B.
+template <bool EXACT>
+__device__ __forceinline__ void gf4_quad_to_halves(const uint4 w4, uint4 &o0, uint4 &o1, uint4 &o2, uint4 &o3) {
+    const uint32_t sb = __byte_perm(__byte_perm(w4.x, w4.y, 0x0040u), __byte_perm(w4.z, w4.w, 0x0040u), 0x5410u);
+    if ((((sb & 0x7f7f7f7fu) + 0x24242424u) & 0x80808080u) == 0u) {
+        uint32_t c0, c1, c2, c3;
+        o0 = gf4_word_fast_levels(w4.x, c0);
+        o1 = gf4_word_fast_levels(w4.y, c1);
+        o2 = gf4_word_fast_levels(w4.z, c2);
+        o3 = gf4_word_fast_levels(w4.w, c3);
+        if (!EXACT) {
+            gf4_elem4_fast(w4.x, w4.y, c0, c1, o0, o1);
+            gf4_elem4_fast(w4.z, w4.w, c2, c3, o2, o3);
+        }
+    } else {
+        gf4_pair_to_halves<EXACT>(w4.x, w4.y, o0, o1);
+        gf4_pair_to_halves<EXACT>(w4.z, w4.w, o2, o3);
+    }
+}
+
 // Q8_0: 8 int8 codes -> 8 exact halves (1024 + (q + 128) - 1152).
 __device__ __forceinline__ uint4 q8_codes_to_halves(uint32_t a, uint32_t b) {
     const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6480));  // 1152
@@ -185,282 +250,349 @@ __device__ __forceinline__ void dq_wait(uint64_t *bar, uint32_t parity, volatile
     if (!mbar_wait(bar, parity, code)) *abort_flag = 1;
 }
 
+// Work schedule: the sequence of (matrix, row tile, k-chunk), chunk fastest,
+// cut into gridDim.x contiguous ranges of whole granules (`gran` chunks: 1,
+// or a whole tile where the epilogue must store rather than accumulate), so
+// every CTA streams the same number of weight chunks.  A range crosses tile
+// boundaries as segments; each segment owns one TMEM accumulation.
+__device__ __forceinline__ void dq_range(const DqParams &p, int &gbeg, int &gend) {
+    const long long g = (long long)p.granules;
+    gbeg = (int)((g * blockIdx.x / gridDim.x) * p.gran);
+    gend = (int)((g * (blockIdx.x + 1) / gridDim.x) * p.gran);
+}
+#define DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, ...)                       \
+    for (int g_ = (gbeg); g_ < (gend);) {                                                  \
+        const int q_ = g_ / (nch);                                                         \
+        const int c0 = g_ - q_ * (nch);                                                    \
+        const int c1 = min((nch), c0 + ((gend) - g_));                                     \
+        const int m = q_ / (p).tiles;                                                      \
+        const int tile = q_ - m * (p).tiles;                                               \
+        __VA_ARGS__                                                                        \
+        g_ += c1 - c0;                                                                     \
+    }
+
+// Stage index and phase of a ring, advanced without divisions (the role
+// loops run on single threads, where an integer division per chunk costs
+// more than the copy it schedules).
+struct Ring {
+    int s = 0;
+    uint32_t ph = 0;
+    __device__ __forceinline__ void next(int n) {
+        if (++s == n) { s = 0; ph ^= 1u; }
+    }
+};
+
 template <int CODEC, int NP, int MODE, bool EXACT>
-__global__ void __launch_bounds__(DqWarps<CODEC>::THREADS, 1)
-dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1, DqParams p, int S) {
-    constexpr int R = dq_regions<CODEC, NP>();
-    constexpr uint32_t TCOLS = dq_tmem_cols<CODEC, NP>();
-    constexpr uint32_t XS = dq_xstage<NP>();
-    constexpr uint32_t AS = dq_astage();
+__global__ void __launch_bounds__(DqGeo<CODEC>::THREADS, 1)
+dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1, DqParams p, int SX,
+          int NW) {
+    using G = DqGeo<CODEC>;
+    using T = DqTmem<CODEC, NP>;
+    constexpr int KC = G::KC;
+    constexpr int R = T::R, RC = T::RC, SA = T::SA;
+    constexpr uint32_t XS = dq_xstage<CODEC, NP>();
+    constexpr uint32_t WS = G::WS;
     constexpr uint32_t IDESC = idesc_f16_f32(TM, 2 * NP);  // B = [x_hi rows ; x_lo rows]
-    constexpr int RC = dq_region_cols<CODEC, NP>();
     constexpr bool BLOCKED = CODEC != QW35_GF4_TYPE;
-    constexpr int DQ_DEC_WARPS = DqWarps<CODEC>::DEC;
-    constexpr int DQ_EPI_WARPS = DqWarps<CODEC>::EPI;
+    constexpr int DEC = G::DEC, EPI = G::EPI;
     extern __shared__ __align__(1024) uint8_t smem[];
 
-    const uint32_t WS = p.wbytes;
     // 1024-byte aligned base (128B-swizzle atoms need it)
-    uint8_t *wst = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);  // [S][WS]
-    uint8_t *xst = wst + (size_t)S * WS;            // [S][XS]
-    uint8_t *ast = xst + (size_t)S * XS;            // [S][AS]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ast + (size_t)S * AS);
-    uint64_t *full = bars;                          // [S] producer tx
-    uint64_t *empty_w = full + S;                   // [S] decoders done with raw weights
-    uint64_t *full_a = empty_w + S;                 // [S] decoded tile ready
-    uint64_t *mma_done = full_a + S;                // [S] MMA done with A and X
-    uint64_t *acc_full = mma_done + S;              // [R]
-    uint64_t *acc_empty = acc_full + R;             // [R]
-    uint64_t *drain = acc_empty + R;                // [1] abort-path drain of in-flight MMAs
+    uint8_t *xst = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);  // [SX][XS]
+    uint8_t *wst = xst + (size_t)SX * XS;                                  // [NW][WS]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(wst + (size_t)NW * WS);
+    uint64_t *full_w = bars;         // [NW] weight chunk landed (tx)
+    uint64_t *empty_w = full_w + NW; // [NW] decoders done with the raw weights
+    uint64_t *full_x = empty_w + NW; // [SX] activation chunk landed (tx)
+    uint64_t *free_x = full_x + SX;  // [SX] MMAs done reading the activation chunk
+    uint64_t *full_a = free_x + SX;  // [SA] decoded tile written to TMEM
+    uint64_t *free_a = full_a + SA;  // [SA] MMAs done reading the decoded tile
+    uint64_t *acc_full = free_a + SA;    // [R]
+    uint64_t *acc_empty = acc_full + R;  // [R]
+    uint64_t *drain = acc_empty + R;     // [1] abort-path drain of in-flight MMAs
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nch = p.K / KC;
+    if (p.trace && threadIdx.x == 0) {
+        const unsigned long long t = globaltimer();
+        if (blockIdx.x == 0) p.trace[255 * 10] = t;
+        atomicMax(&p.trace[255 * 10 + 5], ~t);
+    }
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty_w[s], DQ_DEC_WARPS);
-            mbar_init(&full_a[s], DQ_DEC_WARPS);
-            mbar_init(&mma_done[s], 1);
+        for (int s = 0; s < NW; ++s) {
+            mbar_init(&full_w[s], 1);
+            mbar_init(&empty_w[s], DEC);
+        }
+        for (int s = 0; s < SX; ++s) {
+            mbar_init(&full_x[s], 1);
+            mbar_init(&free_x[s], 1);
+        }
+        for (int s = 0; s < SA; ++s) {
+            mbar_init(&full_a[s], DEC);
+            mbar_init(&free_a[s], 1);
         }
         for (int r = 0; r < R; ++r) {
             mbar_init(&acc_full[r], 1);
-            mbar_init(&acc_empty[r], DQ_EPI_WARPS);
+            mbar_init(&acc_empty[r], EPI);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
-    if (warp == 1) tmem_alloc(tmem_slot, TCOLS);
+    if (warp == 1) tmem_alloc(tmem_slot, 512);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    pdl_trigger();
-
-    // unit u -> (matrix, tile, split)
-    auto unit_of = [&](int u, int &m, int &tile, int &c0, int &c1) {
-        const int per_m = p.tiles * p.ksplit;
-        m = u / per_m;
-        const int rem = u - m * per_m;
-        tile = rem / p.ksplit;
-        const int s = rem - tile * p.ksplit;
-        c0 = (s * nch) / p.ksplit;
-        c1 = ((s + 1) * nch) / p.ksplit;
-    };
+    if (threadIdx.x == 0) DQ_STAMP(1);
+    int gbeg, gend;
+    dq_range(p, gbeg, gend);
 
     if (warp == 0) {
-        // ------------------------------- producer -------------------------------
         if (lane == 0) {
+            // ---------------------------- weight producer ----------------------------
+            // weights are immutable: streaming starts before the previous kernel ends
             const uint64_t pol = policy_evict_first();
-            pdl_wait();  // the activation prep of this matvec was written by the previous kernel
             int c = 0;
-            for (int u = blockIdx.x; u < p.units; u += gridDim.x) {
-                int m, tile, c0, c1;
-                unit_of(u, m, tile, c0, c1);
-                for (int kc = c0; kc < c1; ++kc, ++c) {
-                    const int s = c % S, ph = c / S;
-                    if (c >= S) {
-                        dq_wait(&empty_w[s], (ph - 1) & 1, abort_flag, 8u);
-                        dq_wait(&mma_done[s], (ph - 1) & 1, abort_flag, 8u);
-                    }
+            Ring rw;
+            DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
+                const CUtensorMap *map = m ? &map1 : &map0;
+                for (int kc = c0; kc < c1 && !*abort_flag; ++kc, ++c) {
+                    if (c >= NW) dq_wait(&empty_w[rw.s], rw.ph ^ 1u, abort_flag, 8u);
                     if (*abort_flag) break;
                     DQ_TRACE(c, 0);
-                    mbar_arrive_expect_tx(&full[s], WS + XS);
-                    const int xk = CODEC == QW35_GF4_TYPE ? kc * (KC / 8) : kc * KC;  // element coordinate
-                    tma_load_2d(wst + (size_t)s * WS, m ? &map1 : &map0, xk, tile * TM, &full[s], pol);
-                    bulk_g2s(xst + (size_t)s * XS, p.xprep + (size_t)kc * XS, XS, &full[s], pol);
+                    mbar_arrive_expect_tx(&full_w[rw.s], WS);
+                    // x coordinate in elements: 32-bit words (GF4) or bytes (Q8_0)
+                    const int xk = CODEC == QW35_GF4_TYPE ? kc * (KC / 8) : kc * KC;
+                    tma_load_2d(wst + (size_t)rw.s * WS, map, xk, tile * TM, &full_w[rw.s], pol);
+                    rw.next(NW);
                 }
-                if (*abort_flag) break;
-            }
+            })
+        }
+    } else if (warp == 2) {
+        if (lane == 0) {
+            // -------------------------- activation producer --------------------------
+            // the activation chunks are re-read by every CTA: keep them in L2
+            const uint64_t pol = policy_evict_last();
+            pdl_wait();  // written by the activation prep, the previous kernel
+            DQ_STAMP(2);
+            int c = 0;
+            Ring rx;
+            DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
+                for (int kc = c0; kc < c1 && !*abort_flag; ++kc, ++c) {
+                    if (c >= SX) dq_wait(&free_x[rx.s], rx.ph ^ 1u, abort_flag, 8u);
+                    if (*abort_flag) break;
+                    DQ_TRACE(c, 5);
+                    mbar_arrive_expect_tx(&full_x[rx.s], XS);
+                    bulk_g2s(xst + (size_t)rx.s * XS, p.xprep + (size_t)kc * XS, XS, &full_x[rx.s], pol);
+                    rx.next(SX);
+                }
+            })
         }
     } else if (warp == 1) {
         // ------------------------------ MMA issuer -------------------------------
         if (lane == 0) {
-            int c = 0, blk = 0, ul = 0;
-            for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x, ++ul) {
-                int m, tile, c0, c1;
-                unit_of(u, m, tile, c0, c1);
-                const int ab = ul & 1;
-                if (!BLOCKED && ul >= 2) {
-                    dq_wait(&acc_empty[ab], ((ul >> 1) - 1) & 1, abort_flag, 16u);
-                    tc_fence_after();
-                }
-                for (int kc = c0; kc < c1; ++kc, ++c) {
-                    const int s = c % S, ph = c / S;
-                    dq_wait(&full_a[s], ph & 1, abort_flag, 16u);
-                    if (*abort_flag) break;
-                    DQ_TRACE(c, 3);
-                    tc_fence_after();
-                    const uint32_t a0 = smem_u32(ast + (size_t)s * AS);
-                    const uint32_t x0 = smem_u32(xst + (size_t)s * XS);
+            int c = 0, ul = 0;
+            Ring rx, ra, rb;  // activation stages, A tiles, Q8_0 block accumulators
+            DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
+                if (!*abort_flag) {
+                    const int ab = ul & 1;
+                    if (!BLOCKED && ul >= 2) {
+                        dq_wait(&acc_empty[ab], ((ul >> 1) - 1) & 1, abort_flag, 16u);
+                        tc_fence_after();
+                    }
+                    for (int kc = c0; kc < c1; ++kc, ++c) {
+                        const int sx = rx.s, sa = ra.s;
+                        dq_wait(&full_x[sx], rx.ph, abort_flag, 16u);
+                        DQ_TRACE(c, 6);
+                        dq_wait(&full_a[sa], ra.ph, abort_flag, 16u);
+                        if (*abort_flag) break;
+                        DQ_TRACE(c, 3);
+                        tc_fence_after();
+                        const uint32_t a0 = tmem + T::A0 + sa * G::ACOLS;
+                        // descriptor of k-step 0; later k-steps add a compile-time offset
+                        // (start address field, 16-byte units; smem addresses stay < 2^18)
+                        const uint64_t bd0 = smem_desc_sw128(smem_u32(xst + (size_t)sx * XS));
+                        const uint32_t d0 = tmem + ab * RC;
+                        const long long cyc0 = p.trace ? clock64() : 0;
+                        if constexpr (!BLOCKED) tc_mma_f16_ts(d0, a0, bd0, IDESC, kc > c0 ? 1u : 0u);
 #pragma unroll
-                    for (int j = 0; j < KC / 16; ++j) {
-                        // operands: [k-atom of 64][rows][128 B swizzled]; k-step j = 16 columns
-                        const uint32_t ka = j >> 2, kofs = (j & 3) * 32;
-                        const uint64_t ad = smem_desc_sw128(a0 + ka * (TM * 128) + kofs);
-                        const uint64_t bd = smem_desc_sw128(x0 + ka * (2 * NP * 128) + kofs);
-                        if constexpr (!BLOCKED) {
-                            const uint32_t d = tmem + ab * RC;
-                            tc_mma_f16(d, ad, bd, IDESC, (kc > c0 || j > 0) ? 1u : 0u);
-                        } else {
-                            const int r = blk % R;
-                            if ((j & 1) == 0 && blk >= R) {
-                                dq_wait(&acc_empty[r], ((blk / R) - 1) & 1, abort_flag, 16u);
-                                tc_fence_after();
-                            }
-                            const uint32_t d = tmem + r * RC;
-                            tc_mma_f16(d, ad, bd, IDESC, (j & 1) ? 1u : 0u);
-                            if (j & 1) {
-                                tc_commit(&acc_full[r]);
-                                ++blk;
+                        for (int j = BLOCKED ? 0 : 1; j < KC / 16; ++j) {
+                            // B: [k-atom of 64][2*NP rows][128 B swizzled]; k-step j = 16 columns
+                            const uint64_t bd = bd0 + (uint64_t)((((j >> 2) * (2 * NP * 128)) + (j & 3) * 32) >> 4);
+                            const uint32_t ad = a0 + j * 8;  // 16 f16 of K = 8 TMEM columns
+                            if constexpr (!BLOCKED) {
+                                tc_mma_f16_ts_acc(d0, ad, bd, IDESC);
+                            } else {
+                                const int r = rb.s;
+                                if ((j & 1) == 0 && c * (KC / 32) + (j >> 1) >= R) {
+                                    dq_wait(&acc_empty[r], rb.ph ^ 1u, abort_flag, 16u);
+                                    tc_fence_after();
+                                }
+                                tc_mma_f16_ts(tmem + r * RC, ad, bd, IDESC, (j & 1) ? 1u : 0u);
+                                if (j & 1) {
+                                    tc_commit(&acc_full[r]);
+                                    rb.next(R);
+                                }
                             }
                         }
+                        tc_commit(&free_a[sa]);
+                        tc_commit(&free_x[sx]);
+                        if (p.trace && blockIdx.x == 0 && c < 255) p.trace[c * 10 + 8] = clock64() - cyc0;
+                        DQ_TRACE(c, 4);
+                        rx.next(SX);
+                        ra.next(SA);
                     }
-                    tc_commit(&mma_done[s]);
-                    DQ_TRACE(c, 4);
+                    if constexpr (!BLOCKED) tc_commit(&acc_full[ab]);
+                    ++ul;
                 }
-                if constexpr (!BLOCKED) tc_commit(&acc_full[ab]);
-            }
+            })
         }
-    } else if (warp < 2 + DQ_DEC_WARPS) {
+    } else if (warp < 3 + DEC) {
         // -------------------------------- decoders --------------------------------
-        // items (row, 16-byte piece of the row): consecutive threads take
-        // consecutive pieces, so every quarter-warp reads 128 contiguous bytes
-        constexpr int QPR = CODEC == QW35_GF4_TYPE ? 4 : 8;   // 16-byte pieces per row
-        constexpr int NT = DQ_DEC_WARPS * 32;
-        const int t = threadIdx.x - 64;
+        // thread = one weight row (its TMEM lane); group g of four warps decodes
+        // K columns [g*GK, g*GK + GK) of the chunk into 32 TMEM columns.  The
+        // weight stage is 128B-swizzled: 16-byte piece q of row r sits at
+        // q ^ (r % 8), so the eight rows of a quarter-warp hit distinct banks.
+        const int dw = warp - 3;
+        const int grp = dw >> 2;
+        const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+        const int r = quarter * 32 + lane;
+        const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
         int c = 0;
-        for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x) {
-            int m, tile, c0, c1;
-            unit_of(u, m, tile, c0, c1);
-            for (int kc = c0; kc < c1; ++kc, ++c) {
-                const int s = c % S, ph = c / S;
-                dq_wait(&full[s], ph & 1, abort_flag, 32u);
-                if (t == 0) DQ_TRACE(c, 1);
-                if (c >= S) dq_wait(&mma_done[s], (ph - 1) & 1, abort_flag, 32u);
+        Ring rw, ra;
+        DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
+            for (int kc = c0; kc < c1 && !*abort_flag; ++kc, ++c) {
+                const int sw = rw.s, sa = ra.s;
+                dq_wait(&full_w[sw], rw.ph, abort_flag, 32u);
+                if (dw == 0 && lane == 0) DQ_TRACE(c, 1);
+                if (c >= SA) dq_wait(&free_a[sa], ra.ph ^ 1u, abort_flag, 32u);
                 if (*abort_flag) break;
-                uint8_t *a = ast + (size_t)s * AS;
-                const uint8_t *wst_s = wst + (size_t)s * WS;
+                tc_fence_after();
+                const uint8_t *row = wst + (size_t)sw * WS + r * 128;
+                uint32_t o[32];
+                if constexpr (CODEC == QW35_GF4_TYPE) {
+                    // 64 columns = 8 words = pieces 2g, 2g+1 of the row
+                    const uint4 wa = *reinterpret_cast<const uint4 *>(row + (((2 * grp) ^ (r & 7)) << 4));
+                    const uint4 wb = *reinterpret_cast<const uint4 *>(row + (((2 * grp + 1) ^ (r & 7)) << 4));
+                    uint4 h[8];
+                    gf4_quad_to_halves<EXACT>(wa, h[0], h[1], h[2], h[3]);
+                    gf4_quad_to_halves<EXACT>(wb, h[4], h[5], h[6], h[7]);
 #pragma unroll
-                for (int it = t; it < TM * QPR; it += NT) {
-                    // 16-item groups, each 8-lane phase conflict-free both on the
-                    // staged-weight read (bank group of row*WS/TM + q*16) and on the
-                    // swizzled store (chunk ^ row%8): GF4 covers rows 4g..4g+3 with
-                    // row bit 1 = q bit 1 ^ phase; Q8_0 rows 2g..2g+1 with row bit 0 =
-                    // q bit 2 ^ phase.
-                    const int l = it & 15, ph8 = (l >> 3) & 1;
-                    int r, q;
-                    if constexpr (CODEC == QW35_GF4_TYPE) {
-                        q = l & 3;
-                        r = (it >> 4) * 4 + ((l >> 2) & 1) + 2 * ((q >> 1) ^ ph8);
-                    } else {
-                        q = l & 7;
-                        r = (it >> 4) * 2 + ((q >> 2) ^ ph8);
+                    for (int i = 0; i < 8; ++i) {
+                        o[4 * i] = h[i].x; o[4 * i + 1] = h[i].y; o[4 * i + 2] = h[i].z; o[4 * i + 3] = h[i].w;
                     }
-                    const uint4 w4 = *reinterpret_cast<const uint4 *>(wst_s + (size_t)r * (WS / TM) + q * 16);
-                    // k-block kb (8 columns) -> atom kb / 8, chunk kb % 8 of row r
-                    auto aslot = [&](int kb) -> uint4 * {
-                        return reinterpret_cast<uint4 *>(a + (size_t)(kb >> 3) * (TM * 128) + sw128_off(r, kb & 7));
-                    };
-                    if constexpr (CODEC == QW35_GF4_TYPE) {
-                        uint4 o0, o1, o2, o3;
-                        gf4_pair_to_halves<EXACT>(w4.x, w4.y, o0, o1);
-                        gf4_pair_to_halves<EXACT>(w4.z, w4.w, o2, o3);
-                        *aslot(4 * q + 0) = o0;
-                        *aslot(4 * q + 1) = o1;
-                        *aslot(4 * q + 2) = o2;
-                        *aslot(4 * q + 3) = o3;
-                    } else {
-                        *aslot(2 * q) = q8_codes_to_halves(w4.x, w4.y);
-                        *aslot(2 * q + 1) = q8_codes_to_halves(w4.z, w4.w);
+                } else {
+                    // 64 columns = 64 codes = pieces 4g .. 4g+3 of the row
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint4 w4 = *reinterpret_cast<const uint4 *>(row + (((4 * grp + i) ^ (r & 7)) << 4));
+                        const uint4 h0 = q8_codes_to_halves(w4.x, w4.y), h1 = q8_codes_to_halves(w4.z, w4.w);
+                        o[8 * i] = h0.x; o[8 * i + 1] = h0.y; o[8 * i + 2] = h0.z; o[8 * i + 3] = h0.w;
+                        o[8 * i + 4] = h1.x; o[8 * i + 5] = h1.y; o[8 * i + 6] = h1.z; o[8 * i + 7] = h1.w;
                     }
                 }
-                fence_async_smem();  // generic-proxy writes -> visible to the tensor core
+                tmem_st32(tmem + lane_addr + T::A0 + sa * G::ACOLS + grp * 32, o);
+                tmem_st_wait();
+                tc_fence_before();
                 __syncwarp();
-                if (t == 0) DQ_TRACE(c, 2);
+                if (dw == 0 && lane == 0) DQ_TRACE(c, 2);
                 if (lane == 0) {
-                    mbar_arrive(&empty_w[s]);
-                    mbar_arrive(&full_a[s]);
+                    DQ_TRACE_MAX(c, 7);
+                    mbar_arrive(&empty_w[sw]);
+                    mbar_arrive(&full_a[sa]);
                 }
+                rw.next(NW);
+                ra.next(SA);
             }
-        }
+        })
     } else {
         // -------------------------------- epilogue --------------------------------
         // EPI/4 warps per TMEM lane quarter, each owning NP/(EPI/4) columns
         pdl_wait();  // rowscale / residual y come from earlier kernels
-        constexpr int NH = NP / (DQ_EPI_WARPS / 4);
-        const int ew = warp - 2 - DQ_DEC_WARPS;
-        const int quarter = warp & 3;            // TMEM lane quarter this warp may access
+        constexpr int NH = NP / (EPI / 4);
+        const int ew = warp - 3 - DEC;
+        const int quarter = warp & 3;
         const int n0 = (ew >> 2) * NH;
         const int row_in_tile = quarter * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-        int blk = 0, ul = 0;
-        for (int u = blockIdx.x; u < p.units && !*abort_flag; u += gridDim.x, ++ul) {
-            int m, tile, c0, c1;
-            unit_of(u, m, tile, c0, c1);
-            const int row = tile * TM + row_in_tile;
-            float acc[NH];
+        int ul = 0;
+        Ring rb;
+        DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
+            if (!*abort_flag) {
+                const int row = tile * TM + row_in_tile;
+                float acc[NH];
 #pragma unroll
-            for (int n = 0; n < NH; ++n) acc[n] = 0.0f;
-            if constexpr (!BLOCKED) {
-                const int ab = ul & 1;
-                dq_wait(&acc_full[ab], (ul >> 1) & 1, abort_flag, 64u);
-                tc_fence_after();
+                for (int n = 0; n < NH; ++n) acc[n] = 0.0f;
+                if constexpr (!BLOCKED) {
+                    const int ab = ul & 1;
+                    dq_wait(&acc_full[ab], (ul >> 1) & 1, abort_flag, 64u);
+                    tc_fence_after();
 #pragma unroll
-                for (int part = 0; part < 2; ++part) {  // hi and lo activation products
-                    float tv[NH];
-                    tmem_ld_cols<NH>(tmem + lane_addr + ab * RC + part * NP + n0, tv);
+                    for (int part = 0; part < 2; ++part) {  // hi and lo activation products
+                        float tv[NH];
+                        tmem_ld_cols<NH>(tmem + lane_addr + ab * RC + part * NP + n0, tv);
 #pragma unroll
-                    for (int n = 0; n < NH; ++n) acc[n] += tv[n];
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[ab]);
-            } else {
-                const uint16_t *scl = reinterpret_cast<const uint16_t *>(p.sc[m]) + (size_t)row * (p.K / 32);
-                for (int kc = c0; kc < c1; ++kc) {
-                    uint2 dpk = make_uint2(0, 0);
-                    if (row < p.rows) dpk = *reinterpret_cast<const uint2 *>(scl + kc * 4);
-                    const uint32_t dw[2] = {dpk.x, dpk.y};
+                        for (int n = 0; n < NH; ++n) acc[n] += tv[n];
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&acc_empty[ab]);
+                } else {
+                    const uint16_t *scl = reinterpret_cast<const uint16_t *>(p.sc[m]) + (size_t)row * (p.K / 32);
+                    for (int kc = c0; kc < c1; ++kc) {
+                        uint2 dpk = make_uint2(0, 0);
+                        if (row < p.rows) dpk = *reinterpret_cast<const uint2 *>(scl + kc * 4);
+                        const uint32_t dwd[2] = {dpk.x, dpk.y};
 #pragma unroll
-                    for (int b4 = 0; b4 < 4; ++b4, ++blk) {
-                        const int rg = blk % R;
-                        dq_wait(&acc_full[rg], (blk / R) & 1, abort_flag, 64u);
-                        tc_fence_after();
-                        float tv[NH], tl[NH];
-                        tmem_ld_cols<NH>(tmem + lane_addr + rg * RC + n0, tv);
-                        tmem_ld_cols<NH>(tmem + lane_addr + rg * RC + NP + n0, tl);
+                        for (int b4 = 0; b4 < 4; ++b4) {
+                            const int rg = rb.s;
+                            dq_wait(&acc_full[rg], rb.ph, abort_flag, 64u);
+                            tc_fence_after();
+                            float tv[NH], tl[NH];
+                            tmem_ld_cols<NH>(tmem + lane_addr + rg * RC + n0, tv);
+                            tmem_ld_cols<NH>(tmem + lane_addr + rg * RC + NP + n0, tl);
 #pragma unroll
-                        for (int n = 0; n < NH; ++n) tv[n] += tl[n];
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&acc_empty[rg]);
-                        const float d =
-                            __half2float(__ushort_as_half((unsigned short)((dw[b4 >> 1] >> (16 * (b4 & 1))) & 0xffffu)));
+                            for (int n = 0; n < NH; ++n) tv[n] += tl[n];
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&acc_empty[rg]);
+                            const float d = __half2float(
+                                __ushort_as_half((unsigned short)((dwd[b4 >> 1] >> (16 * (b4 & 1))) & 0xffffu)));
 #pragma unroll
-                        for (int n = 0; n < NH; ++n) acc[n] = fmaf(d, tv[n], acc[n]);
+                            for (int n = 0; n < NH; ++n) acc[n] = fmaf(d, tv[n], acc[n]);
+                            rb.next(R);
+                        }
                     }
                 }
-            }
-            if (row < p.rows && !*abort_flag) {
-                float *y = p.y[MODE == DQ_DUAL ? m : 0];
-                const bool atomic = MODE == DQ_ACCUM || p.ksplit > 1;
+                if (row < p.rows && !*abort_flag) {
+                    float *y = p.y[MODE == DQ_DUAL ? m : 0];
+                    // a segment short of the full K shares its outputs with another CTA
+                    const bool atomic = MODE == DQ_ACCUM || c0 != 0 || c1 != nch;
 #pragma unroll
-                for (int n = 0; n < NH; ++n) {
-                    if (n0 + n < p.B) {
-                        const float v = acc[n] * p.rowscale[n0 + n];
-                        float *dst = y + (size_t)(n0 + n) * p.rows + row;
-                        if (atomic) atomicAdd(dst, v);
-                        else *dst = v;
+                    for (int n = 0; n < NH; ++n) {
+                        if (n0 + n < p.B) {
+                            const float v = acc[n] * p.rowscale[n0 + n];
+                            float *dst = y + (size_t)(n0 + n) * p.rows + row;
+                            if (atomic) atomicAdd(dst, v);
+                            else *dst = v;
+                        }
                     }
+                    if (lane == 0 && ew == 0) DQ_STAMP(3);
                 }
+                ++ul;
             }
-        }
+        })
     }
 
+    // No programmatic launch trigger in this kernel: the next one (normally the
+    // next matvec's activation prep) launches when this grid exits.  Launched
+    // earlier, its CTAs wait beside ours and take issue slots from the decode
+    // warps (a trigger from any thread counts for the whole CTA, and the idle
+    // lanes of the role warps would reach it at once).
     // ---- teardown: nothing of ours may be in flight when TMEM is released ----
     if (threadIdx.x == 32 && *abort_flag) {
         // the MMA issuer drains its own tensor-core work (bounded) before TMEM goes
@@ -470,7 +602,8 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 1) tmem_dealloc(tmem, TCOLS);
+    if (warp == 1) tmem_dealloc(tmem, 512);
+    if (p.trace && threadIdx.x == 0) atomicMax(&p.trace[255 * 10 + 4], globaltimer());
 }
 
 // ---------------------------------------------------------------------------
@@ -479,61 +612,126 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
 // batch row); zeroes the outputs that split-K accumulates into.
 // ---------------------------------------------------------------------------
 template <typename XT>
-__global__ void __launch_bounds__(256) dq_prep_kernel(const XT *x, const float *norm_w, float eps, int K, int B, int NP,
-                                                      int gf4_perm, __half *xh, __half *xl, float *rowscale,
-                                                      float *zero0, float *zero1, int zero_rows) {
-    __shared__ float red[32];
+__device__ __forceinline__ void load8(const XT *p, float *v) {
+    if constexpr (sizeof(XT) == 4) {
+        const float4 a = *reinterpret_cast<const float4 *>(p), b = *reinterpret_cast<const float4 *>(p + 4);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
+        const uint4 u = *reinterpret_cast<const uint4 *>(p);
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __half2 h = *reinterpret_cast<const __half2 *>(&w[i]);
+            v[2 * i] = __low2float(h);
+            v[2 * i + 1] = __high2float(h);
+        }
+    }
+}
+
+// One CTA (128 threads) per padded batch row n; each thread handles groups of
+// 8 consecutive columns (one 16-byte piece of the swizzled tile for hi and one
+// for lo).  Pass 1 reduces sum(x^2) (RMS norm) and max|x * w| together; pass 2
+// writes.  128 threads keep the CTA small enough to share an SM with a
+// running matvec CTA.
+template <typename XT>
+__global__ void __launch_bounds__(128) dq_prep_kernel(const XT *x, const float *norm_w, float eps, int K, int B, int NP,
+                                                      int gf4_perm, __half *xh, float *rowscale, float *zero0,
+                                                      float *zero1, int zero_rows) {
+    __shared__ float red_s[4], red_m[4];
+    pdl_trigger();  // the matvec may start streaming its weights now
+    pdl_wait();     // x (and the outputs zeroed below) belong to earlier kernels
     const int n = blockIdx.x;
+    const int G = K >> 3;
     const XT *xr = x + (size_t)(n < B ? n : 0) * K;
     float inv = 1.0f, e2 = 1.0f;
     if (n < B) {
-        float ss = 0.0f;
-        if (norm_w) {
-            for (int k = threadIdx.x; k < K; k += 256) {
-                const float v = to_f32(xr[k]);
-                ss = fmaf(v, v, ss);
+        float ss = 0.0f, mx = 0.0f;
+        for (int g = threadIdx.x; g < G; g += 128) {
+            float v[8];
+            load8(xr + g * 8, v);
+            if (norm_w) {
+                const float4 w0 = *reinterpret_cast<const float4 *>(norm_w + g * 8);
+                const float4 w1 = *reinterpret_cast<const float4 *>(norm_w + g * 8 + 4);
+                const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    ss = fmaf(v[i], v[i], ss);
+                    mx = fmaxf(mx, fabsf(v[i] * w[i]));
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[i]));
             }
-            ss = block_sum(ss, red);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        }
+        if ((threadIdx.x & 31) == 0) {
+            red_s[threadIdx.x >> 5] = ss;
+            red_m[threadIdx.x >> 5] = mx;
+        }
+        __syncthreads();
+        ss = (red_s[0] + red_s[1]) + (red_s[2] + red_s[3]);
+        mx = fmaxf(fmaxf(red_m[0], red_m[1]), fmaxf(red_m[2], red_m[3]));
+        if (norm_w) {
             inv = rsqrtf(ss / (float)K + eps);
+            mx *= inv;
         }
-        float mx = 0.0f;
-        for (int k = threadIdx.x; k < K; k += 256) {
-            const float v = norm_w ? to_f32(xr[k]) * inv * norm_w[k] : to_f32(xr[k]);
-            mx = fmaxf(mx, fabsf(v));
-        }
-        mx = warp_max(mx);
-        __syncthreads();
-        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-        __syncthreads();
-        mx = 0.0f;
-        for (int i = 0; i < 8; ++i) mx = fmaxf(mx, red[i]);
         int ex = 0;
         if (mx > 0.0f && isfinite(mx)) {
             frexpf(mx, &ex);
-            ex -= 15;  // max |v| * 2^-ex in [2^14, 2^15)
+            ex -= 15;  // max |v| * 2^-ex in [2^14, 2^15) (2x margin for rounding of the max)
         }
         e2 = ldexpf(1.0f, ex);
         if (threadIdx.x == 0) rowscale[n] = e2;
-        if (zero0)
-            for (int r = threadIdx.x; r < zero_rows; r += 256) zero0[(size_t)n * zero_rows + r] = 0.0f;
-        if (zero1)
-            for (int r = threadIdx.x; r < zero_rows; r += 256) zero1[(size_t)n * zero_rows + r] = 0.0f;
     } else if (threadIdx.x == 0) {
         rowscale[n] = 1.0f;
     }
     const float rs = 1.0f / e2;  // exact power of two
-    for (int k = threadIdx.x; k < K; k += 256) {
-        float v = 0.0f;
-        if (n < B) v = (norm_w ? to_f32(xr[k]) * inv * norm_w[k] : to_f32(xr[k])) * rs;
-        const __half hi = __float2half_rn(v);
-        const __half lo = __float2half_rn(v - __half2float(hi));
+    for (int g = threadIdx.x; g < G; g += 128) {
+        float v[8];
+        if (n < B) {
+            load8(xr + g * 8, v);
+            if (norm_w) {
+                const float4 w0 = *reinterpret_cast<const float4 *>(norm_w + g * 8);
+                const float4 w1 = *reinterpret_cast<const float4 *>(norm_w + g * 8 + 4);
+                const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = (v[i] * inv * w[i]) * rs;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = v[i] * rs;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+        }
+        // GF4 tiles hold a word's k in the order [0,4,1,5,2,6,3,7]
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float a = gf4_perm ? v[i] : v[2 * i], b = gf4_perm ? v[i + 4] : v[2 * i + 1];
+            const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+            const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+            hw[i] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+            lw[i] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+        }
         // per 128-column chunk: [k-atom of 64][2*NP rows: hi rows, then lo rows][128 B swizzled]
-        const int i = k & 7, kl = k & 127;
-        const int slot = gf4_perm ? (i < 4 ? 2 * i : 2 * (i - 4) + 1) : i;
-        const size_t base = (size_t)(k >> 7) * (2 * NP) * 128 + (size_t)(kl >> 6) * (2 * NP) * 64 + slot;
+        const int k = g * 8, kl = k & 127;
+        uint8_t *base = reinterpret_cast<uint8_t *>(xh) + (size_t)(k >> 7) * (2 * NP) * 256 +
+                        (size_t)(kl >> 6) * (2 * NP) * 128;
         const uint32_t c = (uint32_t)((kl & 63) >> 3);
-        xh[base + sw128_off((uint32_t)n, c) / 2] = hi;
-        xh[base + sw128_off((uint32_t)(NP + n), c) / 2] = lo;
+        *reinterpret_cast<uint4 *>(base + sw128_off((uint32_t)n, c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *reinterpret_cast<uint4 *>(base + sw128_off((uint32_t)(NP + n), c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    if (n < B && (zero0 || zero1)) {
+        __syncthreads();  // every read of x row n is done (y may alias x)
+        for (int r = threadIdx.x; r < zero_rows; r += 128) {
+            if (zero0) zero0[(size_t)n * zero_rows + r] = 0.0f;
+            if (zero1) zero1[(size_t)n * zero_rows + r] = 0.0f;
+        }
     }
 }
 
@@ -617,17 +815,18 @@ bool weight_map(uint32_t type_id, const void *w, uint32_t rows, uint32_t k, CUte
     cuuint64_t dims[2], strides[1];
     cuuint32_t box[2], estr[2] = {1, 1};
     CUtensorMapDataType dt;
+    // 128 rows x 128 bytes per box, 128B-swizzled (16-byte piece q of row r at q ^ (r % 8))
     if (type_id == QW35_GF4_TYPE) {
         dt = CU_TENSOR_MAP_DATA_TYPE_UINT32;
         dims[0] = k / 8; dims[1] = rows; strides[0] = (cuuint64_t)k / 2;
-        box[0] = KC / 8; box[1] = TM;
+        box[0] = 32; box[1] = TM;
     } else {
         dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
         dims[0] = k; dims[1] = rows; strides[0] = k;
-        box[0] = KC; box[1] = TM;
+        box[0] = 128; box[1] = TM;
     }
     if (fn(&m, dt, 2, const_cast<void *>(w), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
         CUDA_SUCCESS)
         return false;
     cache[key] = m;
@@ -672,8 +871,13 @@ int dq_np(int B) { return B <= 16 ? 16 : (B <= 32 ? 32 : 64); }
 }  // namespace
 
 bool dq_supported(const MatvecArgs &a) {
+    // TMA needs 16-byte aligned weights; the activation prep reads x and the
+    // norm weight 16 bytes at a time
+    auto a16 = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
     return a.batch >= 16 && a.batch <= 64 && (a.type_id == QW35_GF4_TYPE || a.type_id == QW35_Q8_0_TYPE) &&
-           a.k % KC == 0 && encode_fn() != nullptr && !getenv("QW35_NO_TCGEN05");
+           a.k % (a.type_id == QW35_GF4_TYPE ? DqGeo<QW35_GF4_TYPE>::KC : DqGeo<QW35_Q8_0_TYPE>::KC) == 0 &&
+           a16(a.w0) && a16(a.w1) && a16(a.x) && a16(a.norm_w) && encode_fn() != nullptr &&
+           !getenv("QW35_NO_TCGEN05");
 }
 
 size_t dq_scratch_bytes(int B, uint32_t k, uint32_t rows_out) {
@@ -689,26 +893,36 @@ cudaError_t dq_reserve(int max_batch, uint32_t max_k, uint32_t max_rows_out) {
 template <int CODEC, int NP, int MODE, bool EXACT>
 static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, DqParams p, cudaStream_t st) {
     auto kern = dq_kernel<CODEC, NP, MODE, EXACT>;
-    constexpr uint32_t stage = dq_wstage<CODEC, NP>() + dq_xstage<NP>() + dq_astage();
-    const int S = (int)std::min<uint32_t>(4u, (198u * 1024u) / stage);
-    const size_t smem = 1024 + (size_t)S * stage + (4 * S + 2 * dq_regions<CODEC, NP>() + 1) * 8 + 16;
+    // SX activation stages (two when they are 64 KB), then as many weight stages as fit
+    // <= 192 KB, so a 128-thread activation prep CTA fits beside it on the SM
+    constexpr uint32_t budget = 192u * 1024u;
+    constexpr uint32_t xs = dq_xstage<CODEC, NP>(), ws = DqGeo<CODEC>::WS;
+    int SX = xs >= 65536u ? 2 : 3;
+    int NW = std::min(4, (int)((budget - SX * xs) / ws));
+    static const int env_sx = getenv("QW35_DQ_SX") ? atoi(getenv("QW35_DQ_SX")) : 0;  // tuning experiments
+    static const int env_nw = getenv("QW35_DQ_NW") ? atoi(getenv("QW35_DQ_NW")) : 0;
+    if (env_sx) SX = env_sx;
+    if (env_nw) NW = env_nw;
+    if (SX < 2 || NW < 2 || SX * xs + NW * ws > budget) return cudaErrorInvalidValue;
+    using T = DqTmem<CODEC, NP>;
+    const size_t smem = 1024 + (size_t)SX * xs + (size_t)NW * ws + (2 * NW + 2 * SX + 2 * T::SA + 2 * T::R + 1) * 8 + 16;
     static bool attr = false;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 210 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    p.wbytes = dq_wstage<CODEC, NP>();
     static unsigned long long *trace = nullptr;
-    if (getenv("QW35_DQ_TRACE")) {
-        if (!trace) cudaMalloc(&trace, 256 * 6 * 8);
-        cudaMemsetAsync(trace, 0, 256 * 6 * 8, st);
+    static const bool want_trace = getenv("QW35_DQ_TRACE") != nullptr;
+    if (want_trace) {
+        if (!trace) cudaMalloc(&trace, 256 * 10 * 8);
+        cudaMemsetAsync(trace, 0, 256 * 10 * 8, st);
         p.trace = trace;
     }
-    const int grid = std::min(p.units, qw35h::sm_count());
+    const int grid = std::min(p.granules, qw35h::sm_count());
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(DqWarps<CODEC>::THREADS);
+    cfg.blockDim = dim3(DqGeo<CODEC>::THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attrs[1];
@@ -716,16 +930,24 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, DqPar
     attrs[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = getenv("QW35_NO_PDL") ? 0 : 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m0, m1, p, S);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m0, m1, p, SX, NW);
     if (p.trace) {
-        unsigned long long h[256 * 6];
+        unsigned long long h[256 * 10];
         cudaMemcpy(h, trace, sizeof(h), cudaMemcpyDeviceToHost);
         const unsigned long long t0 = h[0];
-        fprintf(stderr, "dq trace units=%d grid=%d S=%d ksplit=%d (ns from first issue)\n", p.units, grid, S, p.ksplit);
-        for (int c = 0; c < 256 && h[c * 6]; ++c)
-            fprintf(stderr, "c%3d issue %7lld full %7lld dec %7lld mma %7lld done %7lld\n", c, (long long)(h[c * 6] - t0),
-                    (long long)(h[c * 6 + 1] - t0), (long long)(h[c * 6 + 2] - t0), (long long)(h[c * 6 + 3] - t0),
-                    (long long)(h[c * 6 + 4] - t0));
+        const unsigned long long *k = h + 255 * 10;
+        auto rel = [&](unsigned long long v) { return v ? (long long)(v - k[0]) : -1ll; };
+        fprintf(stderr, "dq kernel: first CTA entry %lld, CTA0 setup %lld, act released %lld, first W issue %lld, "
+                        "CTA0 last epilogue %lld, last CTA exit %lld (ns from CTA0 entry)\n",
+                rel(~k[5]), rel(k[1]), rel(k[2]), rel(t0), rel(k[3]), rel(k[4]));
+        fprintf(stderr, "dq trace granules=%d gran=%d grid=%d SX=%d SA=%d NW=%d (ns from first issue)\n", p.granules,
+                p.gran, grid, SX, T::SA, NW);
+        for (int c = 0; c < 255 && h[c * 10]; ++c) {
+            const unsigned long long *r = h + c * 10;
+            auto d = [&](int i) { return r[i] ? (long long)(r[i] - t0) : -1ll; };
+            fprintf(stderr, "c%3d w %6lld x %6lld | dec: full %6lld w0 %6lld last %6lld | mma: x %6lld a %6lld done %6lld cyc %4llu\n",
+                    c, d(0), d(5), d(1), d(2), d(7), d(6), d(3), d(4), r[8]);
+        }
     }
     return e;
 }
@@ -752,7 +974,7 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
     if (!weight_map(a.type_id, a.w0, a.rows, a.k, &m0)) return cudaErrorInvalidValue;
     if (dual && !weight_map(a.type_id, a.w1, a.rows, a.k, &m1)) return cudaErrorInvalidValue;
     if (!dual) m1 = m0;
-    // scratch: [xh | xl] halves, rowscale, then (swiglu) gate|up or (head) logits
+    // scratch: activation tiles (hi and lo rows), rowscale, then (swiglu) gate|up or (head) logits
     const size_t xbytes = (size_t)NP * K * 2;
     const size_t extra = (mode == 2) ? (size_t)2 * B * rows * 4 : (mode == 3 && !a.y) ? (size_t)B * rows * 4 : 0;
     void *scr = nullptr;
@@ -760,27 +982,22 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
     if (e != cudaSuccess) return e;
     uint8_t *base = static_cast<uint8_t *>(scr);
     __half *xh = reinterpret_cast<__half *>(base);
-    __half *xl = reinterpret_cast<__half *>(base + xbytes);
     float *rowscale = reinterpret_cast<float *>(base + 2 * xbytes);
     float *ext = reinterpret_cast<float *>(base + 2 * xbytes + 256);
 
     const int tiles = (rows + TM - 1) / TM;
-    const int nch = K / KC;
-    const int sms = qw35h::sm_count();
-    const int per_m_tiles = tiles * (dual ? 2 : 1);
-    int ksplit = (3 * sms + per_m_tiles - 1) / per_m_tiles;
-    ksplit = std::max(1, std::min(ksplit, nch / 4 > 0 ? nch / 4 : 1));
-    if (mode == 3) ksplit = 1;  // logits: plain stores, no atomics
-
+    const int nch = K / (a.type_id == QW35_GF4_TYPE ? DqGeo<QW35_GF4_TYPE>::KC : DqGeo<QW35_Q8_0_TYPE>::KC);
+    // logits (mode 3) are stored, never accumulated: whole tiles per CTA
+    const int gran = mode == 3 ? nch : 1;
     DqParams p{};
     p.xprep = base;
     p.rowscale = rowscale;
     p.rows = rows;
     p.K = K;
     p.B = B;
-    p.ksplit = ksplit;
     p.tiles = tiles;
-    p.units = tiles * ksplit * (dual ? 2 : 1);
+    p.gran = gran;
+    p.granules = tiles * (dual ? 2 : 1) * (nch / gran);
     float *y0, *y1 = nullptr;
     int dmode;
     if (mode == 2) { y0 = ext; y1 = ext + (size_t)B * rows; dmode = DQ_DUAL; }
@@ -793,14 +1010,27 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
         p.sc[1] = dual ? static_cast<const uint8_t *>(a.w1) + (size_t)rows * K : p.sc[0];
     }
     // prep (+ zeroing of split-K outputs)
-    const bool zero = dmode != DQ_ACCUM && ksplit > 1;
+    const bool zero = dmode != DQ_ACCUM && gran < nch;
     const bool gperm = a.type_id == QW35_GF4_TYPE;
-    if (a.x_dtype == QW35_F16_TYPE)
-        dq_prep_kernel<__half><<<NP, 256, 0, st>>>(static_cast<const __half *>(a.x), a.norm_w, a.eps, K, B, NP, gperm,
-                                                  xh, xl, rowscale, zero ? y0 : nullptr, zero ? y1 : nullptr, rows);
-    else
-        dq_prep_kernel<float><<<NP, 256, 0, st>>>(static_cast<const float *>(a.x), a.norm_w, a.eps, K, B, NP, gperm,
-                                                 xh, xl, rowscale, zero ? y0 : nullptr, zero ? y1 : nullptr, rows);
+    {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(NP);
+        cfg.blockDim = dim3(128);
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = getenv("QW35_NO_PDL") ? 0 : 1;
+        float *z0 = zero ? y0 : nullptr, *z1 = zero ? y1 : nullptr;
+        if (a.x_dtype == QW35_F16_TYPE)
+            e = cudaLaunchKernelEx(&cfg, dq_prep_kernel<__half>, static_cast<const __half *>(a.x), a.norm_w, a.eps, K,
+                                   B, NP, (int)gperm, xh, rowscale, z0, z1, (int)rows);
+        else
+            e = cudaLaunchKernelEx(&cfg, dq_prep_kernel<float>, static_cast<const float *>(a.x), a.norm_w, a.eps, K, B,
+                                   NP, (int)gperm, xh, rowscale, z0, z1, (int)rows);
+        if (e != cudaSuccess) return e;
+    }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const bool exact = (a.flags & QW35_MV_GF4_EXACT) != 0;

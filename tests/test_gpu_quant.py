@@ -206,3 +206,38 @@ def test_batched_and_single_paths_agree():
     from qwowl35_b200 import lib
     torch.cuda.synchronize()
     assert lib().qw35_cuda_device_error() == 0
+
+
+def _random_words_all_scales(rng, rows, k):
+    """GF4 words with every finite e5m2 scale byte (both decode paths of the
+    tensor-core kernel: |s| <= 252 and larger) and random codes / junk bits."""
+    w = rng.integers(0, 2**32, size=(rows, k // 8), dtype=np.uint64).astype(np.uint32)
+    sb = rng.integers(0, 256, size=w.shape, dtype=np.uint32)
+    sb = np.where((sb & 0x7C) == 0x7C, sb & 0xF3, sb)  # no inf / NaN scales
+    return ((w & np.uint32(0xFFFFFF00)) | sb).view(np.uint8).reshape(-1)
+
+
+@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE])
+@pytest.mark.parametrize("exact", [False, True])
+def test_batched_path_weights_bit_exact(t, exact):
+    """One-hot activation rows make y[b][r] = W[r][k_b] a single exact product,
+    so the tensor-core path's decoded weights are compared bit for bit with the
+    oracle (GF4 element 4 rounded to half as the reference's tiled path does)."""
+    if t == Q.Q8_0_TYPE and exact:
+        pytest.skip("one Q8_0 mode")
+    rows, k, b = 333, 256, 64
+    rng = np.random.default_rng(31)
+    if t == Q.GF4_TYPE:
+        raw = _random_words_all_scales(rng, rows, k)
+    else:
+        raw = Q.gen_weight(rng, t, rows, k)
+        blocks = raw.reshape(-1, 34)
+        d = rng.standard_normal(blocks.shape[0]).astype(np.float16) * np.float16(4)
+        blocks[:, 0:2] = d.view(np.uint8).reshape(-1, 2)
+    w = ops.upload(t, raw, rows, k)
+    deq = Q.dequant(t, raw, rows, k, gf4_exact=exact, gf4_half=not exact).astype(np.float32)
+    for k0 in range(0, k, b):
+        x = np.zeros((b, k), dtype=np.float32)
+        x[np.arange(b), k0 + np.arange(b)] = 1.0
+        y = ops.matvec(t, w, torch.from_numpy(x).cuda(), rows, k, exact=exact).cpu().numpy()
+        np.testing.assert_array_equal(y, deq[:, k0:k0 + b].T)
