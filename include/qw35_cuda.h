@@ -49,9 +49,13 @@ const char *qw35_cuda_build_info(void);
 uint32_t qw35_cuda_device_error(void);
 
 // Weights ---------------------------------------------------------------------
-// Bytes of a rows x k matrix of `type_id` (identical for GGUF and device layouts).
+// Bytes of a rows x k matrix of `type_id` in GGUF block layout.
 uint64_t qw35_cuda_weight_bytes(uint32_t type_id, uint32_t rows, uint32_t k);
-// GGUF block layout (device memory) -> device layout (quant.cuh).  src != dst.
+// Bytes of the same matrix in device layout: as GGUF, except Q8_0, which adds a
+// plane of one exponent byte per row (16-byte padded) for the tensor-core path.
+uint64_t qw35_cuda_device_bytes(uint32_t type_id, uint32_t rows, uint32_t k);
+// GGUF block layout (device memory) -> device layout (quant.cuh); dst holds
+// qw35_cuda_device_bytes.  src != dst.
 int qw35_cuda_weight_repack(uint32_t type_id, const void *src, void *dst, uint32_t rows, uint32_t k,
                             void *stream, char *err, uintptr_t err_len);
 // Device-layout weights -> float32 [rows][k] (bit-exact dequantisation).

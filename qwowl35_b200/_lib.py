@@ -71,6 +71,7 @@ _SIGS = {
     "qw35_cuda_build_info": (C.c_char_p, []),
     "qw35_cuda_device_error": (C.c_uint32, []),
     "qw35_cuda_weight_bytes": (C.c_uint64, [C.c_uint32, C.c_uint32, C.c_uint32]),
+    "qw35_cuda_device_bytes": (C.c_uint64, [C.c_uint32, C.c_uint32, C.c_uint32]),
     "qw35_cuda_weight_repack": (C.c_int, [C.c_uint32, vp, vp, C.c_uint32, C.c_uint32, vp, cp, up]),
     "qw35_cuda_dequant": (C.c_int, [C.c_uint32, vp, vp, C.c_uint32, C.c_uint32, C.c_uint32, vp, cp, up]),
     "qw35_cuda_matvec": (C.c_int, [C.c_uint32, vp, vp, C.c_uint32, vp, C.c_uint32, C.c_uint32, C.c_uint32, C.c_int,

@@ -43,6 +43,37 @@ __global__ void repack_q8_0_kernel(const uint8_t *src, uint8_t *dst, size_t nblk
     scales[b] = (uint16_t)s[0] | ((uint16_t)s[1] << 8);
 }
 
+// Q8_0 row exponents (device-layout tail plane, one int8 per row): e with
+// 128 * max|d| * 2^e < 2^15, i.e. e = 7 - floor(log2(max|d|)) (0 for an
+// all-zero or non-finite row).  The tensor-core matvec splits q * d * 2^e
+// into exact f16 hi + lo halves and removes 2^e in its epilogue.
+__global__ void q8_0_row_exp_kernel(uint8_t *dst, uint32_t rows, uint32_t k) {
+    const uint32_t r = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    const uint16_t *scales = reinterpret_cast<const uint16_t *>(dst + (size_t)rows * k) + (size_t)r * (k / 32);
+    uint32_t mx = 0;  // max of |d| bits (monotone for finite halves)
+    for (uint32_t b = threadIdx.x & 31; b < k / 32; b += 32) {
+        const uint32_t a = scales[b] & 0x7fffu;
+        mx = a > mx ? a : mx;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint32_t v = __shfl_xor_sync(0xffffffffu, mx, o);
+        mx = v > mx ? v : mx;
+    }
+    if ((threadIdx.x & 31) == 0) {
+        int e = 0;
+        if (mx != 0 && mx < 0x7c00u) {
+            const int ex = (int)(mx >> 10);  // biased exponent, 0 for subnormals
+            int m = ex - 15;                 // floor(log2) of a normal half
+            if (ex == 0) m = 31 - __clz(mx & 0x3ffu) - 24;  // subnormal: mantissa * 2^-24
+            e = 7 - m;
+        }
+        int8_t *ep = reinterpret_cast<int8_t *>(dst + (size_t)rows * (k / 32) * 34);
+        ep[r] = (int8_t)e;
+    }
+}
+
 // Q4_K: one thread per 144-byte block.  GGUF qs byte 32g+l holds element 64g+l
 // (low nibble) and 64g+32+l (high); the device codes plane holds elements in
 // order, two per byte.  The 16-byte header (d, dmin, scales) is kept verbatim.
@@ -76,6 +107,9 @@ cudaError_t weight_repack(uint32_t type_id, const void *src, void *dst, uint32_t
     if (type_id == QW35_Q8_0_TYPE) {
         const size_t nb = (size_t)rows * (k / 32);
         repack_q8_0_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, st>>>(s, d, nb, rows, k);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+        q8_0_row_exp_kernel<<<(rows + 7) / 8, 256, 0, st>>>(d, rows, k);
         return cudaGetLastError();
     }
     if (type_id == QW35_Q4_K_TYPE) {

@@ -47,20 +47,24 @@ namespace qw35 {
 constexpr int TM = 128;  // weight rows per tile (MMA M = TMEM lanes)
 constexpr int XKC = 128; // K columns per chunk of the activation prep layout
 
-// Per-codec geometry.  A weight chunk is 128 rows x 128 bytes (one 16 KB TMA
-// box, 128B-swizzled): 256 K columns of GF4 or 128 of Q8_0.  Its decoded f16
-// tile lives in TMEM (128 lanes x KC/2 32-bit columns) and feeds tcgen05.mma
-// as operand A.  Decode warps come in groups of four (one per TMEM lane
+// Per-codec geometry.  A weight chunk is 128 rows x 128 bytes of codes (one
+// 16 KB TMA box, 128B-swizzled): 256 K columns of GF4 or 128 of Q8_0; Q8_0
+// stages also carry the chunk's block scales (a second 2 KB box).  The
+// decoded f16 tile lives in TMEM (128 lanes x 128 32-bit columns: GF4 256
+// columns of K; Q8_0 hi and lo halves of 128) and feeds tcgen05.mma as
+// operand A.  Decode warps come in groups of four (one per TMEM lane
 // quarter); the groups split a chunk's K range.
 template <int CODEC> struct DqGeo {
-    static constexpr int KC = CODEC == QW35_GF4_TYPE ? 256 : 128;
-    static constexpr int DEC = CODEC == QW35_GF4_TYPE ? 16 : 8;  // decode warps
-    static constexpr int EPI = CODEC == QW35_GF4_TYPE ? 4 : 8;   // epilogue warps
+    static constexpr bool Q8 = CODEC == QW35_Q8_0_TYPE;
+    static constexpr int KC = Q8 ? 128 : 256;
+    static constexpr int DEC = Q8 ? 8 : 16;                       // decode warps
+    static constexpr int EPI = 4;                                 // epilogue warps
     static constexpr int THREADS = (3 + DEC + EPI) * 32;
     static constexpr int NG = DEC / 4;                            // decode groups
     static constexpr int GK = KC / NG;                            // K columns per group (64)
-    static constexpr int ACOLS = KC / 2;                          // TMEM columns of one A tile
-    static constexpr uint32_t WS = 128u * 128u;                   // weight stage bytes
+    static constexpr int ACOLS = 128;                             // TMEM columns of one A tile
+    static constexpr uint32_t WCODES = 128u * 128u;               // codes bytes of a stage
+    static constexpr uint32_t WS = WCODES + (Q8 ? 128u * 16u : 0u);  // + 8 scales per row
 };
 
 enum DqMode { DQ_STORE = 0, DQ_ACCUM = 1, DQ_DUAL = 2 };
@@ -68,7 +72,7 @@ enum DqMode { DQ_STORE = 0, DQ_ACCUM = 1, DQ_DUAL = 2 };
 struct DqParams {
     const uint8_t *xprep;   // per 128-column chunk [2 k-atoms][2*NP rows (hi | lo)][128 B swizzled] f16
     const float *rowscale;  // [NP]
-    const uint8_t *sc[2];   // Q8_0 scales planes [rows][K/32] f16
+    const int8_t *rexp[2];  // Q8_0 per-row exponent planes (device-layout tail)
     float *y[2];
     int rows, K, B, tiles;
     int gran, granules;     // schedule: granules of `gran` k-chunks spread over the grid
@@ -90,18 +94,13 @@ struct DqParams {
 template <int CODEC, int NP>
 __host__ __device__ constexpr uint32_t dq_xstage() { return 2u * NP * DqGeo<CODEC>::KC * 2; }
 
-// TMEM plan (512 columns): accumulators first, then SA decoded A tiles.
-// GF4: two segment accumulators of 2*NP columns [hi products | lo products].
-// Q8_0: R rotating per-32-column-block accumulators (the f16 block scale is
-// applied by the epilogue).
+// TMEM plan (512 columns): two segment accumulators of 2*NP columns
+// [hi-activation products | lo-activation products], then SA decoded A tiles.
 template <int CODEC, int NP> struct DqTmem {
     static constexpr int RC = 2 * NP;  // columns of one accumulator
-    static constexpr int SA = CODEC == QW35_GF4_TYPE ? (NP == 64 ? 2 : 3) : 3;
-    static constexpr int ACC_COLS = 512 - SA * DqGeo<CODEC>::ACOLS;
-    static constexpr int R = CODEC == QW35_GF4_TYPE ? 2 : (ACC_COLS / RC < 8 ? ACC_COLS / RC : 8);
-    static constexpr int A0 = ACC_COLS;  // first A column
-    static_assert(R * RC <= ACC_COLS, "TMEM plan");
-    static_assert(CODEC != QW35_GF4_TYPE || R == 2, "GF4 double-buffers its accumulator");
+    static constexpr int SA = NP == 64 ? 2 : 3;
+    static constexpr int A0 = 512 - SA * DqGeo<CODEC>::ACOLS;  // first A column
+    static_assert(2 * RC <= A0, "TMEM plan");
 };
 
 // ---- decode of one 16-byte chunk of a weight row into 8 halves --------------------
@@ -284,16 +283,18 @@ struct Ring {
 
 template <int CODEC, int NP, int MODE, bool EXACT>
 __global__ void __launch_bounds__(DqGeo<CODEC>::THREADS, 1)
-dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1, DqParams p, int SX,
+dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1,
+          const __grid_constant__ CUtensorMap smap0, const __grid_constant__ CUtensorMap smap1, DqParams p, int SX,
           int NW) {
     using G = DqGeo<CODEC>;
     using T = DqTmem<CODEC, NP>;
+    constexpr bool Q8 = G::Q8;
     constexpr int KC = G::KC;
-    constexpr int R = T::R, RC = T::RC, SA = T::SA;
+    constexpr int RC = T::RC, SA = T::SA;
     constexpr uint32_t XS = dq_xstage<CODEC, NP>();
     constexpr uint32_t WS = G::WS;
     constexpr uint32_t IDESC = idesc_f16_f32(TM, 2 * NP);  // B = [x_hi rows ; x_lo rows]
-    constexpr bool BLOCKED = CODEC != QW35_GF4_TYPE;
+    constexpr uint32_t IDESC_HI = idesc_f16_f32(TM, NP);   // B = x_hi rows only (Q8_0 lo weights)
     constexpr int DEC = G::DEC, EPI = G::EPI;
     extern __shared__ __align__(1024) uint8_t smem[];
 
@@ -307,9 +308,9 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
     uint64_t *free_x = full_x + SX;  // [SX] MMAs done reading the activation chunk
     uint64_t *full_a = free_x + SX;  // [SA] decoded tile written to TMEM
     uint64_t *free_a = full_a + SA;  // [SA] MMAs done reading the decoded tile
-    uint64_t *acc_full = free_a + SA;    // [R]
-    uint64_t *acc_empty = acc_full + R;  // [R]
-    uint64_t *drain = acc_empty + R;     // [1] abort-path drain of in-flight MMAs
+    uint64_t *acc_full = free_a + SA;    // [2] segment accumulator complete
+    uint64_t *acc_empty = acc_full + 2;  // [2] epilogue done reading it
+    uint64_t *drain = acc_empty + 2;     // [1] abort-path drain of in-flight MMAs
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -334,7 +335,7 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
             mbar_init(&full_a[s], DEC);
             mbar_init(&free_a[s], 1);
         }
-        for (int r = 0; r < R; ++r) {
+        for (int r = 0; r < 2; ++r) {
             mbar_init(&acc_full[r], 1);
             mbar_init(&acc_empty[r], EPI);
         }
@@ -360,14 +361,17 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
             Ring rw;
             DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
                 const CUtensorMap *map = m ? &map1 : &map0;
+                const CUtensorMap *smap = m ? &smap1 : &smap0;
                 for (int kc = c0; kc < c1 && !*abort_flag; ++kc, ++c) {
                     if (c >= NW) dq_wait(&empty_w[rw.s], rw.ph ^ 1u, abort_flag, 8u);
                     if (*abort_flag) break;
                     DQ_TRACE(c, 0);
+                    uint8_t *dst = wst + (size_t)rw.s * WS;
                     mbar_arrive_expect_tx(&full_w[rw.s], WS);
                     // x coordinate in elements: 32-bit words (GF4) or bytes (Q8_0)
-                    const int xk = CODEC == QW35_GF4_TYPE ? kc * (KC / 8) : kc * KC;
-                    tma_load_2d(wst + (size_t)rw.s * WS, map, xk, tile * TM, &full_w[rw.s], pol);
+                    tma_load_2d(dst, map, Q8 ? kc * KC : kc * (KC / 8), tile * TM, &full_w[rw.s], pol);
+                    // Q8_0: the 8 block scales (16 B) of each row around this chunk's 4
+                    if constexpr (Q8) tma_load_2d(dst + G::WCODES, smap, (kc * 4) & ~7, tile * TM, &full_w[rw.s], pol);
                     rw.next(NW);
                 }
             })
@@ -396,11 +400,11 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
         // ------------------------------ MMA issuer -------------------------------
         if (lane == 0) {
             int c = 0, ul = 0;
-            Ring rx, ra, rb;  // activation stages, A tiles, Q8_0 block accumulators
+            Ring rx, ra;
             DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
                 if (!*abort_flag) {
                     const int ab = ul & 1;
-                    if (!BLOCKED && ul >= 2) {
+                    if (ul >= 2) {
                         dq_wait(&acc_empty[ab], ((ul >> 1) - 1) & 1, abort_flag, 16u);
                         tc_fence_after();
                     }
@@ -418,26 +422,15 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                         const uint64_t bd0 = smem_desc_sw128(smem_u32(xst + (size_t)sx * XS));
                         const uint32_t d0 = tmem + ab * RC;
                         const long long cyc0 = p.trace ? clock64() : 0;
-                        if constexpr (!BLOCKED) tc_mma_f16_ts(d0, a0, bd0, IDESC, kc > c0 ? 1u : 0u);
+                        tc_mma_f16_ts(d0, a0, bd0, IDESC, kc > c0 ? 1u : 0u);
+                        if constexpr (Q8) tc_mma_f16_ts_acc(d0, a0 + 64, bd0, IDESC_HI);
 #pragma unroll
-                        for (int j = BLOCKED ? 0 : 1; j < KC / 16; ++j) {
+                        for (int j = 1; j < KC / 16; ++j) {
                             // B: [k-atom of 64][2*NP rows][128 B swizzled]; k-step j = 16 columns
                             const uint64_t bd = bd0 + (uint64_t)((((j >> 2) * (2 * NP * 128)) + (j & 3) * 32) >> 4);
-                            const uint32_t ad = a0 + j * 8;  // 16 f16 of K = 8 TMEM columns
-                            if constexpr (!BLOCKED) {
-                                tc_mma_f16_ts_acc(d0, ad, bd, IDESC);
-                            } else {
-                                const int r = rb.s;
-                                if ((j & 1) == 0 && c * (KC / 32) + (j >> 1) >= R) {
-                                    dq_wait(&acc_empty[r], rb.ph ^ 1u, abort_flag, 16u);
-                                    tc_fence_after();
-                                }
-                                tc_mma_f16_ts(tmem + r * RC, ad, bd, IDESC, (j & 1) ? 1u : 0u);
-                                if (j & 1) {
-                                    tc_commit(&acc_full[r]);
-                                    rb.next(R);
-                                }
-                            }
+                            // A: 16 f16 of K = 8 TMEM columns (Q8_0: hi tile, lo tile 64 columns on)
+                            tc_mma_f16_ts_acc(d0, a0 + j * 8, bd, IDESC);
+                            if constexpr (Q8) tc_mma_f16_ts_acc(d0, a0 + 64 + j * 8, bd, IDESC_HI);
                         }
                         tc_commit(&free_a[sa]);
                         tc_commit(&free_x[sx]);
@@ -446,7 +439,7 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                         rx.next(SX);
                         ra.next(SA);
                     }
-                    if constexpr (!BLOCKED) tc_commit(&acc_full[ab]);
+                    tc_commit(&acc_full[ab]);
                     ++ul;
                 }
             })
@@ -454,9 +447,9 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
     } else if (warp < 3 + DEC) {
         // -------------------------------- decoders --------------------------------
         // thread = one weight row (its TMEM lane); group g of four warps decodes
-        // K columns [g*GK, g*GK + GK) of the chunk into 32 TMEM columns.  The
-        // weight stage is 128B-swizzled: 16-byte piece q of row r sits at
-        // q ^ (r % 8), so the eight rows of a quarter-warp hit distinct banks.
+        // K columns [g*GK, g*GK + GK) of the chunk.  The codes of a stage are
+        // 128B-swizzled: 16-byte piece q of row r sits at q ^ (r % 8), so the
+        // eight rows of a quarter-warp hit distinct banks.
         const int dw = warp - 3;
         const int grp = dw >> 2;
         const int quarter = warp & 3;  // TMEM lane quarter this warp may access
@@ -465,6 +458,12 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
         int c = 0;
         Ring rw, ra;
         DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
+            float e2 = 1.0f;  // Q8_0: 2^e of this row (exact f32 power of two)
+            if constexpr (Q8) {
+                const int row = tile * TM + r;
+                const int e = row < p.rows ? (int)p.rexp[m][row] : 0;
+                e2 = __int_as_float((e + 127) << 23);
+            }
             for (int kc = c0; kc < c1 && !*abort_flag; ++kc, ++c) {
                 const int sw = rw.s, sa = ra.s;
                 dq_wait(&full_w[sw], rw.ph, abort_flag, 32u);
@@ -473,29 +472,48 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                 if (*abort_flag) break;
                 tc_fence_after();
                 const uint8_t *row = wst + (size_t)sw * WS + r * 128;
-                uint32_t o[32];
-                if constexpr (CODEC == QW35_GF4_TYPE) {
+                const uint32_t tcol = tmem + lane_addr + T::A0 + sa * G::ACOLS + grp * 32;
+                if constexpr (!Q8) {
                     // 64 columns = 8 words = pieces 2g, 2g+1 of the row
                     const uint4 wa = *reinterpret_cast<const uint4 *>(row + (((2 * grp) ^ (r & 7)) << 4));
                     const uint4 wb = *reinterpret_cast<const uint4 *>(row + (((2 * grp + 1) ^ (r & 7)) << 4));
                     uint4 h[8];
                     gf4_quad_to_halves<EXACT>(wa, h[0], h[1], h[2], h[3]);
                     gf4_quad_to_halves<EXACT>(wb, h[4], h[5], h[6], h[7]);
+                    uint32_t o[32];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         o[4 * i] = h[i].x; o[4 * i + 1] = h[i].y; o[4 * i + 2] = h[i].z; o[4 * i + 3] = h[i].w;
                     }
+                    tmem_st32(tcol, o);
                 } else {
-                    // 64 columns = 64 codes = pieces 4g .. 4g+3 of the row
+                    // 64 codes = pieces 4g .. 4g+3 of the row, blocks 2g and 2g+1 of the
+                    // chunk.  Each weight q * d * 2^e becomes hi = half(q * ds) and
+                    // lo = q * ds - hi (exact: the residual has <= 8 significant bits),
+                    // with ds = half(d * 2^e) (exact unless d is ~2^-21 of the row max).
+                    const uint32_t d2 = *reinterpret_cast<const uint32_t *>(
+                        wst + (size_t)sw * WS + G::WCODES + r * 16 + (((kc & 1) * 4 + 2 * grp) << 1));
+                    const __half2 dh = *reinterpret_cast<const __half2 *>(&d2);
+                    const __half2 ds = __floats2half2_rn(__low2float(dh) * e2, __high2float(dh) * e2);
+                    uint32_t hi[32], lo[32];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const uint4 w4 = *reinterpret_cast<const uint4 *>(row + (((4 * grp + i) ^ (r & 7)) << 4));
-                        const uint4 h0 = q8_codes_to_halves(w4.x, w4.y), h1 = q8_codes_to_halves(w4.z, w4.w);
-                        o[8 * i] = h0.x; o[8 * i + 1] = h0.y; o[8 * i + 2] = h0.z; o[8 * i + 3] = h0.w;
-                        o[8 * i + 4] = h1.x; o[8 * i + 5] = h1.y; o[8 * i + 6] = h1.z; o[8 * i + 7] = h1.w;
+                        const __half2 s2 = __half2half2(i < 2 ? __low2half(ds) : __high2half(ds));
+                        const uint4 q0 = q8_codes_to_halves(w4.x, w4.y), q1 = q8_codes_to_halves(w4.z, w4.w);
+                        const uint32_t qs[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) {
+                            const __half2 q = *reinterpret_cast<const __half2 *>(&qs[t]);
+                            const __half2 h = __hmul2(q, s2);
+                            const __half2 l = __hfma2(q, s2, __hneg2(h));
+                            hi[8 * i + t] = *reinterpret_cast<const uint32_t *>(&h);
+                            lo[8 * i + t] = *reinterpret_cast<const uint32_t *>(&l);
+                        }
                     }
+                    tmem_st32(tcol, hi);
+                    tmem_st32(tcol + 64, lo);
                 }
-                tmem_st32(tmem + lane_addr + T::A0 + sa * G::ACOLS + grp * 32, o);
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
@@ -511,78 +529,48 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
         })
     } else {
         // -------------------------------- epilogue --------------------------------
-        // EPI/4 warps per TMEM lane quarter, each owning NP/(EPI/4) columns
+        // one warp per TMEM lane quarter: row quarter*32 + lane, all NP columns
         pdl_wait();  // rowscale / residual y come from earlier kernels
-        constexpr int NH = NP / (EPI / 4);
-        const int ew = warp - 3 - DEC;
         const int quarter = warp & 3;
-        const int n0 = (ew >> 2) * NH;
         const int row_in_tile = quarter * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+        const int ew = warp - 3 - DEC;
         int ul = 0;
-        Ring rb;
         DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
             if (!*abort_flag) {
                 const int row = tile * TM + row_in_tile;
-                float acc[NH];
+                const int ab = ul & 1;
+                dq_wait(&acc_full[ab], (ul >> 1) & 1, abort_flag, 64u);
+                tc_fence_after();
+                float es = 1.0f;  // Q8_0: 2^-e of the row
+                if constexpr (Q8) {
+                    const int e = row < p.rows ? (int)p.rexp[m][row] : 0;
+                    es = __int_as_float((127 - e) << 23);
+                }
+                float *y = p.y[MODE == DQ_DUAL ? m : 0];
+                // a segment short of the full K shares its outputs with another CTA
+                const bool atomic = MODE == DQ_ACCUM || c0 != 0 || c1 != nch;
 #pragma unroll
-                for (int n = 0; n < NH; ++n) acc[n] = 0.0f;
-                if constexpr (!BLOCKED) {
-                    const int ab = ul & 1;
-                    dq_wait(&acc_full[ab], (ul >> 1) & 1, abort_flag, 64u);
-                    tc_fence_after();
+                for (int n0 = 0; n0 < NP; n0 += 16) {
+                    float th[16], tl[16];
+                    tmem_ld16(tmem + lane_addr + ab * RC + n0, th);
+                    tmem_ld16(tmem + lane_addr + ab * RC + NP + n0, tl);
+                    if (row < p.rows && !*abort_flag) {
 #pragma unroll
-                    for (int part = 0; part < 2; ++part) {  // hi and lo activation products
-                        float tv[NH];
-                        tmem_ld_cols<NH>(tmem + lane_addr + ab * RC + part * NP + n0, tv);
-#pragma unroll
-                        for (int n = 0; n < NH; ++n) acc[n] += tv[n];
-                    }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&acc_empty[ab]);
-                } else {
-                    const uint16_t *scl = reinterpret_cast<const uint16_t *>(p.sc[m]) + (size_t)row * (p.K / 32);
-                    for (int kc = c0; kc < c1; ++kc) {
-                        uint2 dpk = make_uint2(0, 0);
-                        if (row < p.rows) dpk = *reinterpret_cast<const uint2 *>(scl + kc * 4);
-                        const uint32_t dwd[2] = {dpk.x, dpk.y};
-#pragma unroll
-                        for (int b4 = 0; b4 < 4; ++b4) {
-                            const int rg = rb.s;
-                            dq_wait(&acc_full[rg], rb.ph, abort_flag, 64u);
-                            tc_fence_after();
-                            float tv[NH], tl[NH];
-                            tmem_ld_cols<NH>(tmem + lane_addr + rg * RC + n0, tv);
-                            tmem_ld_cols<NH>(tmem + lane_addr + rg * RC + NP + n0, tl);
-#pragma unroll
-                            for (int n = 0; n < NH; ++n) tv[n] += tl[n];
-                            tc_fence_before();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&acc_empty[rg]);
-                            const float d = __half2float(
-                                __ushort_as_half((unsigned short)((dwd[b4 >> 1] >> (16 * (b4 & 1))) & 0xffffu)));
-#pragma unroll
-                            for (int n = 0; n < NH; ++n) acc[n] = fmaf(d, tv[n], acc[n]);
-                            rb.next(R);
+                        for (int n = 0; n < 16; ++n) {
+                            if (n0 + n < p.B) {
+                                const float v = (th[n] + tl[n]) * es * p.rowscale[n0 + n];
+                                float *dst = y + (size_t)(n0 + n) * p.rows + row;
+                                if (atomic) atomicAdd(dst, v);
+                                else *dst = v;
+                            }
                         }
                     }
                 }
-                if (row < p.rows && !*abort_flag) {
-                    float *y = p.y[MODE == DQ_DUAL ? m : 0];
-                    // a segment short of the full K shares its outputs with another CTA
-                    const bool atomic = MODE == DQ_ACCUM || c0 != 0 || c1 != nch;
-#pragma unroll
-                    for (int n = 0; n < NH; ++n) {
-                        if (n0 + n < p.B) {
-                            const float v = acc[n] * p.rowscale[n0 + n];
-                            float *dst = y + (size_t)(n0 + n) * p.rows + row;
-                            if (atomic) atomicAdd(dst, v);
-                            else *dst = v;
-                        }
-                    }
-                    if (lane == 0 && ew == 0) DQ_STAMP(3);
-                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[ab]);
+                if (lane == 0 && ew == 0) DQ_STAMP(3);
                 ++ul;
             }
         })
@@ -834,6 +822,33 @@ bool weight_map(uint32_t type_id, const void *w, uint32_t rows, uint32_t k, CUte
     return true;
 }
 
+// Tensor map over the Q8_0 scales plane ([rows][K/32] f16): boxes of 8 scales
+// (16 bytes, two chunks) x 128 rows.
+bool scale_map(const void *w, uint32_t rows, uint32_t k, CUtensorMap *out) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void *, uint32_t, uint32_t>, CUtensorMap> cache;
+    std::lock_guard<std::mutex> g(mu);
+    auto key = std::make_tuple(w, rows, k);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return true;
+    }
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    CUtensorMap m;
+    cuuint64_t dims[2] = {k / 32, rows}, strides[1] = {(cuuint64_t)(k / 32) * 2};
+    cuuint32_t box[2] = {8, TM}, estr[2] = {1, 1};
+    void *base = static_cast<uint8_t *>(const_cast<void *>(w)) + (size_t)rows * k;
+    if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+        return false;
+    cache[key] = m;
+    *out = m;
+    return true;
+}
+
 // Per-device scratch for the activation prep and the two-pass epilogues.
 // Grows only outside stream capture (the runtime reserves it up front).
 struct Scratch {
@@ -874,8 +889,9 @@ bool dq_supported(const MatvecArgs &a) {
     // TMA needs 16-byte aligned weights; the activation prep reads x and the
     // norm weight 16 bytes at a time
     auto a16 = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
+    // K % 256: GF4 chunks are 256 columns; Q8_0 scale boxes span two 128-column chunks
     return a.batch >= 16 && a.batch <= 64 && (a.type_id == QW35_GF4_TYPE || a.type_id == QW35_Q8_0_TYPE) &&
-           a.k % (a.type_id == QW35_GF4_TYPE ? DqGeo<QW35_GF4_TYPE>::KC : DqGeo<QW35_Q8_0_TYPE>::KC) == 0 &&
+           a.k % 256 == 0 &&
            a16(a.w0) && a16(a.w1) && a16(a.x) && a16(a.norm_w) && encode_fn() != nullptr &&
            !getenv("QW35_NO_TCGEN05");
 }
@@ -891,7 +907,8 @@ cudaError_t dq_reserve(int max_batch, uint32_t max_k, uint32_t max_rows_out) {
 }
 
 template <int CODEC, int NP, int MODE, bool EXACT>
-static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, DqParams p, cudaStream_t st) {
+static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, const CUtensorMap &s0,
+                             const CUtensorMap &s1, DqParams p, cudaStream_t st) {
     auto kern = dq_kernel<CODEC, NP, MODE, EXACT>;
     // SX activation stages (two when they are 64 KB), then as many weight stages as fit
     // <= 192 KB, so a 128-thread activation prep CTA fits beside it on the SM
@@ -901,11 +918,12 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, DqPar
     int NW = std::min(4, (int)((budget - SX * xs) / ws));
     static const int env_sx = getenv("QW35_DQ_SX") ? atoi(getenv("QW35_DQ_SX")) : 0;  // tuning experiments
     static const int env_nw = getenv("QW35_DQ_NW") ? atoi(getenv("QW35_DQ_NW")) : 0;
-    if (env_sx) SX = env_sx;
-    if (env_nw) NW = env_nw;
-    if (SX < 2 || NW < 2 || SX * xs + NW * ws > budget) return cudaErrorInvalidValue;
+    if (env_sx >= 2 && env_nw >= 2 && env_sx * xs + env_nw * ws <= budget) {
+        SX = env_sx;
+        NW = env_nw;
+    }
     using T = DqTmem<CODEC, NP>;
-    const size_t smem = 1024 + (size_t)SX * xs + (size_t)NW * ws + (2 * NW + 2 * SX + 2 * T::SA + 2 * T::R + 1) * 8 + 16;
+    const size_t smem = 1024 + (size_t)SX * xs + (size_t)NW * ws + (2 * NW + 2 * SX + 2 * T::SA + 4 + 1) * 8 + 16;
     static bool attr = false;
     if (!attr) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -930,7 +948,7 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, DqPar
     attrs[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = getenv("QW35_NO_PDL") ? 0 : 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m0, m1, p, SX, NW);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m0, m1, s0, s1, p, SX, NW);
     if (p.trace) {
         unsigned long long h[256 * 10];
         cudaMemcpy(h, trace, sizeof(h), cudaMemcpyDeviceToHost);
@@ -954,15 +972,16 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, DqPar
 
 template <int CODEC, int NP>
 static cudaError_t dq_dispatch_mode(int mode, bool exact, const CUtensorMap &m0, const CUtensorMap &m1,
-                                    const DqParams &p, cudaStream_t st) {
+                                    const CUtensorMap &s0, const CUtensorMap &s1, const DqParams &p,
+                                    cudaStream_t st) {
     if (CODEC == QW35_GF4_TYPE && !exact) {
-        if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, false>(m0, m1, p, st);
-        if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, false>(m0, m1, p, st);
-        return dq_launch<CODEC, NP, DQ_DUAL, false>(m0, m1, p, st);
+        if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, false>(m0, m1, s0, s1, p, st);
+        if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, false>(m0, m1, s0, s1, p, st);
+        return dq_launch<CODEC, NP, DQ_DUAL, false>(m0, m1, s0, s1, p, st);
     }
-    if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, true>(m0, m1, p, st);
-    if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, true>(m0, m1, p, st);
-    return dq_launch<CODEC, NP, DQ_DUAL, true>(m0, m1, p, st);
+    if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, true>(m0, m1, s0, s1, p, st);
+    if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, true>(m0, m1, s0, s1, p, st);
+    return dq_launch<CODEC, NP, DQ_DUAL, true>(m0, m1, s0, s1, p, st);
 }
 
 // mode: 0 store, 1 accumulate, 2 swiglu pair, 3 logits for the argmax head
@@ -974,6 +993,12 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
     if (!weight_map(a.type_id, a.w0, a.rows, a.k, &m0)) return cudaErrorInvalidValue;
     if (dual && !weight_map(a.type_id, a.w1, a.rows, a.k, &m1)) return cudaErrorInvalidValue;
     if (!dual) m1 = m0;
+    CUtensorMap s0 = m0, s1 = m1;  // scales maps (Q8_0 only; unused otherwise)
+    if (a.type_id == QW35_Q8_0_TYPE) {
+        if (!scale_map(a.w0, a.rows, a.k, &s0)) return cudaErrorInvalidValue;
+        if (dual && !scale_map(a.w1, a.rows, a.k, &s1)) return cudaErrorInvalidValue;
+        if (!dual) s1 = s0;
+    }
     // scratch: activation tiles (hi and lo rows), rowscale, then (swiglu) gate|up or (head) logits
     const size_t xbytes = (size_t)NP * K * 2;
     const size_t extra = (mode == 2) ? (size_t)2 * B * rows * 4 : (mode == 3 && !a.y) ? (size_t)B * rows * 4 : 0;
@@ -1006,8 +1031,10 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
     p.y[0] = y0;
     p.y[1] = y1;
     if (a.type_id == QW35_Q8_0_TYPE) {
-        p.sc[0] = static_cast<const uint8_t *>(a.w0) + (size_t)rows * K;
-        p.sc[1] = dual ? static_cast<const uint8_t *>(a.w1) + (size_t)rows * K : p.sc[0];
+        // row exponent plane: after the codes (rows * K) and scales (rows * K / 16) planes
+        const size_t off = (size_t)rows * (K / 32) * 34;
+        p.rexp[0] = reinterpret_cast<const int8_t *>(static_cast<const uint8_t *>(a.w0) + off);
+        p.rexp[1] = dual ? reinterpret_cast<const int8_t *>(static_cast<const uint8_t *>(a.w1) + off) : p.rexp[0];
     }
     // prep (+ zeroing of split-K outputs)
     const bool zero = dmode != DQ_ACCUM && gran < nch;
@@ -1035,13 +1062,13 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
     if (e != cudaSuccess) return e;
     const bool exact = (a.flags & QW35_MV_GF4_EXACT) != 0;
     if (a.type_id == QW35_GF4_TYPE) {
-        if (NP == 16) e = dq_dispatch_mode<QW35_GF4_TYPE, 16>(dmode, exact, m0, m1, p, st);
-        else if (NP == 32) e = dq_dispatch_mode<QW35_GF4_TYPE, 32>(dmode, exact, m0, m1, p, st);
-        else e = dq_dispatch_mode<QW35_GF4_TYPE, 64>(dmode, exact, m0, m1, p, st);
+        if (NP == 16) e = dq_dispatch_mode<QW35_GF4_TYPE, 16>(dmode, exact, m0, m1, s0, s1, p, st);
+        else if (NP == 32) e = dq_dispatch_mode<QW35_GF4_TYPE, 32>(dmode, exact, m0, m1, s0, s1, p, st);
+        else e = dq_dispatch_mode<QW35_GF4_TYPE, 64>(dmode, exact, m0, m1, s0, s1, p, st);
     } else {
-        if (NP == 16) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 16>(dmode, true, m0, m1, p, st);
-        else if (NP == 32) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 32>(dmode, true, m0, m1, p, st);
-        else e = dq_dispatch_mode<QW35_Q8_0_TYPE, 64>(dmode, true, m0, m1, p, st);
+        if (NP == 16) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 16>(dmode, true, m0, m1, s0, s1, p, st);
+        else if (NP == 32) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 32>(dmode, true, m0, m1, s0, s1, p, st);
+        else e = dq_dispatch_mode<QW35_Q8_0_TYPE, 64>(dmode, true, m0, m1, s0, s1, p, st);
     }
     if (e != cudaSuccess) return e;
     if (mode == 2) {

@@ -67,6 +67,13 @@ uint64_t qw35_cuda_weight_bytes(uint32_t type_id, uint32_t rows, uint32_t k) {
     }
 }
 
+uint64_t qw35_cuda_device_bytes(uint32_t type_id, uint32_t rows, uint32_t k) {
+    const uint64_t raw = qw35_cuda_weight_bytes(type_id, rows, k);
+    // Q8_0 carries one exponent byte per row after its scales plane (16-byte padded)
+    if (type_id == QW35_Q8_0_TYPE && raw) return raw + (((uint64_t)rows + 15) & ~(uint64_t)15);
+    return raw;
+}
+
 int qw35_cuda_weight_repack(uint32_t type_id, const void *src, void *dst, uint32_t rows, uint32_t k, void *stream,
                             char *err, uintptr_t err_len) {
     if (!check_shape(type_id, rows, k, 1, err, err_len)) return 0;

@@ -118,8 +118,9 @@ struct Loader {
             off += t.d->bytes;
         }
         DevTensor dt;
-        dt.type_id = type; dt.rows = (uint32_t)rows; dt.k = (uint32_t)k; dt.bytes = bytes;
-        dt.ptr = dalloc(bytes);
+        dt.type_id = type; dt.rows = (uint32_t)rows; dt.k = (uint32_t)k;
+        dt.bytes = qw35_cuda_device_bytes(type, dt.rows, dt.k);
+        dt.ptr = dalloc(dt.bytes);
         ck(weight_repack(type, st, dt.ptr, dt.rows, dt.k, 0), "repack");
         ck(cudaDeviceSynchronize(), "repack sync");
         return dt;

@@ -29,12 +29,18 @@ def _dev(t):
 
 
 def weight_bytes(type_id: int, rows: int, k: int) -> int:
+    """GGUF-layout bytes of a rows x k matrix."""
     return int(lib().qw35_cuda_weight_bytes(type_id, rows, k))
+
+
+def device_bytes(type_id: int, rows: int, k: int) -> int:
+    """Device-layout bytes (Q8_0 adds a per-row exponent plane)."""
+    return int(lib().qw35_cuda_device_bytes(type_id, rows, k))
 
 
 def repack(type_id: int, raw: torch.Tensor, rows: int, k: int) -> torch.Tensor:
     """GGUF-layout bytes (device uint8) -> device layout."""
-    out = torch.empty(weight_bytes(type_id, rows, k), dtype=torch.uint8, device=raw.device)
+    out = torch.empty(device_bytes(type_id, rows, k), dtype=torch.uint8, device=raw.device)
     call("qw35_cuda_weight_repack", type_id, _p(_dev(raw)), _p(out), rows, k, _stream())
     return out
 

@@ -62,6 +62,15 @@ def test_weight_bytes_match_gguf_block_sizes():
     assert L.qw35_cuda_weight_bytes(99, 1, 256) == 0
 
 
+def test_device_bytes_add_the_q8_0_row_exponent_plane():
+    L = lib()
+    assert L.qw35_cuda_device_bytes(100, 12288, 4096) == L.qw35_cuda_weight_bytes(100, 12288, 4096)
+    assert L.qw35_cuda_device_bytes(12, 12288, 4096) == L.qw35_cuda_weight_bytes(12, 12288, 4096)
+    assert L.qw35_cuda_device_bytes(8, 12288, 4096) == 53477376 + 12288
+    assert L.qw35_cuda_device_bytes(8, 333, 1280) == 333 * 40 * 34 + 336
+    assert L.qw35_cuda_device_bytes(99, 1, 256) == 0
+
+
 def test_invalid_handles_and_error_buffers():
     L = lib()
     e = C.create_string_buffer(256)
