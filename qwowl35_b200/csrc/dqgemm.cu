@@ -76,6 +76,7 @@ struct DqParams {
     float *y[2];
     int rows, K, B, tiles;
     int gran, granules;     // schedule: granules of `gran` k-chunks spread over the grid
+    int red_tma;            // split tiles add into y by TMA bulk reduction (else per-element atomics)
     unsigned long long *trace;  // debug: per-chunk event stamps of CTA 0 (QW35_DQ_TRACE), or null
 };
 // trace layout: [chunk][10] = weight issue, decoder sees full_w, decoder done,
@@ -84,7 +85,8 @@ struct DqParams {
 #define DQ_TRACE(c, slot) \
     do { if (p.trace && blockIdx.x == 0 && (c) < 255) p.trace[(c) * 10 + (slot)] = globaltimer(); } while (0)
 // kernel-level stamps live in row 255: 0 entry, 1 setup done, 2 activations
-// released (PDL), 3 last epilogue write, 4 max exit over CTAs, 5 ~min entry over CTAs
+// released (PDL), 3 last epilogue write, 4 max exit over CTAs, 5 ~min entry over
+// CTAs, 6 last accumulator ready, 7 index of the last segment
 #define DQ_STAMP(slot) \
     do { if (p.trace && blockIdx.x == 0) p.trace[255 * 10 + (slot)] = globaltimer(); } while (0)
 #define DQ_TRACE_MAX(c, slot) \
@@ -284,7 +286,8 @@ struct Ring {
 template <int CODEC, int NP, int MODE, bool EXACT>
 __global__ void __launch_bounds__(DqGeo<CODEC>::THREADS, 1)
 dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1,
-          const __grid_constant__ CUtensorMap smap0, const __grid_constant__ CUtensorMap smap1, DqParams p, int SX,
+          const __grid_constant__ CUtensorMap smap0, const __grid_constant__ CUtensorMap smap1,
+          const __grid_constant__ CUtensorMap ymap0, const __grid_constant__ CUtensorMap ymap1, DqParams p, int SX,
           int NW) {
     using G = DqGeo<CODEC>;
     using T = DqTmem<CODEC, NP>;
@@ -301,7 +304,8 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
     // 1024-byte aligned base (128B-swizzle atoms need it)
     uint8_t *xst = smem + ((1024u - (smem_u32(smem) & 1023u)) & 1023u);  // [SX][XS]
     uint8_t *wst = xst + (size_t)SX * XS;                                  // [NW][WS]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(wst + (size_t)NW * WS);
+    float *stg = reinterpret_cast<float *>(wst + (size_t)NW * WS);       // [2][16][128] epilogue staging
+    uint64_t *bars = reinterpret_cast<uint64_t *>(stg + 2 * 16 * TM);
     uint64_t *full_w = bars;         // [NW] weight chunk landed (tx)
     uint64_t *empty_w = full_w + NW; // [NW] decoders done with the raw weights
     uint64_t *full_x = empty_w + NW; // [SX] activation chunk landed (tx)
@@ -398,30 +402,32 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
         }
     } else if (warp == 1) {
         // ------------------------------ MMA issuer -------------------------------
-        if (lane == 0) {
-            int c = 0, ul = 0;
-            Ring rx, ra;
-            DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
-                if (!*abort_flag) {
-                    const int ab = ul & 1;
-                    if (ul >= 2) {
-                        dq_wait(&acc_empty[ab], ((ul >> 1) - 1) & 1, abort_flag, 16u);
-                        tc_fence_after();
-                    }
-                    for (int kc = c0; kc < c1; ++kc, ++c) {
-                        const int sx = rx.s, sa = ra.s;
-                        dq_wait(&full_x[sx], rx.ph, abort_flag, 16u);
-                        DQ_TRACE(c, 6);
-                        dq_wait(&full_a[sa], ra.ph, abort_flag, 16u);
-                        if (*abort_flag) break;
-                        DQ_TRACE(c, 3);
-                        tc_fence_after();
-                        const uint32_t a0 = tmem + T::A0 + sa * G::ACOLS;
-                        // descriptor of k-step 0; later k-steps add a compile-time offset
-                        // (start address field, 16-byte units; smem addresses stay < 2^18)
-                        const uint64_t bd0 = smem_desc_sw128(smem_u32(xst + (size_t)sx * XS));
-                        const uint32_t d0 = tmem + ab * RC;
-                        const long long cyc0 = p.trace ? clock64() : 0;
+        // The whole warp runs the loop (its values stay warp-uniform, in uniform
+        // registers); one elected lane issues the MMAs and commits.
+        int c = 0, ul = 0;
+        Ring rx, ra;
+        DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
+            if (!*abort_flag) {
+                const int ab = ul & 1;
+                if (ul >= 2) {
+                    dq_wait(&acc_empty[ab], ((ul >> 1) - 1) & 1, abort_flag, 16u);
+                    tc_fence_after();
+                }
+                for (int kc = c0; kc < c1; ++kc, ++c) {
+                    const int sx = rx.s, sa = ra.s;
+                    dq_wait(&full_x[sx], rx.ph, abort_flag, 16u);
+                    if (lane == 0) DQ_TRACE(c, 6);
+                    dq_wait(&full_a[sa], ra.ph, abort_flag, 16u);
+                    if (*abort_flag) break;
+                    if (lane == 0) DQ_TRACE(c, 3);
+                    tc_fence_after();
+                    const uint32_t a0 = tmem + T::A0 + sa * G::ACOLS;
+                    // descriptor of k-step 0; later k-steps add a compile-time offset
+                    // (start address field, 16-byte units; smem addresses stay < 2^18)
+                    const uint64_t bd0 = smem_desc_sw128(smem_u32(xst + (size_t)sx * XS));
+                    const uint32_t d0 = tmem + ab * RC;
+                    const long long cyc0 = p.trace ? clock64() : 0;
+                    if (elect_one()) {
                         tc_mma_f16_ts(d0, a0, bd0, IDESC, kc > c0 ? 1u : 0u);
                         if constexpr (Q8) tc_mma_f16_ts_acc(d0, a0 + 64, bd0, IDESC_HI);
 #pragma unroll
@@ -434,16 +440,17 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                         }
                         tc_commit(&free_a[sa]);
                         tc_commit(&free_x[sx]);
-                        if (p.trace && blockIdx.x == 0 && c < 255) p.trace[c * 10 + 8] = clock64() - cyc0;
-                        DQ_TRACE(c, 4);
-                        rx.next(SX);
-                        ra.next(SA);
+                        if (kc + 1 == c1) tc_commit(&acc_full[ab]);
                     }
-                    tc_commit(&acc_full[ab]);
-                    ++ul;
+                    __syncwarp();
+                    if (lane == 0 && p.trace && blockIdx.x == 0 && c < 255) p.trace[c * 10 + 8] = clock64() - cyc0;
+                    if (lane == 0) DQ_TRACE(c, 4);
+                    rx.next(SX);
+                    ra.next(SA);
                 }
-            })
-        }
+                ++ul;
+            }
+        })
     } else if (warp < 3 + DEC) {
         // -------------------------------- decoders --------------------------------
         // thread = one weight row (its TMEM lane); group g of four warps decodes
@@ -535,12 +542,16 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
         const int row_in_tile = quarter * 32 + lane;
         const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
         const int ew = warp - 3 - DEC;
-        int ul = 0;
+        // batch-row scales, lane n holding column n (and 32 + n): broadcast by shuffles
+        const float rs0 = lane < p.B ? p.rowscale[lane] : 0.0f;
+        const float rs1 = (NP > 32 && 32 + lane < p.B) ? p.rowscale[32 + lane] : 0.0f;
+        int ul = 0, sg = 0;
         DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
             if (!*abort_flag) {
                 const int row = tile * TM + row_in_tile;
                 const int ab = ul & 1;
                 dq_wait(&acc_full[ab], (ul >> 1) & 1, abort_flag, 64u);
+                if (lane == 0 && ew == 0) DQ_STAMP(6);
                 tc_fence_after();
                 float es = 1.0f;  // Q8_0: 2^-e of the row
                 if constexpr (Q8) {
@@ -548,32 +559,61 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                     es = __int_as_float((127 - e) << 23);
                 }
                 float *y = p.y[MODE == DQ_DUAL ? m : 0];
-                // a segment short of the full K shares its outputs with another CTA
-                const bool atomic = MODE == DQ_ACCUM || c0 != 0 || c1 != nch;
+                // Split tiles (stream-K: several CTAs per tile, and accumulate mode)
+                // add into y: by TMA bulk reduction of 16-column boxes staged in
+                // shared memory (the adds run in L2), else by per-element atomics.
+                // Whole-tile schedules (gran == nch) store.
+                const bool split = MODE == DQ_ACCUM || p.gran < nch;
+                const CUtensorMap *ymap = (MODE == DQ_DUAL && m) ? &ymap1 : &ymap0;
 #pragma unroll
                 for (int n0 = 0; n0 < NP; n0 += 16) {
-                    float th[16], tl[16];
-                    tmem_ld16(tmem + lane_addr + ab * RC + n0, th);
-                    tmem_ld16(tmem + lane_addr + ab * RC + NP + n0, tl);
-                    if (row < p.rows && !*abort_flag) {
+                    uint32_t th[16], tl[16];
+                    tmem_ld16_async(tmem + lane_addr + ab * RC + n0, th);
+                    tmem_ld16_async(tmem + lane_addr + ab * RC + NP + n0, tl);
+                    tmem_ld_wait();
+                    if (n0 + 16 >= NP) {  // accumulator read out: the MMA may reuse it
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[ab]);
+                    }
+                    float v[16];
+#pragma unroll
+                    for (int n = 0; n < 16; ++n) {
+                        const float rs = __shfl_sync(0xffffffffu, n0 + n < 32 ? rs0 : rs1, (n0 + n) & 31);
+                        v[n] = (__uint_as_float(th[n]) + __uint_as_float(tl[n])) * es * rs;
+                    }
+                    if (split && p.red_tma) {
+                        float *buf = stg + (sg & 1) * (16 * TM);
+                        // the reduction issued two boxes ago must have read this buffer
+                        if (ew == 0 && lane == 0) bulk_wait_read<1>();
+                        named_sync(1, EPI * 32);
+#pragma unroll
+                        for (int n = 0; n < 16; ++n) buf[n * TM + row_in_tile] = v[n];  // [column][row]
+                        fence_async_smem();
+                        named_sync(1, EPI * 32);
+                        if (ew == 0 && lane == 0 && !*abort_flag) {
+                            // rows >= p.rows and columns >= B fall outside the map: not written
+                            tma_reduce_add_2d(ymap, tile * TM, n0, buf);
+                            bulk_commit();
+                        }
+                        ++sg;
+                    } else if (row < p.rows && !*abort_flag) {
 #pragma unroll
                         for (int n = 0; n < 16; ++n) {
                             if (n0 + n < p.B) {
-                                const float v = (th[n] + tl[n]) * es * p.rowscale[n0 + n];
                                 float *dst = y + (size_t)(n0 + n) * p.rows + row;
-                                if (atomic) atomicAdd(dst, v);
-                                else *dst = v;
+                                if (split) atomicAdd(dst, v[n]);
+                                else *dst = v[n];
                             }
                         }
                     }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[ab]);
                 if (lane == 0 && ew == 0) DQ_STAMP(3);
+                if (lane == 0 && ew == 0 && p.trace && blockIdx.x == 0) p.trace[255 * 10 + 7] = ul;
                 ++ul;
             }
         })
+        if (ew == 0 && lane == 0) bulk_wait_all();  // our reductions are complete before exit
     }
 
     // No programmatic launch trigger in this kernel: the next one (normally the
@@ -582,10 +622,15 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
     // warps (a trigger from any thread counts for the whole CTA, and the idle
     // lanes of the role warps would reach it at once).
     // ---- teardown: nothing of ours may be in flight when TMEM is released ----
-    if (threadIdx.x == 32 && *abort_flag) {
-        // the MMA issuer drains its own tensor-core work (bounded) before TMEM goes
-        tc_commit(drain);
-        mbar_wait(drain, 0, 128u);
+    if (warp == 1 && *abort_flag) {
+        // the MMA issuer (the elected lane, as in the issue loop) drains its own
+        // tensor-core work (bounded) before TMEM goes
+        __syncwarp();
+        if (elect_one()) {
+            tc_commit(drain);
+            mbar_wait(drain, 0, 128u);
+        }
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
@@ -596,8 +641,8 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
 
 // ---------------------------------------------------------------------------
 // activation prep: RMS norm (optional), per-row power-of-two scale, f32 ->
-// hi + lo halves in the MMA's K-major core-matrix layout (one CTA per padded
-// batch row); zeroes the outputs that split-K accumulates into.
+// hi + lo halves in the MMA's K-major swizzled layout (one CTA per padded
+// batch row); zeroes the outputs that split tiles add into.
 // ---------------------------------------------------------------------------
 template <typename XT>
 __device__ __forceinline__ void load8(const XT *p, float *v) {
@@ -716,9 +761,18 @@ __global__ void __launch_bounds__(128) dq_prep_kernel(const XT *x, const float *
     }
     if (n < B && (zero0 || zero1)) {
         __syncthreads();  // every read of x row n is done (y may alias x)
-        for (int r = threadIdx.x; r < zero_rows; r += 128) {
-            if (zero0) zero0[(size_t)n * zero_rows + r] = 0.0f;
-            if (zero1) zero1[(size_t)n * zero_rows + r] = 0.0f;
+        for (int z = 0; z < 2; ++z) {
+            float *zp = z ? zero1 : zero0;
+            if (!zp) continue;
+            float *row = zp + (size_t)n * zero_rows;
+            // 16-byte stores over the aligned middle of the row, scalars at its ends
+            const int head = (int)(((16u - ((uintptr_t)row & 15u)) & 15u) >> 2);
+            const int h = head < zero_rows ? head : zero_rows;
+            if (threadIdx.x < h) row[threadIdx.x] = 0.0f;
+            const int nv = (zero_rows - h) >> 2;
+            float4 *v = reinterpret_cast<float4 *>(row + h);
+            for (int i = threadIdx.x; i < nv; i += 128) v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = h + 4 * nv + threadIdx.x; r < zero_rows; r += 128) row[r] = 0.0f;
         }
     }
 }
@@ -849,6 +903,18 @@ bool scale_map(const void *w, uint32_t rows, uint32_t k, CUtensorMap *out) {
     return true;
 }
 
+// Tensor map over an output y [B][rows] f32 (x = row, y = batch column): boxes
+// of 128 rows x 16 columns for the epilogue's bulk reductions.
+bool out_map(const void *y, uint32_t rows, uint32_t B, CUtensorMap *out) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {rows, B}, strides[1] = {(cuuint64_t)rows * 4};
+    cuuint32_t box[2] = {TM, 16}, estr[2] = {1, 1};
+    return fn(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(y), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Per-device scratch for the activation prep and the two-pass epilogues.
 // Grows only outside stream capture (the runtime reserves it up front).
 struct Scratch {
@@ -896,9 +962,24 @@ bool dq_supported(const MatvecArgs &a) {
            !getenv("QW35_NO_TCGEN05");
 }
 
-size_t dq_scratch_bytes(int B, uint32_t k, uint32_t rows_out) {
+// Scratch layout of one batched matvec: activation tiles (hi | lo rows), row
+// scales, gate|up or logits outputs (modes 2 / 3).
+struct DqScratch {
+    size_t x, rowscale, ext, total;
+};
+static DqScratch dq_scratch_layout(int B, uint32_t k, uint32_t rows_out, size_t ext_bytes) {
     const int NP = dq_np(B);
-    return (size_t)2 * NP * k * 2 + 256 + (size_t)2 * B * rows_out * 4 + 256;
+    auto up = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    DqScratch l{};
+    l.x = 0;
+    l.rowscale = up((size_t)2 * NP * k * 2);
+    l.ext = l.rowscale + 256;
+    l.total = up(l.ext + ext_bytes);
+    return l;
+}
+
+size_t dq_scratch_bytes(int B, uint32_t k, uint32_t rows_out) {
+    return dq_scratch_layout(B, k, rows_out, (size_t)2 * B * rows_out * 4).total;
 }
 
 cudaError_t dq_reserve(int max_batch, uint32_t max_k, uint32_t max_rows_out) {
@@ -908,11 +989,13 @@ cudaError_t dq_reserve(int max_batch, uint32_t max_k, uint32_t max_rows_out) {
 
 template <int CODEC, int NP, int MODE, bool EXACT>
 static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, const CUtensorMap &s0,
-                             const CUtensorMap &s1, DqParams p, cudaStream_t st) {
+                             const CUtensorMap &s1, const CUtensorMap &y0, const CUtensorMap &y1, DqParams p,
+                             cudaStream_t st) {
     auto kern = dq_kernel<CODEC, NP, MODE, EXACT>;
     // SX activation stages (two when they are 64 KB), then as many weight stages as fit
-    // <= 192 KB, so a 128-thread activation prep CTA fits beside it on the SM
-    constexpr uint32_t budget = 192u * 1024u;
+    // stages <= 176 KB (+ 16 KB epilogue staging), so a 128-thread activation
+    // prep CTA fits beside it on the SM
+    constexpr uint32_t budget = 176u * 1024u;
     constexpr uint32_t xs = dq_xstage<CODEC, NP>(), ws = DqGeo<CODEC>::WS;
     int SX = xs >= 65536u ? 2 : 3;
     int NW = std::min(4, (int)((budget - SX * xs) / ws));
@@ -923,7 +1006,8 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, const
         NW = env_nw;
     }
     using T = DqTmem<CODEC, NP>;
-    const size_t smem = 1024 + (size_t)SX * xs + (size_t)NW * ws + (2 * NW + 2 * SX + 2 * T::SA + 4 + 1) * 8 + 16;
+    const size_t smem = 1024 + (size_t)SX * xs + (size_t)NW * ws + 2 * 16 * TM * 4 +
+                        (2 * NW + 2 * SX + 2 * T::SA + 4 + 1) * 8 + 16;
     static bool attr = false;
     if (!attr) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -948,7 +1032,7 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, const
     attrs[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = getenv("QW35_NO_PDL") ? 0 : 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m0, m1, s0, s1, p, SX, NW);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m0, m1, s0, s1, y0, y1, p, SX, NW);
     if (p.trace) {
         unsigned long long h[256 * 10];
         cudaMemcpy(h, trace, sizeof(h), cudaMemcpyDeviceToHost);
@@ -956,8 +1040,9 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, const
         const unsigned long long *k = h + 255 * 10;
         auto rel = [&](unsigned long long v) { return v ? (long long)(v - k[0]) : -1ll; };
         fprintf(stderr, "dq kernel: first CTA entry %lld, CTA0 setup %lld, act released %lld, first W issue %lld, "
-                        "CTA0 last epilogue %lld, last CTA exit %lld (ns from CTA0 entry)\n",
-                rel(~k[5]), rel(k[1]), rel(k[2]), rel(t0), rel(k[3]), rel(k[4]));
+                        "CTA0 last acc ready %lld, last epilogue done %lld (segment %llu), last CTA exit %lld "
+                        "(ns from CTA0 entry)\n",
+                rel(~k[5]), rel(k[1]), rel(k[2]), rel(t0), rel(k[6]), rel(k[3]), k[7], rel(k[4]));
         fprintf(stderr, "dq trace granules=%d gran=%d grid=%d SX=%d SA=%d NW=%d (ns from first issue)\n", p.granules,
                 p.gran, grid, SX, T::SA, NW);
         for (int c = 0; c < 255 && h[c * 10]; ++c) {
@@ -972,16 +1057,16 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, const
 
 template <int CODEC, int NP>
 static cudaError_t dq_dispatch_mode(int mode, bool exact, const CUtensorMap &m0, const CUtensorMap &m1,
-                                    const CUtensorMap &s0, const CUtensorMap &s1, const DqParams &p,
-                                    cudaStream_t st) {
+                                    const CUtensorMap &s0, const CUtensorMap &s1, const CUtensorMap &y0,
+                                    const CUtensorMap &y1, const DqParams &p, cudaStream_t st) {
     if (CODEC == QW35_GF4_TYPE && !exact) {
-        if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, false>(m0, m1, s0, s1, p, st);
-        if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, false>(m0, m1, s0, s1, p, st);
-        return dq_launch<CODEC, NP, DQ_DUAL, false>(m0, m1, s0, s1, p, st);
+        if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, false>(m0, m1, s0, s1, y0, y1, p, st);
+        if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, false>(m0, m1, s0, s1, y0, y1, p, st);
+        return dq_launch<CODEC, NP, DQ_DUAL, false>(m0, m1, s0, s1, y0, y1, p, st);
     }
-    if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, true>(m0, m1, s0, s1, p, st);
-    if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, true>(m0, m1, s0, s1, p, st);
-    return dq_launch<CODEC, NP, DQ_DUAL, true>(m0, m1, s0, s1, p, st);
+    if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, true>(m0, m1, s0, s1, y0, y1, p, st);
+    if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, true>(m0, m1, s0, s1, y0, y1, p, st);
+    return dq_launch<CODEC, NP, DQ_DUAL, true>(m0, m1, s0, s1, y0, y1, p, st);
 }
 
 // mode: 0 store, 1 accumulate, 2 swiglu pair, 3 logits for the argmax head
@@ -999,16 +1084,15 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
         if (dual && !scale_map(a.w1, a.rows, a.k, &s1)) return cudaErrorInvalidValue;
         if (!dual) s1 = s0;
     }
-    // scratch: activation tiles (hi and lo rows), rowscale, then (swiglu) gate|up or (head) logits
-    const size_t xbytes = (size_t)NP * K * 2;
     const size_t extra = (mode == 2) ? (size_t)2 * B * rows * 4 : (mode == 3 && !a.y) ? (size_t)B * rows * 4 : 0;
+    const DqScratch lay = dq_scratch_layout(B, a.k, a.rows, extra);
     void *scr = nullptr;
-    cudaError_t e = scratch_get(2 * xbytes + 256 + extra + 256, &scr, st);
+    cudaError_t e = scratch_get(lay.total, &scr, st);
     if (e != cudaSuccess) return e;
     uint8_t *base = static_cast<uint8_t *>(scr);
-    __half *xh = reinterpret_cast<__half *>(base);
-    float *rowscale = reinterpret_cast<float *>(base + 2 * xbytes);
-    float *ext = reinterpret_cast<float *>(base + 2 * xbytes + 256);
+    __half *xh = reinterpret_cast<__half *>(base + lay.x);
+    float *rowscale = reinterpret_cast<float *>(base + lay.rowscale);
+    float *ext = reinterpret_cast<float *>(base + lay.ext);
 
     const int tiles = (rows + TM - 1) / TM;
     const int nch = K / (a.type_id == QW35_GF4_TYPE ? DqGeo<QW35_GF4_TYPE>::KC : DqGeo<QW35_Q8_0_TYPE>::KC);
@@ -1036,8 +1120,13 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
         p.rexp[0] = reinterpret_cast<const int8_t *>(static_cast<const uint8_t *>(a.w0) + off);
         p.rexp[1] = dual ? reinterpret_cast<const int8_t *>(static_cast<const uint8_t *>(a.w1) + off) : p.rexp[0];
     }
-    // prep (+ zeroing of split-K outputs)
+    // outputs that split tiles add into start at zero
     const bool zero = dmode != DQ_ACCUM && gran < nch;
+    // TMA bulk reductions need 16-byte aligned outputs with 16-byte row strides
+    CUtensorMap y0m = m0, y1m = m0;
+    p.red_tma = (rows % 4 == 0) && ((uintptr_t)y0 & 15u) == 0 && (!dual || ((uintptr_t)y1 & 15u) == 0) &&
+                out_map(y0, rows, B, &y0m) && (!dual || out_map(y1, rows, B, &y1m));
+    if (!dual) y1m = y0m;
     const bool gperm = a.type_id == QW35_GF4_TYPE;
     {
         cudaLaunchConfig_t cfg{};
@@ -1049,26 +1138,25 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
         at[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = at;
         cfg.numAttrs = getenv("QW35_NO_PDL") ? 0 : 1;
-        float *z0 = zero ? y0 : nullptr, *z1 = zero ? y1 : nullptr;
         if (a.x_dtype == QW35_F16_TYPE)
             e = cudaLaunchKernelEx(&cfg, dq_prep_kernel<__half>, static_cast<const __half *>(a.x), a.norm_w, a.eps, K,
-                                   B, NP, (int)gperm, xh, rowscale, z0, z1, (int)rows);
+                                   B, NP, (int)gperm, xh, rowscale, zero ? y0 : nullptr, zero ? y1 : nullptr, rows);
         else
             e = cudaLaunchKernelEx(&cfg, dq_prep_kernel<float>, static_cast<const float *>(a.x), a.norm_w, a.eps, K, B,
-                                   NP, (int)gperm, xh, rowscale, z0, z1, (int)rows);
+                                   NP, (int)gperm, xh, rowscale, zero ? y0 : nullptr, zero ? y1 : nullptr, rows);
         if (e != cudaSuccess) return e;
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const bool exact = (a.flags & QW35_MV_GF4_EXACT) != 0;
     if (a.type_id == QW35_GF4_TYPE) {
-        if (NP == 16) e = dq_dispatch_mode<QW35_GF4_TYPE, 16>(dmode, exact, m0, m1, s0, s1, p, st);
-        else if (NP == 32) e = dq_dispatch_mode<QW35_GF4_TYPE, 32>(dmode, exact, m0, m1, s0, s1, p, st);
-        else e = dq_dispatch_mode<QW35_GF4_TYPE, 64>(dmode, exact, m0, m1, s0, s1, p, st);
+        if (NP == 16) e = dq_dispatch_mode<QW35_GF4_TYPE, 16>(dmode, exact, m0, m1, s0, s1, y0m, y1m, p, st);
+        else if (NP == 32) e = dq_dispatch_mode<QW35_GF4_TYPE, 32>(dmode, exact, m0, m1, s0, s1, y0m, y1m, p, st);
+        else e = dq_dispatch_mode<QW35_GF4_TYPE, 64>(dmode, exact, m0, m1, s0, s1, y0m, y1m, p, st);
     } else {
-        if (NP == 16) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 16>(dmode, true, m0, m1, s0, s1, p, st);
-        else if (NP == 32) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 32>(dmode, true, m0, m1, s0, s1, p, st);
-        else e = dq_dispatch_mode<QW35_Q8_0_TYPE, 64>(dmode, true, m0, m1, s0, s1, p, st);
+        if (NP == 16) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 16>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
+        else if (NP == 32) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 32>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
+        else e = dq_dispatch_mode<QW35_Q8_0_TYPE, 64>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
     }
     if (e != cudaSuccess) return e;
     if (mode == 2) {
