@@ -31,7 +31,7 @@ constexpr int AKV = 4;      // kv heads
 constexpr int AHD = 256;    // head dim
 constexpr int AGRP = AH / AKV;
 constexpr int ACHUNK = 256; // positions per chunk
-constexpr int ASPLIT = 1024;  // positions per split (4 warps x 256)
+constexpr int ASPLIT = 256;  // positions per split (4 warps x 64): ~2 waves of CTAs at batch 32, ctx 4096
 constexpr int QFULL = AH * AHD * 2;  // q | gate per head
 
 // ---- preprocess: RMS norm + NeoX RoPE + f16 KV write -------------------------

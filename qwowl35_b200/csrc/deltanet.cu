@@ -34,12 +34,18 @@ constexpr int ROWS = 32;        // state rows per CTA
 
 // Delta-rule update of this CTA's 32 rows.  4 warps x 8 rows; each lane owns
 // 4 consecutive state columns (one float4) of every row.
-__device__ __forceinline__ void delta_rows(float *S, const float4 kc, const float4 qc, const float *vrow,
-                                           float gate, float beta, float kq, float scale, float *ysm) {
+// This thread's 4 state columns of its warp's 8 rows (streamed: read once).
+__device__ __forceinline__ void load_rows(const float *S, float4 *sv) {
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    float4 sv[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) sv[i] = reinterpret_cast<const float4 *>(S + (size_t)(wid * 8 + i) * DS)[lane];
+    for (int i = 0; i < 8; ++i)
+        sv[i] = __ldcs(reinterpret_cast<const float4 *>(S + (size_t)(wid * 8 + i) * DS) + lane);
+}
+
+__device__ __forceinline__ void delta_rows(float *S, const float4 *sv, const float4 kc, const float4 qc,
+                                           const float *vrow, float gate, float beta, float kq, float scale,
+                                           float *ysm) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     float kd[8], qd[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -62,7 +68,7 @@ __device__ __forceinline__ void delta_rows(float *S, const float4 kc, const floa
         n.y = sv[i].y * gate + kc.y * delta;
         n.z = sv[i].z * gate + kc.z * delta;
         n.w = sv[i].w * gate + kc.w * delta;
-        reinterpret_cast<float4 *>(S + (size_t)r * DS)[lane] = n;
+        __stcs(reinterpret_cast<float4 *>(S + (size_t)r * DS) + lane, n);  // written once, not re-read soon
         if (lane == 0) ysm[r] = (gate * qd[i] + delta * kq) * scale;
     }
 }
@@ -88,6 +94,11 @@ deltanet_step_kernel(DeltaNetArgs p) {
     const float *proj = p.proj + (size_t)seq * p.proj_stride;
     float *cs = p.conv_state + slot * p.conv_stride;
     float *S = p.ssm_state + slot * p.ssm_stride + ((size_t)h * DS + rb * ROWS) * DS;
+
+    // the state rows are the bulk of the traffic: their loads go out first and
+    // land while the conv / norm prologue runs
+    float4 sv[8];
+    load_rows(S, sv);
 
     // (1) conv + SiLU of this group's q and k channels (every CTA of the cluster)
     const int qc = g * DS + tid, kc = NQK * DS + g * DS + tid;
@@ -131,7 +142,7 @@ deltanet_step_kernel(DeltaNetArgs p) {
     const int lane = tid & 31;
     const float4 kc4 = reinterpret_cast<const float4 *>(kn_s)[lane];
     const float4 qc4 = reinterpret_cast<const float4 *>(qn_s)[lane];
-    delta_rows(S, kc4, qc4, v_s, gate, beta, kq, 0.08838834764831845f, y_s);
+    delta_rows(S, sv, kc4, qc4, v_s, gate, beta, kq, 0.08838834764831845f, y_s);
     __syncthreads();
 
     // (4) per-head RMS of y across the 4 CTAs of this head (DSMEM)
@@ -159,6 +170,9 @@ __global__ void __launch_bounds__(128) deltanet_core_kernel(DeltaCoreArgs p) {
     const int seq = blockIdx.y;
     const int tid = threadIdx.x;
     const int g = h % NQK;
+    float *S = p.state + (((size_t)seq * NV + h) * DS + rb * ROWS) * DS;
+    float4 sv[8];
+    load_rows(S, sv);  // issued first: lands while q/k/v are staged
     __shared__ __align__(16) float qn_s[DS];
     __shared__ __align__(16) float kn_s[DS];
     __shared__ float v_s[ROWS];
@@ -175,8 +189,7 @@ __global__ void __launch_bounds__(128) deltanet_core_kernel(DeltaCoreArgs p) {
     const int lane = tid & 31;
     const float4 kc4 = reinterpret_cast<const float4 *>(kn_s)[lane];
     const float4 qc4 = reinterpret_cast<const float4 *>(qn_s)[lane];
-    float *S = p.state + (((size_t)seq * NV + h) * DS + rb * ROWS) * DS;
-    delta_rows(S, kc4, qc4, v_s, gate, beta, kq, p.scale, y_s);
+    delta_rows(S, sv, kc4, qc4, v_s, gate, beta, kq, p.scale, y_s);
     __syncthreads();
     if (tid < ROWS) p.y[((size_t)seq * NV + h) * DS + rb * ROWS + tid] = y_s[tid];
 }

@@ -45,7 +45,6 @@
 namespace qw35 {
 
 constexpr int TM = 128;  // weight rows per tile (MMA M = TMEM lanes)
-constexpr int XKC = 128; // K columns per chunk of the activation prep layout
 
 // Per-codec geometry.  A weight chunk is 128 rows x 128 bytes of codes (one
 // 16 KB TMA box, 128B-swizzled): 256 K columns of GF4 or 128 of Q8_0; Q8_0
@@ -268,6 +267,7 @@ __device__ __forceinline__ void dq_range(const DqParams &p, int &gbeg, int &gend
         const int c1 = min((nch), c0 + ((gend) - g_));                                     \
         const int m = q_ / (p).tiles;                                                      \
         const int tile = q_ - m * (p).tiles;                                               \
+        (void)tile;                                                                        \
         __VA_ARGS__                                                                        \
         g_ += c1 - c0;                                                                     \
     }

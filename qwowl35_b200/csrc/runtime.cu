@@ -58,7 +58,6 @@ struct Loader {
         if (it == byname.end()) fail("missing tensor %s", name.c_str());
         return it->second;
     }
-    bool has(const std::string &name) const { return byname.count(name) != 0; }
 
     void *dalloc(size_t bytes) {
         void *p = nullptr;
