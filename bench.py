@@ -166,6 +166,14 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # the step's kernels timed alone (roofline of the dominant one)
 # ---------------------------------------------------------------------------
+# DRAM bytes (read + write) per launch measured by ncu for a kernel class of the
+# table, from the capture summarised in profiles/ (see the file named per entry).
+NCU_TRAFFIC = {
+    # profiles/dq_kernel_gf4_gateup_b32.md: 54.075 MB read + 0.530 MB written
+    "gate_up_swiglu GF4 12288x4096": 54_605_312,
+}
+
+
 def kernel_table(B: int, ctx: int, device):
     """Times each kernel class of the step alone and returns rows of
     (name, algorithmic bytes per launch, avg seconds per launch, launches per step).
@@ -399,9 +407,11 @@ def main():
     with ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else
                       int(os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])) as clk:
         ev0.record(ext)
+        torch.cuda.nvtx.range_push("timed_steps")  # lets a profiler select just these launches
         for _ in range(args.steps):
             rt.eval_batch(ids, tok, [pos] * B, LogitsMode.ARGMAX)
             pos += 1
+        torch.cuda.nvtx.range_pop()
         ev1.record(ext)
         ev1.synchronize()
     rt.sync()
@@ -460,7 +470,8 @@ def main():
         dom = max(rows, key=lambda r: r[2] * r[3])
         achieved = dom[1] / dom[2] / 1e9
         line["roofline"] = {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": peak,
-                            "peak_kind": kind, "unit": "GB/s", "frac": achieved / peak, "traffic": None,
+                            "peak_kind": kind, "unit": "GB/s", "frac": achieved / peak,
+                            "traffic": NCU_TRAFFIC.get(dom[0]),
                             "bytes_per_launch": dom[1], "us_per_launch": dom[2] * 1e6}
         line["kernels"] = table
     if rank == 0 and world == 1 and not args.no_cpu:

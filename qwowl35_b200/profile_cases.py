@@ -1,0 +1,64 @@
+"""Named single-kernel workloads for profiling (ncu) through the public ops API.
+
+    python -m qwowl35_b200.profile_cases gateup_gf4_b32
+    python -m qwowl35_b200.profile_cases matvec_q8_0_b32
+
+Each case runs the call the decode step makes for one kernel class, over
+enough rotating weight copies (> the 126 MB L2) that a launch after the first
+two streams its weights from HBM; e.g. capture the third launch with
+``ncu -k regex:dq_kernel -s 2 -c 1``.  Weights are random codes with
+realistic scales (GF4 e5m2 scale 2^-6, Q8_0 d = 2^-13); activations N(0, 1).
+"""
+from __future__ import annotations
+
+import sys
+
+import torch
+
+from . import ops
+
+B, H, F = 32, 4096, 12288
+
+
+def _weight(type_id: int, rows: int, k: int, device) -> torch.Tensor:
+    raw = torch.randint(0, 256, (ops.weight_bytes(type_id, rows, k),), dtype=torch.uint8, device=device)
+    if type_id == ops.GF4:
+        raw.view(-1, 4)[:, 0] = 0x24
+    elif type_id == ops.Q8_0:
+        raw.view(-1, 34)[:, 0:2] = torch.tensor([0x00, 0x20], dtype=torch.uint8, device=device)
+    return ops.repack(type_id, raw, rows, k)
+
+
+def gateup_gf4_b32(device) -> None:
+    """FFN gate/up pair (GF4 2 x 12288 x 4096, batch 32): one dq_kernel launch each."""
+    ws = [(_weight(ops.GF4, F, H, device), _weight(ops.GF4, F, H, device)) for _ in range(4)]
+    x = torch.randn(B, H, device=device)
+    for wg, wu in ws:
+        ops.gate_up_swiglu(ops.GF4, wg, wu, x, F, H)
+
+
+def matvec_q8_0_b32(device) -> None:
+    """DeltaNet input projection (Q8_0 12352 x 4096, batch 32)."""
+    ws = [_weight(ops.Q8_0, 12352, H, device) for _ in range(4)]
+    x = torch.randn(B, H, device=device)
+    y = torch.empty(B, 12352, device=device)
+    for w in ws:
+        ops.matvec(ops.Q8_0, w, x, 12352, H, y=y)
+
+
+CASES = {"gateup_gf4_b32": gateup_gf4_b32, "matvec_q8_0_b32": matvec_q8_0_b32}
+
+
+def main(argv: list[str]) -> int:
+    if len(argv) != 1 or argv[0] not in CASES:
+        print("usage: python -m qwowl35_b200.profile_cases {" + "|".join(CASES) + "}", file=sys.stderr)
+        return 2
+    device = torch.device("cuda")
+    CASES[argv[0]](device)
+    torch.cuda.synchronize()
+    print("done")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main(sys.argv[1:]))
