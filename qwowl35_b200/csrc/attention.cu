@@ -33,6 +33,8 @@ constexpr int AGRP = AH / AKV;
 constexpr int ACHUNK = 256; // positions per chunk
 constexpr int ASPLIT = 256;  // positions per split (4 warps x 64): ~2 waves of CTAs at batch 32, ctx 4096
 constexpr int QFULL = AH * AHD * 2;  // q | gate per head
+constexpr int ASTG = 3;     // cp.async stages per warp in the split kernel (8 positions each)
+constexpr size_t ASMEM = (size_t)4 * ASTG * 2 * 8 * 32 * 16;  // 48 KiB of K/V staging per CTA
 
 // ---- preprocess: RMS norm + NeoX RoPE + f16 KV write -------------------------
 __global__ void __launch_bounds__(256) attn_pre_kernel(AttnPreArgs p) {
@@ -91,6 +93,15 @@ __global__ void __launch_bounds__(256) attn_pre_kernel(AttnPreArgs p) {
 }
 
 // ---- split-K decode -----------------------------------------------------------
+// 16-byte global -> shared copy (L2 only); zero-filled when !valid.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(valid ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 __device__ __forceinline__ void h8_to_f(const uint4 &u, float *f) {
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -148,24 +159,51 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_
     const uint64_t *ctab = p.chunk_ptrs + (p.slots ? (size_t)p.slots[seq] : (size_t)seq) * p.max_chunks;
     const size_t head_off = (size_t)kvh * ACHUNK * AHD;
 
+    // Per-warp ring of ASTG stages; a stage holds K and V of 8 positions, one
+    // 16-byte piece per lane and row (cp.async, zero-filled past i1), so the
+    // next blocks' loads are in flight while this block is computed.
+    extern __shared__ __align__(16) uint4 ring[];  // [4 warps][ASTG][2][8][32]
+    uint4 *wring = ring + (size_t)wid * ASTG * 2 * 8 * 32;
+    auto issue = [&](int ib, int stage) {
+        uint4 *dst = wring + (size_t)stage * 2 * 8 * 32;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const int idx = ib + t;
+            const bool ok = idx < i1;
+            const int pos = ok ? (idx < sk ? idx : rstart + (idx - sk)) : 0;
+            const uint64_t base = ctab[ok ? pos / ACHUNK : 0];
+            const size_t off = (head_off + (size_t)(pos % ACHUNK) * AHD + lane * 8) * sizeof(__half);
+            cp_async16(dst + t * 32 + lane, reinterpret_cast<const void *>(base + p.k_off + off), ok);
+            cp_async16(dst + (8 + t) * 32 + lane, reinterpret_cast<const void *>(base + p.v_off + off), ok);
+        }
+    };
+#pragma unroll
+    for (int s0 = 0; s0 < ASTG - 1; ++s0) {
+        if (i0 + 8 * s0 < i1) issue(i0 + 8 * s0, s0);
+        cp_async_commit();
+    }
+    int stage = 0;
     for (int ib = i0; ib < i1; ib += 8) {
+        {   // next block into the stage consumed last iteration
+            const int nb = ib + 8 * (ASTG - 1);
+            int ns = stage + ASTG - 1;
+            if (ns >= ASTG) ns -= ASTG;
+            if (nb < i1) issue(nb, ns);
+            cp_async_commit();
+        }
+        cp_async_wait<ASTG - 1>();  // this block's group has landed
+        __syncwarp();
+        const uint4 *cur = wring + (size_t)stage * 2 * 8 * 32;
         uint4 kr[8], vr[8];
         bool valid[8];
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
-            const int idx = ib + t;
-            valid[t] = idx < i1;
-            const int pos = idx < sk ? idx : rstart + (idx - sk);
-            if (valid[t]) {
-                const uint64_t base = ctab[pos / ACHUNK];
-                const size_t off = (head_off + (size_t)(pos % ACHUNK) * AHD + lane * 8) * sizeof(__half);
-                kr[t] = ldg_stream(reinterpret_cast<const void *>(base + p.k_off + off));
-                vr[t] = ldg_stream(reinterpret_cast<const void *>(base + p.v_off + off));
-            } else {
-                kr[t] = make_uint4(0, 0, 0, 0);
-                vr[t] = make_uint4(0, 0, 0, 0);
-            }
+            valid[t] = ib + t < i1;
+            kr[t] = cur[t * 32 + lane];
+            vr[t] = cur[(8 + t) * 32 + lane];
         }
+        __syncwarp();  // the stage may be refilled by the next iteration's issue
+        if (++stage == ASTG) stage = 0;
         // partial dots: s[t*4 + hh]
         float s[32];
 #pragma unroll
@@ -299,7 +337,14 @@ cudaError_t attn_decode_run(const AttnArgs &a, cudaStream_t st) {
     if (a.ws_bytes < attn_workspace_bytes(a.n_seq, a.max_len)) return cudaErrorInvalidValue;
     const int ns = (a.max_len + ASPLIT - 1) / ASPLIT;
     dim3 g1(ns, AKV, a.n_seq);
-    attn_split_kernel<<<g1, 128, 0, st>>>(a, ns);
+    cudaError_t e0;
+    static bool attr = false;
+    if (!attr) {
+        e0 = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
+        if (e0 != cudaSuccess) return e0;
+        attr = true;
+    }
+    attn_split_kernel<<<g1, 128, ASMEM, st>>>(a, ns);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     dim3 g2(AH, a.n_seq);

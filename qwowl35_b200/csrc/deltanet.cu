@@ -5,15 +5,12 @@
 //
 // Per layer and sequence: 32 value heads x 128 state rows x 128 columns of
 // fp32 state (2 MiB), read once and written once.  The reference runs one
-// 256-thread threadgroup per qk group (16 per sequence).  Here a thread-block
-// CLUSTER of 8 CTAs owns one qk group g: CTA rank r handles value head
-// g + 16*(r/4) and state rows [32*(r%4), 32*(r%4)+32).  That gives 128 CTAs
-// per sequence (one per SM at batch 1) and keeps every state byte on a
-// single coalesced 512-byte row walk.  Cross-CTA pieces use the cluster:
-//   * the q/k conv window is read by all 8 CTAs, so rank 0 retires the
-//     conv-state shift only after a cluster barrier;
-//   * the per-head RMS of y spans the 4 CTAs of a head and is exchanged
-//     through distributed shared memory.
+// 256-thread threadgroup per qk group (16 per sequence).  Here one 512-thread
+// CTA owns one value head (all 128 state rows, so the per-head RMS of y stays
+// in the CTA), and the two heads g and g + 16 that share qk group g form a
+// thread-block cluster of 2: both read the group's q/k conv window, so rank 0
+// retires the conv-state shift only after a cluster barrier.  Every state
+// byte is on a coalesced 512-byte row walk, issued at kernel entry.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -73,48 +70,50 @@ __device__ __forceinline__ void delta_rows(float *S, const float4 *sv, const flo
     }
 }
 
-__global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(128)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512)
 deltanet_step_kernel(DeltaNetArgs p) {
     cg::cluster_group cluster = cg::this_cluster();
-    const int rank = (int)cluster.block_rank();  // == blockIdx.x
+    const int rank = (int)cluster.block_rank();  // == blockIdx.x: value head g or g + 16
     const int g = blockIdx.y;
     const int seq = blockIdx.z;
-    const int h = g + NQK * (rank >> 2);
-    const int rb = rank & 3;
+    const int h = g + NQK * rank;
     const int tid = threadIdx.x;
     const long long slot = p.slots ? (long long)p.slots[seq] : (long long)seq;
 
     __shared__ __align__(16) float qn_s[DS];
     __shared__ __align__(16) float kn_s[DS];
-    __shared__ float v_s[ROWS];
-    __shared__ float y_s[ROWS];
+    __shared__ float v_s[DS];
+    __shared__ float y_s[DS];
     __shared__ float red[32];
-    __shared__ float ssq;
 
     const float *proj = p.proj + (size_t)seq * p.proj_stride;
     float *cs = p.conv_state + slot * p.conv_stride;
-    float *S = p.ssm_state + slot * p.ssm_stride + ((size_t)h * DS + rb * ROWS) * DS;
+    float *S = p.ssm_state + slot * p.ssm_stride + (size_t)h * DS * DS;
 
-    // the state rows are the bulk of the traffic: their loads go out first and
-    // land while the conv / norm prologue runs
+    // the head's 128 state rows are the bulk of the traffic: their loads go
+    // out first (16 warps x 8 rows) and land while the prologue runs
     float4 sv[8];
     load_rows(S, sv);
 
-    // (1) conv + SiLU of this group's q and k channels (every CTA of the cluster)
-    const int qc = g * DS + tid, kc = NQK * DS + g * DS + tid;
-    const float q0 = cs[qc * 3 + 0], q1 = cs[qc * 3 + 1], q2 = cs[qc * 3 + 2], qx = proj[qc];
-    const float k0 = cs[kc * 3 + 0], k1 = cs[kc * 3 + 1], k2 = cs[kc * 3 + 2], kx = proj[kc];
-    const float4 wq = reinterpret_cast<const float4 *>(p.conv_w)[qc];
-    const float4 wk = reinterpret_cast<const float4 *>(p.conv_w)[kc];
-    const float q = silu_f(q0 * wq.x + q1 * wq.y + q2 * wq.z + qx * wq.w);
-    const float k = silu_f(k0 * wk.x + k1 * wk.y + k2 * wk.z + kx * wk.w);
-
-    // value channels owned by this CTA (exclusive: shift their window right away)
-    if (tid < ROWS) {
-        const int vc = 2 * NQK * DS + h * DS + rb * ROWS + tid;
+    // (1) conv + SiLU: threads 0..127 the group's q channels, 128..255 its k
+    // channels (both read by the two CTAs of the cluster), 256..383 this
+    // head's value channels (exclusive: their window shifts right away)
+    float q = 0.0f, k = 0.0f, qwin[3] = {0.f, 0.f, 0.f}, qx = 0.0f;
+    int ch = -1;
+    if (tid < 2 * DS) {
+        ch = tid < DS ? g * DS + tid : NQK * DS + g * DS + (tid - DS);
+        qwin[0] = cs[ch * 3 + 0]; qwin[1] = cs[ch * 3 + 1]; qwin[2] = cs[ch * 3 + 2];
+        qx = proj[ch];
+        const float4 w = reinterpret_cast<const float4 *>(p.conv_w)[ch];
+        const float o = silu_f(qwin[0] * w.x + qwin[1] * w.y + qwin[2] * w.z + qx * w.w);
+        if (tid < DS) q = o;
+        else k = o;
+    } else if (tid < 3 * DS) {
+        const int d = tid - 2 * DS;
+        const int vc = 2 * NQK * DS + h * DS + d;
         const float v0 = cs[vc * 3 + 0], v1 = cs[vc * 3 + 1], v2 = cs[vc * 3 + 2], vx = proj[vc];
         const float4 wv = reinterpret_cast<const float4 *>(p.conv_w)[vc];
-        v_s[tid] = silu_f(v0 * wv.x + v1 * wv.y + v2 * wv.z + vx * wv.w);
+        v_s[d] = silu_f(v0 * wv.x + v1 * wv.y + v2 * wv.z + vx * wv.w);
         cs[vc * 3 + 0] = v1;
         cs[vc * 3 + 1] = v2;
         cs[vc * 3 + 2] = vx;
@@ -123,20 +122,20 @@ deltanet_step_kernel(DeltaNetArgs p) {
     // (2) L2 norms with max(norm, eps) and the normalised k.q dot
     const float q_ss = block_sum(q * q, red);
     const float k_ss = block_sum(k * k, red);
-    const float qn = q * (1.0f / fmaxf(sqrtf(q_ss), p.eps));
-    const float kn = k * (1.0f / fmaxf(sqrtf(k_ss), p.eps));
-    const float kq = block_sum(qn * kn, red);
-    qn_s[tid] = qn;
-    kn_s[tid] = kn;
+    if (tid < DS) qn_s[tid] = q * (1.0f / fmaxf(sqrtf(q_ss), p.eps));
+    else if (tid < 2 * DS) kn_s[tid - DS] = k * (1.0f / fmaxf(sqrtf(k_ss), p.eps));
+    __syncthreads();
+    const float kq = block_sum(tid < DS ? qn_s[tid] * kn_s[tid] : 0.0f, red);
 
-    // every CTA has read the old q/k window: rank 0 retires the shift
+    // both heads of the group have read the old q/k window: rank 0 retires the shift
     cluster.sync();
-    if (rank == 0) {
-        cs[qc * 3 + 0] = q1; cs[qc * 3 + 1] = q2; cs[qc * 3 + 2] = qx;
-        cs[kc * 3 + 0] = k1; cs[kc * 3 + 1] = k2; cs[kc * 3 + 2] = kx;
+    if (rank == 0 && ch >= 0) {
+        cs[ch * 3 + 0] = qwin[1];
+        cs[ch * 3 + 1] = qwin[2];
+        cs[ch * 3 + 2] = qx;
     }
 
-    // (3) gates and the delta-rule state update
+    // (3) gates and the delta-rule state update (16 warps x 8 rows)
     const float beta = sigmoid_f(proj[BOFF + h]);
     const float gate = expf(softplus_f(proj[AOFF + h] + p.dt[h]) * p.a[h]);
     const int lane = tid & 31;
@@ -145,22 +144,13 @@ deltanet_step_kernel(DeltaNetArgs p) {
     delta_rows(S, sv, kc4, qc4, v_s, gate, beta, kq, 0.08838834764831845f, y_s);
     __syncthreads();
 
-    // (4) per-head RMS of y across the 4 CTAs of this head (DSMEM)
-    float y2 = tid < ROWS ? y_s[tid] * y_s[tid] : 0.0f;
-    y2 = block_sum(y2, red);
-    if (tid == 0) ssq = y2;
-    cluster.sync();
-    float tot = 0.0f;
-    const int first = rank & 4;
-#pragma unroll
-    for (int r = 0; r < 4; ++r) tot += *cluster.map_shared_rank(&ssq, first + r);
-    const float inv = rsqrtf(tot / (float)DS + p.eps);
-    if (tid < ROWS) {
-        const int d = rb * ROWS + tid;
-        const float z = proj[ZOFF + h * DS + d];
-        p.out[(size_t)seq * p.out_stride + h * DS + d] = y_s[tid] * inv * p.norm_w[d] * silu_f(z);
+    // (4) per-head RMS of y (all 128 rows are in this CTA), gated output
+    const float y2 = block_sum(tid < DS ? y_s[tid] * y_s[tid] : 0.0f, red);
+    const float inv = rsqrtf(y2 / (float)DS + p.eps);
+    if (tid < DS) {
+        const float z = proj[ZOFF + h * DS + tid];
+        p.out[(size_t)seq * p.out_stride + h * DS + tid] = y_s[tid] * inv * p.norm_w[tid] * silu_f(z);
     }
-    cluster.sync();  // peers may still read ssq
 }
 
 // Recurrent core only (config 3 of the benchmark): prepared q/k/v, beta, g.
@@ -197,8 +187,8 @@ __global__ void __launch_bounds__(128) deltanet_core_kernel(DeltaCoreArgs p) {
 cudaError_t deltanet_step_run(const DeltaNetArgs &a, cudaStream_t st) {
     if (a.n_seq <= 0) return cudaSuccess;
     if (a.n_seq > 65535) return cudaErrorInvalidValue;
-    dim3 grid(8, NQK, a.n_seq);
-    deltanet_step_kernel<<<grid, 128, 0, st>>>(a);
+    dim3 grid(2, NQK, a.n_seq);
+    deltanet_step_kernel<<<grid, 512, 0, st>>>(a);
     return cudaGetLastError();
 }
 
