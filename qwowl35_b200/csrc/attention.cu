@@ -125,9 +125,50 @@ __device__ __forceinline__ void attended_range(int L, int window, int sink, int 
     }
 }
 
+// m16n8k16 f16 x f16 -> f32 (legacy warp MMA; this kernel is bound by HBM, the
+// tensor cores only retire its arithmetic)
+__device__ __forceinline__ void mma16816(float *d, const uint32_t *a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t *r, const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t *r, const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+// a = hi + lo in f16 (hi rounded, lo the rounded remainder): ~22 bits of a
+__device__ __forceinline__ void split_h2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = pack_h2(a - hf.x, b - hf.y);
+}
+
+// One CTA per (split of ASPLIT positions, kv head, sequence); 4 warps take
+// ASPLIT/4 consecutive positions each, 8 per step.  Scores S^T = K Q^T and
+// the output O^T += V^T P^T run on mma.sync (M = 16: the step's 8 positions
+// fill rows 0-7 and repeat in rows 8-15, whose results are dropped; N = 8:
+// the group's 4 query heads, zero-padded).  q and p enter as f16 hi + lo
+// pairs (two MMAs each), so both products keep ~22 bits; K and V are the
+// cache's f16.  Lane (g = lane/4, t = lane%4) holds the scores of position
+// g for heads 2t, 2t+1 and O^T rows (dims) 16 j + g, + 8 for the same heads;
+// lanes with t >= 2 carry the padding.
 __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_max) {
     const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int g = lane >> 2, t4 = lane & 3;
     const int L = p.seq_len[seq];
     int total, sk, rstart;
     attended_range(L, p.window, p.sink, total, sk, rstart);
@@ -137,44 +178,49 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_
     __shared__ float wm[4][AGRP], wl[4][AGRP];
     __shared__ __align__(16) float wacc[4][AGRP][AHD];
 
-    // q for the 4 heads of the group, pre-scaled by sm_scale (1/16: exact)
-    float q[AGRP][8];
+    // B fragments of Q^T (k = dims, n = head g): k-step j needs dims
+    // 16j + 2t, +1 (b0) and 16j + 8 + 2t, +1 (b1); pre-scaled by sm_scale.
+    uint32_t qh[16][2], ql[16][2];
+    {
+        const bool real = g < AGRP;
+        const float *qr = p.q + ((size_t)seq * AH + kvh * AGRP + (real ? g : 0)) * AHD;
 #pragma unroll
-    for (int hh = 0; hh < AGRP; ++hh) {
-        const float4 *qp = reinterpret_cast<const float4 *>(p.q + ((size_t)seq * AH + kvh * AGRP + hh) * AHD + lane * 8);
-        const float4 a = qp[0], b = qp[1];
-        q[hh][0] = a.x * p.scale; q[hh][1] = a.y * p.scale; q[hh][2] = a.z * p.scale; q[hh][3] = a.w * p.scale;
-        q[hh][4] = b.x * p.scale; q[hh][5] = b.y * p.scale; q[hh][6] = b.z * p.scale; q[hh][7] = b.w * p.scale;
+        for (int j = 0; j < 16; ++j) {
+#pragma unroll
+            for (int hb = 0; hb < 2; ++hb) {
+                const float2 v = *reinterpret_cast<const float2 *>(qr + 16 * j + 8 * hb + 2 * t4);
+                const float a = real ? v.x * p.scale : 0.0f, b = real ? v.y * p.scale : 0.0f;
+                split_h2(a, b, qh[j][hb], ql[j][hb]);
+            }
+        }
     }
-    float m[AGRP], l[AGRP], acc[AGRP][8];
+    float o[16][4];
 #pragma unroll
-    for (int hh = 0; hh < AGRP; ++hh) {
-        m[hh] = -INFINITY; l[hh] = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[hh][i] = 0.0f;
-    }
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+    float ma = -INFINITY, mb = -INFINITY, la = 0.0f, lb = 0.0f;  // heads 2t, 2t+1
 
     const int i0 = split * ASPLIT + wid * (ASPLIT / 4);
     const int i1 = min(i0 + ASPLIT / 4, total);
     const uint64_t *ctab = p.chunk_ptrs + (p.slots ? (size_t)p.slots[seq] : (size_t)seq) * p.max_chunks;
     const size_t head_off = (size_t)kvh * ACHUNK * AHD;
 
-    // Per-warp ring of ASTG stages; a stage holds K and V of 8 positions, one
-    // 16-byte piece per lane and row (cp.async, zero-filled past i1), so the
-    // next blocks' loads are in flight while this block is computed.
-    extern __shared__ __align__(16) uint4 ring[];  // [4 warps][ASTG][2][8][32]
+    // Per-warp ring of ASTG stages; a stage holds K then V of 8 positions, each
+    // row's 16-byte piece c stored at c ^ (row % 8) so ldmatrix reads hit eight
+    // distinct bank groups (cp.async, zero-filled past i1).
+    extern __shared__ __align__(16) uint4 ring[];  // [4 warps][ASTG][2][8 rows][32 pieces]
     uint4 *wring = ring + (size_t)wid * ASTG * 2 * 8 * 32;
     auto issue = [&](int ib, int stage) {
         uint4 *dst = wring + (size_t)stage * 2 * 8 * 32;
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            const int idx = ib + t;
+        for (int r = 0; r < 8; ++r) {
+            const int idx = ib + r;
             const bool ok = idx < i1;
             const int pos = ok ? (idx < sk ? idx : rstart + (idx - sk)) : 0;
             const uint64_t base = ctab[ok ? pos / ACHUNK : 0];
             const size_t off = (head_off + (size_t)(pos % ACHUNK) * AHD + lane * 8) * sizeof(__half);
-            cp_async16(dst + t * 32 + lane, reinterpret_cast<const void *>(base + p.k_off + off), ok);
-            cp_async16(dst + (8 + t) * 32 + lane, reinterpret_cast<const void *>(base + p.v_off + off), ok);
+            const int pc = lane ^ r;
+            cp_async16(dst + r * 32 + pc, reinterpret_cast<const void *>(base + p.k_off + off), ok);
+            cp_async16(dst + (8 + r) * 32 + pc, reinterpret_cast<const void *>(base + p.v_off + off), ok);
         }
     };
 #pragma unroll
@@ -182,6 +228,7 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_
         if (i0 + 8 * s0 < i1) issue(i0 + 8 * s0, s0);
         cp_async_commit();
     }
+    const int lr = lane & 7;  // ldmatrix row (position) this lane addresses
     int stage = 0;
     for (int ib = i0; ib < i1; ib += 8) {
         {   // next block into the stage consumed last iteration
@@ -193,85 +240,90 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_
         }
         cp_async_wait<ASTG - 1>();  // this block's group has landed
         __syncwarp();
-        const uint4 *cur = wring + (size_t)stage * 2 * 8 * 32;
-        uint4 kr[8], vr[8];
-        bool valid[8];
+        const uint4 *ks = wring + (size_t)stage * 2 * 8 * 32;
+        const uint4 *vs = ks + 8 * 32;
+
+        // S^T (16 x 8) = K (16 x 256) Q^T (256 x 8): A rows = positions (rows 8-15 repeat 0-7)
+        // four independent accumulators (q hi / lo x even / odd k-step) keep four
+        // MMA chains in flight instead of one 32-long dependent chain
+        float acc4[4][4] = {};
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            valid[t] = ib + t < i1;
-            kr[t] = cur[t * 32 + lane];
-            vr[t] = cur[(8 + t) * 32 + lane];
+        for (int j = 0; j < 16; ++j) {
+            uint32_t a[4];
+            const int c = 2 * j + ((lane >> 4) & 1);  // matrices 2, 3: dims + 8
+            ldsm_x4(a, ks + lr * 32 + (c ^ lr));
+            mma16816(acc4[j & 1], a, qh[j][0], qh[j][1]);
+            mma16816(acc4[2 + (j & 1)], a, ql[j][0], ql[j][1]);
+        }
+        float sc[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sc[i] = (acc4[0][i] + acc4[1][i]) + (acc4[2][i] + acc4[3][i]);
+        // online softmax of heads 2t, 2t+1 over this step's 8 positions (lane rows g)
+        const bool valid = ib + g < i1;
+        const float sa = valid ? sc[0] : -INFINITY, sb = valid ? sc[1] : -INFINITY;
+        float bma = sa, bmb = sb;
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            bma = fmaxf(bma, __shfl_xor_sync(0xffffffffu, bma, off));
+            bmb = fmaxf(bmb, __shfl_xor_sync(0xffffffffu, bmb, off));
+        }
+        const float na = fmaxf(ma, bma), nb2 = fmaxf(mb, bmb);
+        const float pa = sa == -INFINITY ? 0.0f : expf(sa - na);
+        const float pb = sb == -INFINITY ? 0.0f : expf(sb - nb2);
+        float ra = pa, rb = pb;
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            ra += __shfl_xor_sync(0xffffffffu, ra, off);
+            rb += __shfl_xor_sync(0xffffffffu, rb, off);
+        }
+        const float alpha_a = ma == -INFINITY ? 0.0f : expf(ma - na);
+        const float alpha_b = mb == -INFINITY ? 0.0f : expf(mb - nb2);
+        la = la * alpha_a + ra;
+        lb = lb * alpha_b + rb;
+        if (__any_sync(0xffffffffu, na != ma || nb2 != mb)) {  // a running max moved: rescale O
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                o[j][0] *= alpha_a; o[j][1] *= alpha_b; o[j][2] *= alpha_a; o[j][3] *= alpha_b;
+            }
+        }
+        ma = na;
+        mb = nb2;
+        // B fragment of P^T (k = positions 2t, 2t+1; n = head g): from lanes
+        // (2t, g/2) and (2t+1, g/2), their head-pair slot g%2; heads >= 4 are zero
+        const int src0 = (2 * t4) * 4 + (g >> 1), src1 = src0 + 4;
+        const float x0a = __shfl_sync(0xffffffffu, pa, src0), x0b = __shfl_sync(0xffffffffu, pb, src0);
+        const float x1a = __shfl_sync(0xffffffffu, pa, src1), x1b = __shfl_sync(0xffffffffu, pb, src1);
+        const float p0 = g < AGRP ? ((g & 1) ? x0b : x0a) : 0.0f;
+        const float p1 = g < AGRP ? ((g & 1) ? x1b : x1a) : 0.0f;
+        uint32_t ph, pl;
+        split_h2(p0, p1, ph, pl);
+        // O^T (256 x 8) += V^T (256 x 16) P^T (16 x 8): positions 8-15 have p = 0
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            uint32_t a[4];
+            const int c = 2 * j + ((lane >> 3) & 1);  // matrices 1, 3: dims + 8
+            ldsm_x4_t(a, vs + lr * 32 + (c ^ lr));
+            mma16816(o[j], a, ph, 0u);
+            mma16816(o[j], a, pl, 0u);
         }
         __syncwarp();  // the stage may be refilled by the next iteration's issue
         if (++stage == ASTG) stage = 0;
-        // partial dots: s[t*4 + hh]
-        float s[32];
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            float kf[8];
-            h8_to_f(kr[t], kf);
-#pragma unroll
-            for (int hh = 0; hh < AGRP; ++hh) {
-                float d = 0.0f;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) d = fmaf(q[hh][i], kf[i], d);
-                s[t * 4 + hh] = d;
-            }
-        }
-        // transpose-reduce: lane j ends with the full dot of value j = (t = j/4, hh = j%4)
-#pragma unroll
-        for (int o = 16, n = 32; o >= 1; o >>= 1, n >>= 1) {
-            const bool upper = (lane & o) != 0;
-#pragma unroll
-            for (int i = 0; i < n / 2; ++i) {
-                const float send = upper ? s[i] : s[i + n / 2];
-                const float keep = upper ? s[i + n / 2] : s[i];
-                s[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-            }
-        }
-        const int my_t = lane >> 2;
-        const float score = valid[0] && (ib + my_t) < i1 ? s[0] : -INFINITY;
-        // per-head block max: lanes with equal (lane & 3)
-        float bm = score;
-        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 4));
-        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 8));
-        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 16));
-        const float mold = m[lane & 3];
-        const float mnew = fmaxf(mold, bm);
-        const float pr = score == -INFINITY ? 0.0f : expf(score - mnew);
-        float ps = pr;
-        ps += __shfl_xor_sync(0xffffffffu, ps, 4);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 8);
-        ps += __shfl_xor_sync(0xffffffffu, ps, 16);
-#pragma unroll
-        for (int hh = 0; hh < AGRP; ++hh) {
-            const float mn = __shfl_sync(0xffffffffu, mnew, hh);
-            const float psum = __shfl_sync(0xffffffffu, ps, hh);
-            const float alpha = m[hh] == -INFINITY ? 0.0f : expf(m[hh] - mn);
-            l[hh] = l[hh] * alpha + psum;
-            m[hh] = mn;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[hh][i] *= alpha;
-        }
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            float vf[8];
-            h8_to_f(vr[t], vf);
-#pragma unroll
-            for (int hh = 0; hh < AGRP; ++hh) {
-                const float pw = __shfl_sync(0xffffffffu, pr, t * 4 + hh);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) acc[hh][i] = fmaf(pw, vf[i], acc[hh][i]);
-            }
-        }
     }
 
     // merge the 4 warps, write the split partial
-    if (lane < AGRP) { wm[wid][lane] = m[lane]; wl[wid][lane] = l[lane]; }
+    if (g == 0 && t4 < 2) {
+        wm[wid][2 * t4] = ma; wm[wid][2 * t4 + 1] = mb;
+        wl[wid][2 * t4] = la; wl[wid][2 * t4 + 1] = lb;
+    }
+    if (t4 < 2) {
 #pragma unroll
-    for (int hh = 0; hh < AGRP; ++hh)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) wacc[wid][hh][lane * 8 + i] = acc[hh][i];
+        for (int j = 0; j < 16; ++j) {
+            wacc[wid][2 * t4][16 * j + g] = o[j][0];
+            wacc[wid][2 * t4 + 1][16 * j + g] = o[j][1];
+            wacc[wid][2 * t4][16 * j + g + 8] = o[j][2];
+            wacc[wid][2 * t4 + 1][16 * j + g + 8] = o[j][3];
+        }
+    }
     __syncthreads();
     const size_t nsm = (size_t)nsplit_max;
     SplitPart *parts = static_cast<SplitPart *>(p.ws);

@@ -46,7 +46,28 @@ def matvec_q8_0_b32(device) -> None:
         ops.matvec(ops.Q8_0, w, x, 12352, H, y=y)
 
 
-CASES = {"gateup_gf4_b32": gateup_gf4_b32, "matvec_q8_0_b32": matvec_q8_0_b32}
+def gqa_b8_ctx4096(device) -> None:
+    """GQA split-K decode (one attention layer) at batch 8, 4096 positions each,
+    over 3 rotating KV pools (3 x 134 MB): the per-CTA work of the batch-32 step
+    with a quarter of the grid (small enough for a full ncu capture)."""
+    plane = 4 * 256 * 256  # f16 elements of one K (or V) plane of a chunk
+    ctx, nch, B = 4096, 16, 8
+    pools, tables = [], []
+    for _ in range(3):
+        pool = torch.randn(B * nch * 2 * plane, device=device).to(torch.float16)
+        base = pool.data_ptr()
+        tables.append(torch.tensor([[base + (s * nch + c) * 2 * plane * 2 for c in range(nch)] for s in range(B)],
+                                   dtype=torch.int64, device=device))
+        pools.append(pool)
+    q, gate = torch.randn(B, 16, 256, device=device), torch.randn(B, 16, 256, device=device)
+    lens = torch.full((B,), ctx, dtype=torch.int32, device=device)
+    ws = ops.gqa_workspace(B, ctx, device)
+    out = torch.empty(B, 4096, device=device)
+    for t in tables:
+        ops.gqa_decode(q, gate, lens, ctx, t, 0, plane * 2, ws=ws, out=out)
+
+
+CASES = {"gateup_gf4_b32": gateup_gf4_b32, "matvec_q8_0_b32": matvec_q8_0_b32, "gqa_b8_ctx4096": gqa_b8_ctx4096}
 
 
 def main(argv: list[str]) -> int:
