@@ -186,12 +186,13 @@ def kernel_table(B: int, ctx: int, device):
 
     from qwowl35_b200 import ops
 
+    from qwowl35_b200 import synth
+
+    gen = synth._Gen(1, device)
+
     def rnd_weight(t, rows, k):
-        raw = torch.randint(0, 256, (ops.weight_bytes(t, rows, k),), dtype=torch.uint8, device=device)
-        if t == ops.GF4:
-            raw.view(-1, 4)[:, 0] = 0x24
-        elif t == ops.Q8_0:
-            raw.view(-1, 34)[:, 0:2] = torch.tensor([0x00, 0x20], dtype=torch.uint8, device=device)
+        # the model's own code / scale distributions (decode cost depends on the scales)
+        raw = synth.gen_tensor(gen, t, k, rows, "weight")
         return ops.repack(t, raw, rows, k)
 
     def graph_time(fns, reps=3):

@@ -167,56 +167,50 @@ __device__ __forceinline__ void gf4_pair_to_halves(uint32_t w0, uint32_t w1, uin
     }
 }
 
-// Fast path for one word whose 2^-13 <= |s| <= 252.  The codes of pair i sit
-// (in `packed`, two halves) at bits 4+3i; pairs 0/1 use bits 4-6 and 7-9
-// directly and pairs 2/3 after one shift by 6, each OR-ed into the mantissa of
-// 1024 with a single LOP3: h = 1024 + 16 q_raw (bits 4-6) or 1024 + 128 q_raw
-// (bits 7-9).  Then (q_raw - 4) * (-0.25 s) = h * (-s/64) + 17 s, or
-// h * (-s/512) + 3 s, in one HFMA2 each: exact, since every constant is exact
-// in half for this range of s (3 significant bits, no underflow) and the exact
-// result is representable.  In Metal mode element 4 (high half of pair 0)
-// then gains junk * s * -0.25 * 2^-13 = (junk * 2^-6) * (-s/512) through one
-// more HFMA2 whose low lane adds 0: the exact value rounded once, the
-// reference's half(float(int16 * s')).
+// Fast path for one word whose |s| <= 252.  The codes of pair i sit (in
+// `packed`, two halves) at bits 4+3i; shifted down to bits 4-6 they are OR-ed
+// into the mantissa of 1024 with one LOP3: h = 1024 + 16 q_raw.  Then
+// (q_raw - 4) * (-0.25 s) = h * (-s/64) + 17 s in one HFMA2: exact, since
+// -s/64 and 17 s are exact in half for every such s (subnormal s included)
+// and the exact result is representable.  In Metal mode element 4 (high half
+// of pair 0) then gains junk * s * -0.25 * 2^-13 = (junk * 2^-9) * (-s/64)
+// through one more HFMA2 whose low lane adds 0: the exact value rounded once,
+// the reference's half(float(int16 * s')).
 template <bool EXACT>
 __device__ __forceinline__ uint4 gf4_word_fast(uint32_t w) {
     const uint32_t packed = (w & 0xfff00000u) | ((w >> 4) & 0x0000fff0u);  // codes i | i+4 16 bits apart
-    const uint32_t p6 = packed >> 6;
     const uint32_t hs = __byte_perm(w, 0u, 0x0404u);  // {s, s} as half2
     const __half2 s2 = *reinterpret_cast<const __half2 *>(&hs);
-    const __half2 m16 = __hmul2(s2, __half2half2(__ushort_as_half((unsigned short)0xA400)));   // -s/64
-    const __half2 a16 = __hmul2(s2, __half2half2(__ushort_as_half((unsigned short)0x4C40)));   // 17 s
-    const __half2 m128 = __hmul2(s2, __half2half2(__ushort_as_half((unsigned short)0x9800)));  // -s/512
-    const __half2 a128 = __hmul2(s2, __half2half2(__ushort_as_half((unsigned short)0x4200)));  // 3 s
+    const __half2 m16 = __hmul2(s2, __half2half2(__ushort_as_half((unsigned short)0xA400)));  // -s/64
+    const __half2 a16 = __hmul2(s2, __half2half2(__ushort_as_half((unsigned short)0x4C40)));  // 17 s
     const uint32_t v0 = (packed & 0x00700070u) ^ 0x64406440u;  // 1024 + 16 q_raw
-    const uint32_t v1 = (packed & 0x03800380u) ^ 0x66006600u;  // 1024 + 128 q_raw
-    const uint32_t v2 = (p6 & 0x00700070u) ^ 0x64406440u;
-    const uint32_t v3 = (p6 & 0x03800380u) ^ 0x66006600u;
+    const uint32_t v1 = ((packed >> 3) & 0x00700070u) ^ 0x64406440u;
+    const uint32_t v2 = ((packed >> 6) & 0x00700070u) ^ 0x64406440u;
+    const uint32_t v3 = ((packed >> 9) & 0x00700070u) ^ 0x64406440u;
     __half2 h0 = __hfma2(*reinterpret_cast<const __half2 *>(&v0), m16, a16);
-    const __half2 h1 = __hfma2(*reinterpret_cast<const __half2 *>(&v1), m128, a128);
+    const __half2 h1 = __hfma2(*reinterpret_cast<const __half2 *>(&v1), m16, a16);
     const __half2 h2 = __hfma2(*reinterpret_cast<const __half2 *>(&v2), m16, a16);
-    const __half2 h3 = __hfma2(*reinterpret_cast<const __half2 *>(&v3), m128, a128);
+    const __half2 h3 = __hfma2(*reinterpret_cast<const __half2 *>(&v3), m16, a16);
     if (!EXACT) {
-        // {+0, 16 + junk * 2^-6} - {0, 16}: the junk (w bits 11-19) in the high lane
-        const uint32_t jb = ((w << 5) & 0x01ff0000u) | 0x4C000000u;
+        // {+0, 2 + junk * 2^-9} - {0, 2}: the junk (w bits 11-19) in the high lane
+        const uint32_t jb = ((w << 5) & 0x01ff0000u) | 0x40000000u;
         const __half2 j = __hsub2(*reinterpret_cast<const __half2 *>(&jb),
                                   __halves2half2(__ushort_as_half((unsigned short)0x0000),
-                                                 __ushort_as_half((unsigned short)0x4C00)));
-        h0 = __hfma2(j, m128, h0);
+                                                 __ushort_as_half((unsigned short)0x4000)));
+        h0 = __hfma2(j, m16, h0);
     }
     return make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
                       *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
 }
 
 // Four words (one 16-byte piece of a weight row) -> four 8-half outputs.  The
-// fast path is taken when all four scales have 2^-13 <= |s| <= 252, i.e. e5m2
-// byte & 0x7f in [0x08, 0x5B], checked at once: adding 0x78 to a byte sets its
-// top bit exactly when it is >= 0x08, adding 0x24 exactly when it is > 0x5B.
+// fast path is taken when all four scales have |s| <= 252 (e5m2 byte & 0x7f
+// <= 0x5B), checked at once: adding 0x24 to each byte sets its top bit
+// exactly when the byte exceeds 0x5B.  Realistic scales never leave it.
 template <bool EXACT>
 __device__ __forceinline__ void gf4_quad_to_halves(const uint4 w4, uint4 &o0, uint4 &o1, uint4 &o2, uint4 &o3) {
     const uint32_t sb = __byte_perm(__byte_perm(w4.x, w4.y, 0x0040u), __byte_perm(w4.z, w4.w, 0x0040u), 0x5410u);
-    const uint32_t m = sb & 0x7f7f7f7fu;
-    if ((((m + 0x78787878u) & ~(m + 0x24242424u)) & 0x80808080u) == 0x80808080u) {
+    if ((((sb & 0x7f7f7f7fu) + 0x24242424u) & 0x80808080u) == 0u) {
         o0 = gf4_word_fast<EXACT>(w4.x);
         o1 = gf4_word_fast<EXACT>(w4.y);
         o2 = gf4_word_fast<EXACT>(w4.z);

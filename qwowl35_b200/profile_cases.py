@@ -6,8 +6,8 @@
 Each case runs the call the decode step makes for one kernel class, over
 enough rotating weight copies (> the 126 MB L2) that a launch after the first
 two streams its weights from HBM; e.g. capture the third launch with
-``ncu -k regex:dq_kernel -s 2 -c 1``.  Weights are random codes with
-realistic scales (GF4 e5m2 scale 2^-6, Q8_0 d = 2^-13); activations N(0, 1).
+``ncu -k regex:dq_kernel -s 2 -c 1``.  Weights follow the synthetic model's
+distributions (qwowl35_b200.synth); activations N(0, 1).
 """
 from __future__ import annotations
 
@@ -20,13 +20,14 @@ from . import ops
 B, H, F = 32, 4096, 12288
 
 
+_GEN = {}
+
+
 def _weight(type_id: int, rows: int, k: int, device) -> torch.Tensor:
-    raw = torch.randint(0, 256, (ops.weight_bytes(type_id, rows, k),), dtype=torch.uint8, device=device)
-    if type_id == ops.GF4:
-        raw.view(-1, 4)[:, 0] = 0x24
-    elif type_id == ops.Q8_0:
-        raw.view(-1, 34)[:, 0:2] = torch.tensor([0x00, 0x20], dtype=torch.uint8, device=device)
-    return ops.repack(type_id, raw, rows, k)
+    """Random weight with the synthetic model's code and scale distributions."""
+    from . import synth
+    g = _GEN.setdefault(str(device), synth._Gen(7, device))
+    return ops.repack(type_id, synth.gen_tensor(g, type_id, k, rows, "weight"), rows, k)
 
 
 def gateup_gf4_b32(device) -> None:
