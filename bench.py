@@ -298,6 +298,18 @@ def dist_env():
     return rank, world, local
 
 
+def max_over_ranks(v: float, world: int, device) -> float:
+    """The slowest rank's value (device-timed seconds): all_reduce(MAX) over the
+    process group (NCCL on GPUs; gloo with a CPU device in the tests)."""
+    if world == 1:
+        return v
+    import torch
+
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
 def run_reference(args, world):
     rank, _, _ = dist_env()
     if rank != 0:
@@ -390,12 +402,6 @@ def main():
         if world > 1:
             torch.distributed.barrier()
 
-    def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        return float(t.item())
 
     # ---- device-timed steps (inputs resident, no host reads inside) --------
     ext = torch.cuda.ExternalStream(rt.stream(), device=device)
@@ -417,7 +423,7 @@ def main():
         ev1.synchronize()
     rt.sync()
     barrier()
-    dev_s = max_over_ranks(ev0.elapsed_time(ev1) / 1e3)
+    dev_s = max_over_ranks(ev0.elapsed_time(ev1) / 1e3, world, device)
     kernels = rt.last_step_kernels()
     value = B * world * args.steps / dev_s
 
@@ -433,7 +439,7 @@ def main():
         rt.eval_batch(ids, cur, [pos] * B, LogitsMode.ARGMAX)
         cur, _ = rt.argmax_batch(B)
         pos += 1
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world, device)
     barrier()
 
     # ---- batch 1 on the same runtime (sequence 0) ---------------------------
@@ -449,7 +455,7 @@ def main():
         pos += 1
     e1.record(ext)
     e1.synchronize()
-    b1_s = max_over_ranks(e0.elapsed_time(e1) / 1e3)
+    b1_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, device)
     rt.close()
     del model
 
