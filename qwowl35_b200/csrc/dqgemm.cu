@@ -1,9 +1,9 @@
-// dqgemm.cu -- batched (B >= 16) fused dequantise-and-multiply on the 5th-gen
-// tensor cores (tcgen05, TMEM accumulators, TMA-fed weight stages).
+// dqgemm.cu -- batched (3 <= B <= 64) fused dequantise-and-multiply on the
+// 5th-gen tensor cores (tcgen05, TMEM accumulators, TMA-fed weight stages).
 //
-// Y[b][r] (+)= sum_k W[r][k] * X[b][k] for a decode batch of B sequences.  At
-// B >= 16 the weight stream is shared by B tokens, so the CUDA-core matvec
-// (matvec.cu) becomes FMA-bound; here each weight is decoded ONCE per launch
+// Y[b][r] (+)= sum_k W[r][k] * X[b][k] for a decode batch of B sequences.  The
+// CUDA-core matvec (matvec.cu) decodes the weights once per pair of batch
+// rows; from 3 rows on, decoding them ONCE per launch (here) into an f16 tile
 // into an f16 tile and multiplied against all B activation rows by
 // tcgen05.mma.  Reference semantics: the reference engine has no batched
 // decode; its multi-token path (qw35_kernel_mul_mm, qw35_tiled_mm.metal:36-255)
@@ -949,7 +949,7 @@ bool dq_supported(const MatvecArgs &a) {
     // norm weight 16 bytes at a time
     auto a16 = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
     // K % 256: GF4 chunks are 256 columns; Q8_0 scale boxes span two 128-column chunks
-    return a.batch >= 16 && a.batch <= 64 && (a.type_id == QW35_GF4_TYPE || a.type_id == QW35_Q8_0_TYPE) &&
+    return a.batch >= kDqMinBatch && a.batch <= 64 && (a.type_id == QW35_GF4_TYPE || a.type_id == QW35_Q8_0_TYPE) &&
            a.k % 256 == 0 &&
            a16(a.w0) && a16(a.w1) && a16(a.x) && a16(a.norm_w) && encode_fn() != nullptr &&
            !getenv("QW35_NO_TCGEN05");

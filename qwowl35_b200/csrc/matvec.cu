@@ -154,7 +154,7 @@ __device__ __forceinline__ float chunk_fast(const uint8_t *codes, const uint8_t 
 // Shared-memory carve-up (dynamic): [NM][kStages][stage_bytes] weights |
 // [2][G][B][NM][KW] partials | 64 floats scratch | 2*kStages mbarriers | abort.
 template <int CODEC, int B, int MODE, bool EXACT, typename XT>
-__global__ void __launch_bounds__(416, 1) mv_kernel(MvParams p) {
+__global__ void __launch_bounds__(544, 1) mv_kernel(MvParams p) {
     constexpr int NM = MODE == MV_SWIGLU ? 2 : 1;
     constexpr int NC = Codec<CODEC>::NC;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -406,12 +406,20 @@ static MvGeom mv_geometry(int rows, int K, const void *kern) {
     MvGeom g;
     const int nchunk = K / 32;
     g.kw = (nchunk + 31) / 32;
-    g.rs = g.kw >= 8 ? 1 : 8 / g.kw;
-    g.threads = (g.kw * g.rs + 1) * 32;
     codec_rows(CODEC, K, g.code_row, g.scale_row);
     const uint32_t rb = g.code_row + g.scale_row;
-    g.G = (int)(20 * 1024 / rb);
+    if (CODEC == QW35_GF4_TYPE) {
+        // GF4 decode is latency-heavy: ~16 consumer warps keep rows in flight
+        // (measured: gate/up pair 31.5 -> 28.2 us at B = 1)
+        g.rs = g.kw >= 16 ? 1 : 16 / g.kw;
+        g.G = (int)(32 * 1024 / NM / rb);  // <= 32 KB of weights per stage over all matrices
+    } else {
+        g.rs = g.kw >= 8 ? 1 : 8 / g.kw;
+        g.G = (int)(20 * 1024 / rb);
+    }
+    g.threads = (g.kw * g.rs + 1) * 32;
     g.G = g.G < 1 ? 1 : (g.G > 16 ? 16 : g.G);
+    if (CODEC == QW35_GF4_TYPE && g.G >= g.rs) g.G -= g.G % g.rs;  // whole rounds of the row slots
     g.stage_bytes = ((uint32_t)g.G * rb + 127u) & ~127u;
     g.smem = (size_t)NM * kStages * g.stage_bytes + (size_t)2 * g.G * B * NM * g.kw * 4 + 64 * 4 +
              2 * kStages * 8 + 16;
@@ -506,7 +514,7 @@ static MvParams base_params(const MatvecArgs &a, int b0) {
 // Batch rows beyond the register-resident tile of two are processed in tiles
 // of two; each tile re-reads the weights (from L2 when they fit).
 cudaError_t matvec_run(const MatvecArgs &a, cudaStream_t st) {
-    if (dq_supported(a)) return dq_run(a, a.mode, nullptr, nullptr, st);  // tensor-core path, B >= 16
+    if (dq_supported(a)) return dq_run(a, a.mode, nullptr, nullptr, st);  // tensor-core path, B >= kDqMinBatch
     for (int b0 = 0; b0 < a.batch; b0 += 2) {
         const int nb = a.batch - b0 < 2 ? a.batch - b0 : 2;
         MvParams p = base_params(a, b0);
@@ -532,7 +540,7 @@ size_t argmax_workspace_bytes(uint32_t rows, uint32_t batch) {
 cudaError_t argmax_head_run(const MatvecArgs &a, uint32_t *tok, float *val, void *ws, size_t ws_bytes,
                             cudaStream_t st) {
     if (ws_bytes < argmax_workspace_bytes(a.rows, a.batch)) return cudaErrorInvalidValue;
-    if (dq_supported(a)) return dq_run(a, 3, tok, val, st);  // tensor-core path, B >= 16
+    if (dq_supported(a)) return dq_run(a, 3, tok, val, st);  // tensor-core path, B >= kDqMinBatch
     const size_t half_ws = ws_bytes / 2;
     for (int b0 = 0; b0 < a.batch; b0 += 2) {
         const int nb = a.batch - b0 < 2 ? a.batch - b0 : 2;

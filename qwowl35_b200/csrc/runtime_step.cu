@@ -133,7 +133,7 @@ Runtime *create_runtime(std::shared_ptr<ModelStore> ms, uint32_t ctx, uint32_t v
     rt->attn_ws = dmalloc<uint8_t>(rt->attn_ws_bytes);
 
     // scratch of the batched tensor-core matvec, reserved before any graph capture
-    if (S >= 16) ck(dq_reserve((int)S, 12288, std::max<uint32_t>(vocab, F)), "reserve matvec scratch");
+    if (S >= (uint32_t)kDqMinBatch) ck(dq_reserve((int)S, 12288, std::max<uint32_t>(vocab, F)), "reserve matvec scratch");
 
     // RoPE ladder freq[i] = base^(-2i/n_rot) in fp32 (Qw35MetalRuntime.m:772-795)
     float freq[32];

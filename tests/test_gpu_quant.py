@@ -160,7 +160,7 @@ def test_no_device_wait_timed_out():
 
 # ---- batched (B >= 16) tensor-core path -----------------------------------------
 @pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE])
-@pytest.mark.parametrize("b", [16, 32, 64, 20])
+@pytest.mark.parametrize("b", [3, 8, 16, 32, 64, 20])
 @pytest.mark.parametrize("shape", [(12288, 4096), (4096, 12288), (333, 1280)])
 def test_batched_matvec_parity(t, b, shape):
     rows, k = shape

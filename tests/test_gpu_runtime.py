@@ -64,8 +64,7 @@ def test_prefill_chunk_equals_token_steps(small):
     rt.close()
 
 
-def test_batch_equals_single_sequence_bitwise(small):
-    seqs = [[3, 9, 27, 81], [100, 200, 300, 400], [4095, 0, 1, 2]]
+def _single_logits(small, seqs):
     single = []
     rt1 = Runtime(small, ctx=512)
     for s in seqs:
@@ -74,14 +73,35 @@ def test_batch_equals_single_sequence_bitwise(small):
             rt1.eval_token(tok, pos, LogitsMode.FULL)
         single.append(rt1.copy_logits())
     rt1.close()
+    return single
+
+
+def _batch_logits(small, seqs):
     rt = Runtime(small, ctx=512, max_seqs=4)
-    ids = [0] + [rt.seq_alloc() for _ in range(2)]
-    for pos in range(4):
-        rt.eval_batch(ids, [s[pos] for s in seqs], [pos] * 3, LogitsMode.FULL)
-    out = rt.copy_logits_batch(3)
-    for i in range(3):
-        np.testing.assert_array_equal(out[i], single[i])
+    ids = [0] + [rt.seq_alloc() for _ in range(len(seqs) - 1)]
+    for pos in range(len(seqs[0])):
+        rt.eval_batch(ids, [s[pos] for s in seqs], [pos] * len(seqs), LogitsMode.FULL)
+    out = rt.copy_logits_batch(len(seqs))
     rt.close()
+    return out
+
+
+def test_batch_of_two_equals_single_sequence_bitwise(small):
+    # batches of 1-2 run the CUDA-core matvecs, whose per-row arithmetic does not
+    # depend on the batch
+    seqs = [[3, 9, 27, 81], [100, 200, 300, 400]]
+    single, out = _single_logits(small, seqs), _batch_logits(small, seqs)
+    for i in range(2):
+        np.testing.assert_array_equal(out[i], single[i])
+
+
+def test_batch_of_three_matches_single_sequences(small):
+    # from 3 rows on, the matvecs run on the tensor cores (f16 hi + lo
+    # activations): the same results within the 1e-3 bar, not bit for bit
+    seqs = [[3, 9, 27, 81], [100, 200, 300, 400], [4095, 0, 1, 2]]
+    single, out = _single_logits(small, seqs), _batch_logits(small, seqs)
+    for i in range(3):
+        assert relerr(out[i], single[i].astype(np.float64)) < TOL
 
 
 def test_ragged_positions_in_one_batch(small):
@@ -150,14 +170,21 @@ def test_window_and_sink_match_oracle(small):
 
 
 def test_seq_fork_continues_identically(small):
+    # two rows run the CUDA-core matvecs: a fork continues bit for bit
     rt = Runtime(small, ctx=1024, max_seqs=3)
     b, c = rt.seq_alloc(), rt.seq_alloc()
     for pos in range(270):  # crosses a 256-position chunk boundary
         rt.eval_token((pos * 13) % 4096, pos, LogitsMode.NONE)
     rt.seq_fork(0, b)
-    rt.seq_fork(0, c)
-    rt.eval_batch([0, b, c], [5, 5, 5], [270, 270, 270], LogitsMode.FULL)
-    out = rt.copy_logits_batch(3)
+    rt.eval_batch([0, b], [5, 5], [270, 270], LogitsMode.FULL)
+    out = rt.copy_logits_batch(2)
     np.testing.assert_array_equal(out[0], out[1])
-    np.testing.assert_array_equal(out[0], out[2])
+    # three rows run on the tensor cores, whose split tiles are added in L2 in
+    # an order that may differ per batch column: equal within the 1e-3 bar
+    rt.seq_fork(0, c)
+    rt.seq_fork(0, b)
+    rt.eval_batch([0, b, c], [7, 7, 7], [271, 271, 271], LogitsMode.FULL)
+    out = rt.copy_logits_batch(3)
+    assert relerr(out[1], out[0].astype(np.float64)) < TOL
+    assert relerr(out[2], out[0].astype(np.float64)) < TOL
     rt.close()
