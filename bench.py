@@ -169,8 +169,8 @@ class ClockSampler:
 # DRAM bytes (read + write) per launch measured by ncu for a kernel class of the
 # table, from the capture summarised in profiles/ (see the file named per entry).
 NCU_TRAFFIC = {
-    # profiles/dq_kernel_gf4_gateup_b32.md: 54.075 MB read + 0.530 MB written
-    "gate_up_swiglu GF4 12288x4096": 54_605_312,
+    # profiles/dq_kernel_gf4_gateup_b32.md: DRAM read + write of one launch
+    "gate_up_swiglu GF4 12288x4096": 54618368,
 }
 
 
