@@ -29,6 +29,8 @@ extern "C" {
 #define QW35_TYPE_F16 1u
 #define QW35_TYPE_Q8_0 8u
 #define QW35_TYPE_Q4_K 12u
+#define QW35_TYPE_Q5_K 13u
+#define QW35_TYPE_Q6_K 14u
 #define QW35_TYPE_GF4 100u
 
 // Matvec flags.  Default GF4 decode is bit-exact with the reference decode

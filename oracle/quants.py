@@ -17,10 +17,20 @@ Formats (GGUF type ids as the reference's loader uses them,
   weight = d*sc_j*q - dmin*m_j.
   Reference: ``qw35_types.metal:2-7``, ``:70-83``, ``qw35_matvec.metal:2-12``;
   gguf-py ``Q4_K.dequantize_blocks``.
+* Q5_K (type 13): 176-byte blocks ``{f16 d; f16 dmin; u8 scales[12]; u8 qh[32];
+  u8 qs[128]}``; Q4_K's sub-blocks with a fifth code bit (bit j of qh[l] for
+  sub-block j), weight = d*sc_j*(q + 16 h) - dmin*m_j.
+  Reference: ``qw35_types.metal:9-15``, ``qw35_matvec.metal:41-64``;
+  gguf-py ``Q5_K.dequantize_blocks``.
+* Q6_K (type 14): 210-byte blocks ``{u8 ql[128]; u8 qh[64]; i8 scales[16];
+  f16 d}``; sixteen 16-weight sub-blocks, weight = d*sc_j*(q6 - 32).
+  Reference: ``qw35_types.metal:17-22``, ``qw35_matvec.metal:66-98``,
+  ``qw35_output.metal:2-139`` (the fused argmax head); gguf-py
+  ``Q6_K.dequantize_blocks``.
 
 All dequantisers return float32 and are bit-exact with the reference's
 arithmetic (every product involved is exact in fp32; the single rounding is
-the final subtraction in Q4_K, done in the same order as gguf-py).
+the final subtraction in Q4_K / Q5_K, done in the same order as gguf-py).
 """
 from __future__ import annotations
 
@@ -29,9 +39,12 @@ import numpy as np
 GF4_TYPE = 100
 Q8_0_TYPE = 8
 Q4_K_TYPE = 12
+Q5_K_TYPE = 13
+Q6_K_TYPE = 14
 F32_TYPE = 0
 
-BLOCK = {GF4_TYPE: (8, 4), Q8_0_TYPE: (32, 34), Q4_K_TYPE: (256, 144)}
+BLOCK = {GF4_TYPE: (8, 4), Q8_0_TYPE: (32, 34), Q4_K_TYPE: (256, 144), Q5_K_TYPE: (256, 176),
+         Q6_K_TYPE: (256, 210)}
 
 
 def row_bytes(type_id: int, k: int) -> int:
@@ -184,6 +197,60 @@ def q4_k_dequant(raw: np.ndarray, rows: int, k: int) -> np.ndarray:
     return out.reshape(rows, k)
 
 
+# --------------------------------------------------------------------------
+# Q5_K (qw35_types.metal:9-15; qw35_matvec.metal:41-64)
+# --------------------------------------------------------------------------
+def q5_k_codes(b: np.ndarray) -> np.ndarray:
+    """[n,176] blocks -> [n,256] 5-bit codes: element 32j+l = nibble (j even: low,
+    j odd: high) of qs[32(j//2)+l] plus 16 * bit j of qh[l]."""
+    qh, qs = b[:, 16:48], b[:, 48:176]
+    out = np.empty((b.shape[0], 256), dtype=np.uint8)
+    for j in range(8):
+        grp = qs[:, (j // 2) * 32:(j // 2) * 32 + 32]
+        lo = (grp & 0x0F) if (j % 2 == 0) else (grp >> 4)
+        out[:, j * 32:(j + 1) * 32] = lo | (((qh >> j) & 1) << 4)
+    return out
+
+
+def q5_k_dequant(raw: np.ndarray, rows: int, k: int) -> np.ndarray:
+    b = np.asarray(raw, dtype=np.uint8).reshape(rows * (k // 256), 176)
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)
+    dmin = b[:, 2:4].copy().view(np.float16).astype(np.float32)
+    sc, mn = q4_k_scale_min(b[:, 4:16])
+    q = q5_k_codes(b).astype(np.float32).reshape(-1, 8, 32)
+    dl = (d * sc.astype(np.float32))[:, :, None]
+    ml = (dmin * mn.astype(np.float32))[:, :, None]
+    return (dl * q - ml).reshape(rows, k)
+
+
+# --------------------------------------------------------------------------
+# Q6_K (qw35_types.metal:17-22; qw35_matvec.metal:66-98, :458-542)
+# --------------------------------------------------------------------------
+def q6_k_codes(b: np.ndarray) -> np.ndarray:
+    """[n,210] blocks -> [n,256] unsigned 6-bit codes (weight uses code - 32).
+    In each 128-element half h, element 128h+32m+l takes the low (m < 2) or
+    high (m >= 2) nibble of ql[64h + 32(m&1) + l] and bits 2m..2m+1 of
+    qh[32h + l]."""
+    ql, qh = b[:, 0:128], b[:, 128:192]
+    out = np.empty((b.shape[0], 256), dtype=np.uint8)
+    for h in range(2):
+        for m in range(4):
+            src = ql[:, 64 * h + 32 * (m & 1):64 * h + 32 * (m & 1) + 32]
+            lo = (src & 0x0F) if m < 2 else (src >> 4)
+            hi = (qh[:, 32 * h:32 * h + 32] >> (2 * m)) & 3
+            out[:, 128 * h + 32 * m:128 * h + 32 * m + 32] = lo | (hi << 4)
+    return out
+
+
+def q6_k_dequant(raw: np.ndarray, rows: int, k: int) -> np.ndarray:
+    b = np.asarray(raw, dtype=np.uint8).reshape(rows * (k // 256), 210)
+    sc = b[:, 192:208].copy().view(np.int8).astype(np.float32)
+    d = b[:, 208:210].copy().view(np.float16).astype(np.float32)
+    dl = (d * sc)[:, :, None]                                     # exact in fp32
+    q = (q6_k_codes(b).astype(np.float32) - 32.0).reshape(-1, 16, 16)
+    return (dl * q).reshape(rows, k)
+
+
 def dequant(type_id: int, raw: np.ndarray, rows: int, k: int, gf4_exact: bool = False,
             gf4_half: bool = False) -> np.ndarray:
     if type_id == GF4_TYPE:
@@ -192,6 +259,10 @@ def dequant(type_id: int, raw: np.ndarray, rows: int, k: int, gf4_exact: bool = 
         return q8_0_dequant(raw, rows, k)
     if type_id == Q4_K_TYPE:
         return q4_k_dequant(raw, rows, k)
+    if type_id == Q5_K_TYPE:
+        return q5_k_dequant(raw, rows, k)
+    if type_id == Q6_K_TYPE:
+        return q6_k_dequant(raw, rows, k)
     if type_id == F32_TYPE:
         return np.asarray(raw).view(np.float32).reshape(rows, k)
     raise ValueError(f"unsupported type {type_id}")
@@ -228,6 +299,24 @@ def gen_q4_k(rng: np.random.Generator, rows: int, k: int, d_div: float = 1.0) ->
     return out.reshape(-1)
 
 
+def gen_q5_k(rng: np.random.Generator, rows: int, k: int, d_div: float = 1.0) -> np.ndarray:
+    """Q5_K blocks: fp16 d, dmin = |N(0,0.02)|/d_div / 2; scales, mins, qh and qs uniform."""
+    nb = rows * (k // 256)
+    out = rng.integers(0, 256, size=(nb, 176), dtype=np.uint16).astype(np.uint8)
+    out[:, 0:2] = (np.abs(rng.normal(0.0, 0.01, size=nb)) / d_div).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    out[:, 2:4] = (np.abs(rng.normal(0.0, 0.01, size=nb)) / d_div).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    return out.reshape(-1)
+
+
+def gen_q6_k(rng: np.random.Generator, rows: int, k: int, d_div: float = 1.0) -> np.ndarray:
+    """Q6_K blocks: ql/qh uniform, int8 scales uniform in [-64, 63], d = fp16(|N(0,0.001)|/d_div)."""
+    nb = rows * (k // 256)
+    out = rng.integers(0, 256, size=(nb, 210), dtype=np.uint16).astype(np.uint8)
+    out[:, 192:208] = rng.integers(-64, 64, size=(nb, 16)).astype(np.int8).view(np.uint8)
+    out[:, 208:210] = (np.abs(rng.normal(0.0, 0.001, size=nb)) / d_div).astype(np.float16).view(np.uint8).reshape(nb, 2)
+    return out.reshape(-1)
+
+
 def gen_weight(rng: np.random.Generator, type_id: int, rows: int, k: int, d_div: float = 1.0) -> np.ndarray:
     """Raw GGUF-layout bytes (uint8) of a synthetic weight."""
     if type_id == GF4_TYPE:
@@ -236,4 +325,8 @@ def gen_weight(rng: np.random.Generator, type_id: int, rows: int, k: int, d_div:
         return gen_q8_0(rng, rows, k, d_div)
     if type_id == Q4_K_TYPE:
         return gen_q4_k(rng, rows, k, d_div)
+    if type_id == Q5_K_TYPE:
+        return gen_q5_k(rng, rows, k, d_div)
+    if type_id == Q6_K_TYPE:
+        return gen_q6_k(rng, rows, k, d_div)
     raise ValueError(type_id)

@@ -8,12 +8,29 @@
 #define QW35_GF4_TYPE 100u
 #define QW35_Q8_0_TYPE 8u
 #define QW35_Q4_K_TYPE 12u
+#define QW35_Q5_K_TYPE 13u
+#define QW35_Q6_K_TYPE 14u
 #define QW35_F32_TYPE 0u
 #define QW35_F16_TYPE 1u
 
 namespace qw35 {
 
 constexpr int kWarp = 32;
+
+// Device layout of the K-quants with a fifth/sixth code bit, per row of k
+// weights (k % 256 == 0):
+//   Q5_K codes plane row: k/2 bytes of element-ordered nibbles, then k/8 bytes
+//        of high bits, one uint32 per 32-weight sub-block j: bit 4n + w holds
+//        the high bit of element 8w + n of the sub-block (w = 0..3, n = 0..7).
+//        Header plane row: the 16-byte {d, dmin, scales[12]} of each block.
+//   Q6_K codes plane row: k/2 bytes of element-ordered low nibbles, then k/4
+//        bytes of high bit pairs, one uint32 per 16 weights: bits 4n..4n+1 hold
+//        element n's pair, bits 4n+2..4n+3 element 8+n's.
+//        Scales plane row (q6k_scale_row bytes): k/16 int8 sub-block scales,
+//        then the k/256 f16 block scales d, zero-padded to 16 bytes.
+// The two-bits-per-nibble-slot placement lets the matvec decode a high part
+// with the same shift-and-mask steps as a nibble.
+__host__ __device__ constexpr uint32_t q6k_scale_row(uint32_t k) { return (k / 16 + k / 128 + 15u) & ~15u; }
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

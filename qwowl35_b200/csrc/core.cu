@@ -97,6 +97,67 @@ __global__ void repack_q4_k_kernel(const uint8_t *src, uint8_t *dst, size_t nblk
     }
 }
 
+// GGUF code of element e of a Q5_K block (qw35_matvec.metal:41-64): nibble of
+// qs[32(j/2) + l] (low for even sub-block j) plus 16 * bit j of qh[l].
+__device__ __forceinline__ uint32_t q5k_code(const uint8_t *s, int e) {
+    const int j = e >> 5, l = e & 31;
+    const uint8_t byte = s[48 + 32 * (j >> 1) + l];
+    const uint32_t lo = (j & 1) ? (byte >> 4) : (byte & 0xfu);
+    return lo | (((uint32_t)(s[16 + l] >> j) & 1u) << 4);
+}
+
+// GGUF code of element e of a Q6_K block (qw35_matvec.metal:66-98): element
+// 128h + 32m + l takes a nibble of ql[64h + 32(m&1) + l] (high for m >= 2) and
+// bits 2m..2m+1 of qh[32h + l].
+__device__ __forceinline__ uint32_t q6k_code(const uint8_t *s, int e) {
+    const int h = e >> 7, m = (e >> 5) & 3, l = e & 31;
+    const uint8_t byte = s[64 * h + 32 * (m & 1) + l];
+    const uint32_t lo = m < 2 ? (byte & 0xfu) : (byte >> 4);
+    return lo | ((((uint32_t)s[128 + 32 * h + l] >> (2 * m)) & 3u) << 4);
+}
+
+// Q5_K / Q6_K: one thread per 256-weight block, into the layout described in
+// common.cuh (element-ordered nibbles, high parts in nibble slots).
+template <int TYPE>
+__global__ void repack_k56_kernel(const uint8_t *src, uint8_t *dst, size_t nblk, size_t rows, uint32_t k) {
+    const size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblk) return;
+    const uint32_t nbr = k / 256;
+    const size_t r = b / nbr;
+    const uint32_t bi = (uint32_t)(b % nbr);
+    constexpr uint32_t kBlk = TYPE == QW35_Q5_K_TYPE ? 176 : 210;
+    const uint8_t *s = src + b * kBlk;
+    const size_t code_row = TYPE == QW35_Q5_K_TYPE ? (size_t)k / 2 + k / 8 : (size_t)k / 2 + k / 4;
+    uint8_t *row = dst + r * code_row;
+    uint32_t code[256];
+#pragma unroll 4
+    for (int e = 0; e < 256; ++e) code[e] = TYPE == QW35_Q5_K_TYPE ? q5k_code(s, e) : q6k_code(s, e);
+    for (int j = 0; j < 128; ++j) row[bi * 128 + j] = (uint8_t)((code[2 * j] & 15u) | ((code[2 * j + 1] & 15u) << 4));
+    uint32_t *hw = reinterpret_cast<uint32_t *>(row + k / 2);
+    if (TYPE == QW35_Q5_K_TYPE) {
+        for (int j = 0; j < 8; ++j) {  // sub-block j: bit 4n + w <- element 32j + 8w + n
+            uint32_t v = 0;
+            for (int w = 0; w < 4; ++w)
+                for (int n = 0; n < 8; ++n) v |= (code[32 * j + 8 * w + n] >> 4) << (4 * n + w);
+            hw[bi * 8 + j] = v;
+        }
+        uint8_t *hdr = dst + rows * code_row + b * 16;
+        for (int i = 0; i < 16; ++i) hdr[i] = s[i];
+    } else {
+        for (int t = 0; t < 16; ++t) {  // 16 weights: bits 4n.. <- element n, 4n+2.. <- element 8+n
+            uint32_t v = 0;
+            for (int n = 0; n < 8; ++n) v |= ((code[16 * t + n] >> 4) << (4 * n)) | ((code[16 * t + 8 + n] >> 4) << (4 * n + 2));
+            hw[bi * 16 + t] = v;
+        }
+        uint8_t *sr = dst + rows * code_row + r * q6k_scale_row(k);
+        for (int i = 0; i < 16; ++i) sr[bi * 16 + i] = s[192 + i];
+        sr[k / 16 + 2 * bi] = s[208];
+        sr[k / 16 + 2 * bi + 1] = s[209];
+        if (bi == 0)
+            for (uint32_t i = k / 16 + k / 128; i < q6k_scale_row(k); ++i) sr[i] = 0;
+    }
+}
+
 cudaError_t weight_repack(uint32_t type_id, const void *src, void *dst, uint32_t rows, uint32_t k, cudaStream_t st) {
     const uint8_t *s = static_cast<const uint8_t *>(src);
     uint8_t *d = static_cast<uint8_t *>(dst);
@@ -115,6 +176,13 @@ cudaError_t weight_repack(uint32_t type_id, const void *src, void *dst, uint32_t
     if (type_id == QW35_Q4_K_TYPE) {
         const size_t nb = (size_t)rows * (k / 256);
         repack_q4_k_kernel<<<(unsigned)((nb + 127) / 128), 128, 0, st>>>(s, d, nb, rows, k);
+        return cudaGetLastError();
+    }
+    if (type_id == QW35_Q5_K_TYPE || type_id == QW35_Q6_K_TYPE) {
+        const size_t nb = (size_t)rows * (k / 256);
+        const unsigned grid = (unsigned)((nb + 63) / 64);
+        if (type_id == QW35_Q5_K_TYPE) repack_k56_kernel<QW35_Q5_K_TYPE><<<grid, 64, 0, st>>>(s, d, nb, rows, k);
+        else repack_k56_kernel<QW35_Q6_K_TYPE><<<grid, 64, 0, st>>>(s, d, nb, rows, k);
         return cudaGetLastError();
     }
     return cudaErrorInvalidValue;
@@ -140,6 +208,31 @@ __device__ __forceinline__ float dequant_at(uint32_t type_id, const uint8_t *w, 
         float dl, ml;
         q4k_scale_min(h, (int)((c % 256) / 32), dl, ml);
         return dl * (float)q - ml;
+    }
+    if (type_id == QW35_Q5_K_TYPE) {
+        const uint8_t *row = w + r * ((size_t)k / 2 + k / 8);
+        const uint8_t byte = row[c / 2];
+        const uint32_t lo = (c & 1) ? (byte >> 4) : (byte & 0xf);
+        const uint32_t hw = reinterpret_cast<const uint32_t *>(row + k / 2)[c / 32];
+        const uint32_t e = c & 31;
+        const uint32_t q = lo | (((hw >> (4 * (e & 7) + (e >> 3))) & 1u) << 4);
+        const uint4 h = *reinterpret_cast<const uint4 *>(w + rows * ((size_t)k / 2 + k / 8) + (r * (k / 256) + c / 256) * 16);
+        float dl, ml;
+        q4k_scale_min(h, (int)((c % 256) / 32), dl, ml);
+        return dl * (float)q - ml;  // d*sc*q is exact: one rounding, as gguf-py
+    }
+    if (type_id == QW35_Q6_K_TYPE) {
+        const size_t code_row = (size_t)k / 2 + k / 4;
+        const uint8_t *row = w + r * code_row;
+        const uint8_t byte = row[c / 2];
+        const uint32_t lo = (c & 1) ? (byte >> 4) : (byte & 0xf);
+        const uint32_t hw = reinterpret_cast<const uint32_t *>(row + k / 2)[c / 16];
+        const uint32_t e = c & 15;
+        const uint32_t q = lo | (((hw >> (4 * (e & 7) + 2 * (e >> 3))) & 3u) << 4);
+        const uint8_t *sr = w + rows * code_row + r * q6k_scale_row(k);
+        const float sc = (float)reinterpret_cast<const int8_t *>(sr)[c / 16];
+        const float d = __half2float(__ushort_as_half(reinterpret_cast<const unsigned short *>(sr + k / 16)[c / 256]));
+        return (d * sc) * (float)((int)q - 32);  // both products exact in fp32
     }
     return reinterpret_cast<const float *>(w)[r * k + c];
 }

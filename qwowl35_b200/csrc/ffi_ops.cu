@@ -18,7 +18,10 @@ int cuda_ok(cudaError_t e, const char *what, char *err, uintptr_t len) {
     return 0;
 }
 
-bool type_ok(uint32_t t) { return t == QW35_GF4_TYPE || t == QW35_Q8_0_TYPE || t == QW35_Q4_K_TYPE; }
+bool type_ok(uint32_t t) {
+    return t == QW35_GF4_TYPE || t == QW35_Q8_0_TYPE || t == QW35_Q4_K_TYPE || t == QW35_Q5_K_TYPE ||
+           t == QW35_Q6_K_TYPE;
+}
 
 int check_shape(uint32_t type_id, uint32_t rows, uint32_t k, uint32_t batch, char *err, uintptr_t len) {
     if (!type_ok(type_id)) {
@@ -62,6 +65,8 @@ uint64_t qw35_cuda_weight_bytes(uint32_t type_id, uint32_t rows, uint32_t k) {
         case QW35_GF4_TYPE: return (uint64_t)rows * (k / 8) * 4;
         case QW35_Q8_0_TYPE: return (uint64_t)rows * (k / 32) * 34;
         case QW35_Q4_K_TYPE: return (uint64_t)rows * (k / 256) * 144;
+        case QW35_Q5_K_TYPE: return (uint64_t)rows * (k / 256) * 176;
+        case QW35_Q6_K_TYPE: return (uint64_t)rows * (k / 256) * 210;
         case QW35_F32_TYPE: return (uint64_t)rows * k * 4;
         default: return 0;
     }
@@ -71,6 +76,8 @@ uint64_t qw35_cuda_device_bytes(uint32_t type_id, uint32_t rows, uint32_t k) {
     const uint64_t raw = qw35_cuda_weight_bytes(type_id, rows, k);
     // Q8_0 carries one exponent byte per row after its scales plane (16-byte padded)
     if (type_id == QW35_Q8_0_TYPE && raw) return raw + (((uint64_t)rows + 15) & ~(uint64_t)15);
+    // Q6_K rows of scales (k/16 int8 + k/128 bytes of f16 d) are padded to 16 bytes
+    if (type_id == QW35_Q6_K_TYPE && raw) return (uint64_t)rows * (3 * (k / 4) + qw35::q6k_scale_row(k));
     return raw;
 }
 

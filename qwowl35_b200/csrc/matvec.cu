@@ -1,4 +1,4 @@
-// matvec.cu -- fused dequantise-and-multiply for GF4 / Q8_0 / Q4_K on sm_100a.
+// matvec.cu -- fused dequantise-and-multiply for GF4 / Q8_0 / Q4_K / Q5_K / Q6_K on sm_100a.
 //
 // Replaces the reference's decode matvec family:
 //   qw35_decode_matmul_gf4_2row[_residual]_f32   qw35_gf4.metal:99-136, :209-246
@@ -6,6 +6,9 @@
 //   qw35_output_gf4_argmax_partials_16row_f32    qw35_gf4.metal:140-206
 //   qw35_decode_matmul_q8_0[_residual]_f32       qw35_matvec.metal:630-683
 //   qw35_decode_matmul_q4_k_2row[_residual]_f32  qw35_matvec.metal:171-353
+//   qw35_decode_matmul_q5_k_2row_f32             qw35_matvec.metal:355-456
+//   qw35_decode_matmul_q6_k_llama[_residual]_f32 qw35_matvec.metal:458-628
+//   qw35_output_q6_k_argmax_partials_16row_f32   qw35_output.metal:2-139
 //   qw35_output_argmax_reduce_partials_f32       qw35_output.metal:141-182
 //   qw35_rms_norm_weight_f32 (fused as a prologue) qw35_core.metal:14-48
 //
@@ -51,6 +54,8 @@ template <int CODEC> struct Codec;
 template <> struct Codec<QW35_GF4_TYPE> { static constexpr int NC = 8; };   // per-lane constants per b
 template <> struct Codec<QW35_Q8_0_TYPE> { static constexpr int NC = 1; };
 template <> struct Codec<QW35_Q4_K_TYPE> { static constexpr int NC = 2; };
+template <> struct Codec<QW35_Q5_K_TYPE> { static constexpr int NC = 2; };
+template <> struct Codec<QW35_Q6_K_TYPE> { static constexpr int NC = 2; };  // one per 16-weight sub-block
 
 template <typename XT>
 __device__ __forceinline__ void load_x32(float *dst, const XT *src) {
@@ -99,6 +104,20 @@ __device__ __forceinline__ void prep_x(float *xs, float *cst) {
         }
     } else if constexpr (CODEC == QW35_Q8_0_TYPE) {
         cst[0] = 0.0f;
+    } else if constexpr (CODEC == QW35_Q6_K_TYPE) {
+        // per 16-weight sub-block: low and high passes each add sum(xs); the
+        // code offset of -32 adds 32 * sum(x)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float s = 0.0f, sx = 0.0f;
+#pragma unroll
+            for (int i = 16 * h; i < 16 * h + 16; ++i) {
+                s += xs[i];
+                xs[i] *= q4_xscale(i & 7);
+                sx += xs[i];
+            }
+            cst[h] = 17.0f * sx + 32.0f * s;
+        }
     } else {
         float s = 0.0f, sx = 0.0f;
 #pragma unroll
@@ -107,7 +126,7 @@ __device__ __forceinline__ void prep_x(float *xs, float *cst) {
             xs[i] *= q4_xscale(i & 7);
             sx += xs[i];
         }
-        cst[0] = sx;
+        cst[0] = CODEC == QW35_Q5_K_TYPE ? 17.0f * sx : sx;  // Q5_K: low + 16 x high pass
         cst[1] = s;
     }
 }
@@ -115,7 +134,7 @@ __device__ __forceinline__ void prep_x(float *xs, float *cst) {
 // Dot of the lane's chunk of one row (weights in shared memory) with x.
 template <int CODEC, bool EXACT>
 __device__ __forceinline__ float chunk_fast(const uint8_t *codes, const uint8_t *scales, int c, const float *xs,
-                                            const float *cst) {
+                                            const float *cst, int K) {
     if constexpr (CODEC == QW35_GF4_TYPE) {
         const uint4 w = *reinterpret_cast<const uint4 *>(codes + c * 16);
         float r = gf4_word_fast<EXACT>(w.x, xs + 0, cst[0], cst[4], 0.0f);
@@ -137,6 +156,43 @@ __device__ __forceinline__ float chunk_fast(const uint8_t *codes, const uint8_t 
         acc = q8_word_fast(b.z, xs + 24, acc);
         acc = q8_word_fast(b.w, xs + 28, acc);
         return acc * __half2float(__ushort_as_half(sb));
+    } else if constexpr (CODEC == QW35_Q5_K_TYPE) {
+        // chunk c is sub-block c & 7 of block c >> 3; the high bits of word w
+        // sit at bit w of each nibble slot of one uint32
+        const uint4 w = *reinterpret_cast<const uint4 *>(codes + c * 16);
+        const uint32_t hb = *reinterpret_cast<const uint32_t *>(codes + K / 2 + c * 4);
+        const uint4 h = *reinterpret_cast<const uint4 *>(scales + (c >> 3) * 16);
+        float dl, ml;
+        q4k_scale_min(h, c & 7, dl, ml);
+        constexpr uint32_t M1 = 0x11111111u;
+        float acc = -cst[0], hacc = 0.0f;
+        acc = q4_word_fast(w.x, xs + 0, acc);
+        acc = q4_word_fast(w.y, xs + 8, acc);
+        acc = q4_word_fast(w.z, xs + 16, acc);
+        acc = q4_word_fast(w.w, xs + 24, acc);
+        hacc = q4_word_fast(hb & M1, xs + 0, hacc);
+        hacc = q4_word_fast((hb >> 1) & M1, xs + 8, hacc);
+        hacc = q4_word_fast((hb >> 2) & M1, xs + 16, hacc);
+        hacc = q4_word_fast((hb >> 3) & M1, xs + 24, hacc);
+        return dl * fmaf(16.0f, hacc, acc) - ml * cst[1];
+    } else if constexpr (CODEC == QW35_Q6_K_TYPE) {
+        // chunk c = sub-blocks 2c, 2c+1; high pairs of 16 weights per uint32
+        const uint4 w = *reinterpret_cast<const uint4 *>(codes + c * 16);
+        const uint2 hb = *reinterpret_cast<const uint2 *>(codes + K / 2 + c * 8);
+        const uint32_t sc2 = *reinterpret_cast<const unsigned short *>(scales + c * 2);
+        const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(scales + K / 16 + (c >> 3) * 2)));
+        constexpr uint32_t M2 = 0x33333333u;
+        float a0 = -cst[0], a1 = -cst[1], h0 = 0.0f, h1 = 0.0f;
+        a0 = q4_word_fast(w.x, xs + 0, a0);
+        a0 = q4_word_fast(w.y, xs + 8, a0);
+        a1 = q4_word_fast(w.z, xs + 16, a1);
+        a1 = q4_word_fast(w.w, xs + 24, a1);
+        h0 = q4_word_fast(hb.x & M2, xs + 0, h0);
+        h0 = q4_word_fast((hb.x >> 2) & M2, xs + 8, h0);
+        h1 = q4_word_fast(hb.y & M2, xs + 16, h1);
+        h1 = q4_word_fast((hb.y >> 2) & M2, xs + 24, h1);
+        const float s0 = (float)(int8_t)(sc2 & 0xffu), s1 = (float)(int8_t)(sc2 >> 8);
+        return d * fmaf(s0, fmaf(16.0f, h0, a0), s1 * fmaf(16.0f, h1, a1));
     } else {
         const uint4 w = *reinterpret_cast<const uint4 *>(codes + c * 16);
         const uint4 h = *reinterpret_cast<const uint4 *>(scales + (c >> 3) * 16);
@@ -296,7 +352,7 @@ __global__ void __launch_bounds__(544, 1) mv_kernel(MvParams p) {
                 const uint8_t *scales = st + (size_t)G * p.code_row + (size_t)i * p.scale_row;
 #pragma unroll
                 for (int b = 0; b < B; ++b)
-                    acc[m][b] = (active && i < nr) ? chunk_fast<CODEC, EXACT>(codes, scales, c, xs[b], cst[b]) : 0.0f;
+                    acc[m][b] = (active && i < nr) ? chunk_fast<CODEC, EXACT>(codes, scales, c, xs[b], cst[b], p.K) : 0.0f;
             }
 #pragma unroll
             for (int m = 0; m < NM; ++m)
@@ -397,6 +453,8 @@ struct MvGeom {
 static void codec_rows(uint32_t type_id, int K, uint32_t &code_row, uint32_t &scale_row) {
     if (type_id == QW35_GF4_TYPE) { code_row = K / 2; scale_row = 0; }
     else if (type_id == QW35_Q8_0_TYPE) { code_row = K; scale_row = K / 16; }
+    else if (type_id == QW35_Q5_K_TYPE) { code_row = K / 2 + K / 8; scale_row = K / 16; }
+    else if (type_id == QW35_Q6_K_TYPE) { code_row = K / 2 + K / 4; scale_row = q6k_scale_row(K); }
     else { code_row = K / 2; scale_row = K / 16; }
 }
 
@@ -482,6 +540,8 @@ static cudaError_t mv_dispatch_codec(uint32_t type_id, MvParams p, int B, cudaSt
         case QW35_GF4_TYPE: return mv_dispatch_b<QW35_GF4_TYPE, MODE, EXACT, XT>(p, B, st, ctas);
         case QW35_Q8_0_TYPE: return mv_dispatch_b<QW35_Q8_0_TYPE, MODE, true, XT>(p, B, st, ctas);
         case QW35_Q4_K_TYPE: return mv_dispatch_b<QW35_Q4_K_TYPE, MODE, true, XT>(p, B, st, ctas);
+        case QW35_Q5_K_TYPE: return mv_dispatch_b<QW35_Q5_K_TYPE, MODE, true, XT>(p, B, st, ctas);
+        case QW35_Q6_K_TYPE: return mv_dispatch_b<QW35_Q6_K_TYPE, MODE, true, XT>(p, B, st, ctas);
         default: return cudaErrorInvalidValue;
     }
 }

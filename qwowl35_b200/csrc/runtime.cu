@@ -101,7 +101,8 @@ struct Loader {
             const uint64_t tk = t.d->dims[0], tr = t.d->n_dims >= 2 ? t.d->dims[1] : 1;
             if (i == 0) { type = t.d->type_id; k = tk; }
             if (t.d->type_id != type || tk != k) fail("%s: mixed type/K in a fused projection", names[i].c_str());
-            if (t.d->type_id != QW35_GF4_TYPE && t.d->type_id != QW35_Q8_0_TYPE && t.d->type_id != QW35_Q4_K_TYPE)
+            if (t.d->type_id != QW35_GF4_TYPE && t.d->type_id != QW35_Q8_0_TYPE && t.d->type_id != QW35_Q4_K_TYPE &&
+                t.d->type_id != QW35_Q5_K_TYPE && t.d->type_id != QW35_Q6_K_TYPE)
                 fail("%s: unsupported weight type %u", names[i].c_str(), t.d->type_id);
             if (t.d->bytes != tbytes(type, tr, tk)) fail("%s: byte size does not match its type", names[i].c_str());
             rows += tr;
@@ -159,7 +160,7 @@ std::shared_ptr<ModelStore> load_model(const void *map, uint64_t map_size, const
     const uint32_t interval = hp.full_attention_interval ? hp.full_attention_interval : 4;
 
     ms->tok_embd = L.matrix("token_embd.weight", H, vocab);
-    if (ms->tok_embd.type_id == QW35_GF4_TYPE) fail("token_embd.weight must be q8_0 or q4_k");
+    if (ms->tok_embd.type_id == QW35_GF4_TYPE) fail("token_embd.weight must be a block (q8_0 / q4_k / q5_k / q6_k) type");
     ms->output = L.matrix("output.weight", H, vocab);
     ms->output_norm = L.f32("output_norm.weight", H);
 

@@ -10,7 +10,7 @@ import torch
 
 from ._lib import call, lib
 
-GF4, Q8_0, Q4_K = 100, 8, 12
+GF4, Q8_0, Q4_K, Q5_K, Q6_K = 100, 8, 12, 13, 14
 EXACT = 1
 
 

@@ -6,15 +6,17 @@ container).  Sources of truth:
 
 * GF4: the reference's own cooker, ``tools/qw35_cook_common.py``
   (``pack_gf4_prepared``, ``_gf4_quantize_with_scale``, ``e5m2_byte_to_fp32``).
-* Q8_0 / Q4_K: gguf-py 0.19.0 ``gguf.quants`` (``Q8_0.quantize_blocks`` /
-  ``dequantize_blocks``, ``Q4_K.dequantize_blocks``), the third-party library
+* Q8_0 / Q4_K / Q5_K / Q6_K: gguf-py 0.19.0 ``gguf.quants``
+  (``Q8_0.quantize_blocks`` / ``dequantize_blocks``, ``Q4_K`` / ``Q5_K`` /
+  ``Q6_K.dequantize_blocks``), the third-party library
   the reference's tools call (``qw35_cook_common.py:34-35``, ``:155-179``).
 
 Usage::
 
     python tests/golden/make_golden.py /path/to/reference
 
-Writes ``gf4.npz``, ``q8_0.npz``, ``q4_k.npz`` beside this script.
+Writes ``gf4.npz``, ``q8_0.npz``, ``q4_k.npz``, ``q5_k.npz``, ``q6_k.npz`` beside
+this script.
 """
 from __future__ import annotations
 
@@ -27,7 +29,7 @@ import numpy as np
 def main(ref_root: str) -> None:
     sys.path.insert(0, str(Path(ref_root) / "tools"))
     import qw35_cook_common as cc  # the reference's own module
-    from gguf.quants import Q4_K, Q8_0
+    from gguf.quants import Q4_K, Q5_K, Q6_K, Q8_0
     import gguf
 
     out_dir = Path(__file__).resolve().parent
@@ -76,6 +78,20 @@ def main(ref_root: str) -> None:
     q4[:, 2:4] = np.abs(rng.normal(0, 0.02, size=(nb, 1))).astype(np.float16).view(np.uint8)
     q4_deq = Q4_K.dequantize_blocks(q4).reshape(16, 1024).astype(np.float32)
     np.savez_compressed(out_dir / "q4_k.npz", raw=q4.reshape(-1), deq=q4_deq)
+
+    # ---- Q5_K: random blocks with finite d/dmin ------------------------------
+    q5 = rng.integers(0, 256, size=(nb, 176), dtype=np.uint16).astype(np.uint8)
+    q5[:, 0:2] = np.abs(rng.normal(0, 0.02, size=(nb, 1))).astype(np.float16).view(np.uint8)
+    q5[:, 2:4] = np.abs(rng.normal(0, 0.02, size=(nb, 1))).astype(np.float16).view(np.uint8)
+    q5_deq = Q5_K.dequantize_blocks(q5).reshape(16, 1024).astype(np.float32)
+    np.savez_compressed(out_dir / "q5_k.npz", raw=q5.reshape(-1), deq=q5_deq)
+
+    # ---- Q6_K: random blocks (signed scales, signed finite d); gguf-py 0.19.0
+    # has no Q6_K quantizer, so the fixture pins the dequantiser only ---------
+    q6 = rng.integers(0, 256, size=(nb, 210), dtype=np.uint16).astype(np.uint8)
+    q6[:, 208:210] = rng.normal(0, 0.002, size=(nb, 1)).astype(np.float16).view(np.uint8)
+    q6_deq = Q6_K.dequantize_blocks(q6).reshape(16, 1024).astype(np.float32)
+    np.savez_compressed(out_dir / "q6_k.npz", raw=q6.reshape(-1), deq=q6_deq)
 
     (out_dir / "PROVENANCE.txt").write_text(
         "Generated by tests/golden/make_golden.py from the reference's tools/qw35_cook_common.py\n"

@@ -59,6 +59,8 @@ def test_weight_bytes_match_gguf_block_sizes():
     assert L.qw35_cuda_weight_bytes(100, 248320, 4096) == 508559360
     assert L.qw35_cuda_weight_bytes(8, 248320, 4096) == 1080688640
     assert L.qw35_cuda_weight_bytes(12, 248320, 4096) == 572129280
+    assert L.qw35_cuda_weight_bytes(13, 4096, 4096) == 4096 * 16 * 176
+    assert L.qw35_cuda_weight_bytes(14, 248320, 4096) == 248320 * 16 * 210
     assert L.qw35_cuda_weight_bytes(99, 1, 256) == 0
 
 
@@ -69,6 +71,11 @@ def test_device_bytes_add_the_q8_0_row_exponent_plane():
     assert L.qw35_cuda_device_bytes(8, 12288, 4096) == 53477376 + 12288
     assert L.qw35_cuda_device_bytes(8, 333, 1280) == 333 * 40 * 34 + 336
     assert L.qw35_cuda_device_bytes(99, 1, 256) == 0
+    # Q5_K: nibble + high-bit planes and 16-byte headers: same size as GGUF
+    assert L.qw35_cuda_device_bytes(13, 4096, 4096) == L.qw35_cuda_weight_bytes(13, 4096, 4096)
+    # Q6_K: 3k/4 code bytes + (k/16 scales + k/128 d bytes, 16-byte padded) per row
+    assert L.qw35_cuda_device_bytes(14, 248320, 4096) == 248320 * (3072 + 288)
+    assert L.qw35_cuda_device_bytes(14, 7, 256) == 7 * (192 + 32)
 
 
 def test_invalid_handles_and_error_buffers():

@@ -14,7 +14,7 @@ from qwowl35_b200 import ops
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
-CODECS = [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE]
+CODECS = [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE, Q.Q5_K_TYPE, Q.Q6_K_TYPE]
 
 
 def relerr(y, ref):
@@ -57,6 +57,14 @@ def test_q8_0_and_q4_k_dequant_of_gguf_golden():
     g = np.load("tests/golden/q4_k.npz")
     w = ops.upload(Q.Q4_K_TYPE, g["raw"], 16, 1024)
     np.testing.assert_array_equal(ops.dequant(Q.Q4_K_TYPE, w, 16, 1024).cpu().numpy().view(np.uint32),
+                                  g["deq"].view(np.uint32))
+
+
+@pytest.mark.parametrize("t,name", [(Q.Q5_K_TYPE, "q5_k"), (Q.Q6_K_TYPE, "q6_k")])
+def test_q5_k_q6_k_dequant_of_gguf_golden(t, name):
+    g = np.load(f"tests/golden/{name}.npz")
+    w = ops.upload(t, g["raw"], 16, 1024)
+    np.testing.assert_array_equal(ops.dequant(t, w, 16, 1024).cpu().numpy().view(np.uint32),
                                   g["deq"].view(np.uint32))
 
 
@@ -106,7 +114,7 @@ def test_gate_up_swiglu(t, b):
     assert relerr(h, ref) < TOL
 
 
-@pytest.mark.parametrize("t", [Q.Q8_0_TYPE, Q.GF4_TYPE])
+@pytest.mark.parametrize("t", [Q.Q8_0_TYPE, Q.GF4_TYPE, Q.Q6_K_TYPE])
 @pytest.mark.parametrize("b", [1, 3])
 def test_argmax_head_matches_logits_bit_exact(t, b):
     rows, k = 50000, 4096

@@ -86,7 +86,27 @@ def test_q4_k_dequant_matches_gguf():
     np.testing.assert_array_equal(Q.q4_k_dequant(g["raw"], 16, 1024).view(np.uint32), g["deq"].view(np.uint32))
 
 
-@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE])
+@pytest.mark.parametrize("name,fn", [("q5_k.npz", Q.q5_k_dequant), ("q6_k.npz", Q.q6_k_dequant)])
+def test_q5_k_q6_k_dequant_matches_gguf(name, fn):
+    g = load(name)
+    np.testing.assert_array_equal(fn(g["raw"], 16, 1024).view(np.uint32), g["deq"].view(np.uint32))
+
+
+def test_q6_k_code_order_follows_the_block_layout():
+    # one block whose ql/qh encode code = element index % 64 in GGUF order
+    blk = np.zeros(210, dtype=np.uint8)
+    want = np.arange(256) % 64
+    for h in range(2):
+        for m in range(4):
+            for l in range(32):
+                e = 128 * h + 32 * m + l
+                qi = 64 * h + 32 * (m & 1) + l
+                blk[qi] |= (want[e] & 15) << (0 if m < 2 else 4)
+                blk[128 + 32 * h + l] |= (want[e] >> 4) << (2 * m)
+    np.testing.assert_array_equal(Q.q6_k_codes(blk[None]), want[None])
+
+
+@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE, Q.Q5_K_TYPE, Q.Q6_K_TYPE])
 def test_generators_row_bytes(t):
     rng = np.random.default_rng(1)
     raw = Q.gen_weight(rng, t, 8, 512)
