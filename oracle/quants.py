@@ -252,13 +252,22 @@ def q6_k_dequant(raw: np.ndarray, rows: int, k: int) -> np.ndarray:
 
 
 def dequant(type_id: int, raw: np.ndarray, rows: int, k: int, gf4_exact: bool = False,
-            gf4_half: bool = False) -> np.ndarray:
+            gf4_half: bool = False, tiled: bool = False) -> np.ndarray:
+    """Dequantised weights [rows, k] float32.
+
+    ``tiled=True`` gives the weights of the reference's multi-row (tiled)
+    path, which dequantises into half tiles (``qw35_tiled_mm.metal:197-213``):
+    GF4 element 4 rounded to half (``gf4_half``, unless ``gf4_exact``) and
+    Q4_K's fp32 ``dl*q - ml`` rounded to half (``qw35_matvec.metal:20-38``).
+    """
     if type_id == GF4_TYPE:
-        return gf4_dequant(np.asarray(raw).view(np.uint32).reshape(rows, k // 8), exact=gf4_exact, half=gf4_half)
+        return gf4_dequant(np.asarray(raw).view(np.uint32).reshape(rows, k // 8), exact=gf4_exact,
+                           half=gf4_half or (tiled and not gf4_exact))
     if type_id == Q8_0_TYPE:
         return q8_0_dequant(raw, rows, k)
     if type_id == Q4_K_TYPE:
-        return q4_k_dequant(raw, rows, k)
+        w = q4_k_dequant(raw, rows, k)
+        return w.astype(np.float16).astype(np.float32) if tiled else w
     if type_id == Q5_K_TYPE:
         return q5_k_dequant(raw, rows, k)
     if type_id == Q6_K_TYPE:

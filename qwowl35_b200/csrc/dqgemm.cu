@@ -14,10 +14,12 @@
 // hi + lo halves so the product keeps ~22 bits of the activation.
 //
 // Q8_0 weights are not exact in f16 once multiplied by their block scale, so
-// the int8 codes (exact) go through the tensor core per 32-column block into a
-// rotating set of TMEM accumulators and the epilogue warps apply the f16 block
-// scale in fp32 (acc += d * block_sum): bit-for-bit the reference's
-// per-block arithmetic up to summation order.
+// each q * d (times a per-row power of two) is split into hi + lo halves and
+// both go through the tensor core (the epilogue removes the power of two).
+// Q4_K weights become half(d*sc*q - dmin*m), computed in fp32 and rounded
+// once: the reference's tiled path (qw35_dequantize_q4_k into half,
+// qw35_matvec.metal:20-38, instantiated for half tiles at
+// qw35_tiled_mm.metal:204-213).
 //
 // CTA: warp 0 weight TMA producer, warp 1 MMA issuer (+ TMEM owner), warp 2
 // activation producer, then decode warps (thread = weight row, writing the
@@ -40,6 +42,7 @@
 #include "common.cuh"
 #include "ops.h"
 #include "pipe.cuh"
+#include "quant.cuh"
 #include "tc.cuh"
 
 namespace qw35 {
@@ -55,6 +58,7 @@ constexpr int TM = 128;  // weight rows per tile (MMA M = TMEM lanes)
 // quarter); the groups split a chunk's K range.
 template <int CODEC> struct DqGeo {
     static constexpr bool Q8 = CODEC == QW35_Q8_0_TYPE;
+    static constexpr bool K4 = CODEC == QW35_Q4_K_TYPE;  // one 256-column block per row per chunk
     static constexpr int KC = Q8 ? 128 : 256;
     static constexpr int DEC = Q8 ? 8 : 16;                       // decode warps
     static constexpr int EPI = 4;                                 // epilogue warps
@@ -63,7 +67,7 @@ template <int CODEC> struct DqGeo {
     static constexpr int GK = KC / NG;                            // K columns per group (64)
     static constexpr int ACOLS = 128;                             // TMEM columns of one A tile
     static constexpr uint32_t WCODES = 128u * 128u;               // codes bytes of a stage
-    static constexpr uint32_t WS = WCODES + (Q8 ? 128u * 16u : 0u);  // + 8 scales per row
+    static constexpr uint32_t WS = WCODES + ((Q8 || K4) ? 128u * 16u : 0u);  // + 8 scales / a header per row
 };
 
 enum DqMode { DQ_STORE = 0, DQ_ACCUM = 1, DQ_DUAL = 2 };
@@ -367,8 +371,10 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                     mbar_arrive_expect_tx(&full_w[rw.s], WS);
                     // x coordinate in elements: 32-bit words (GF4) or bytes (Q8_0)
                     tma_load_2d(dst, map, Q8 ? kc * KC : kc * (KC / 8), tile * TM, &full_w[rw.s], pol);
-                    // Q8_0: the 8 block scales (16 B) of each row around this chunk's 4
+                    // Q8_0: the 8 block scales (16 B) of each row around this chunk's 4;
+                    // Q4_K: the chunk's 16-byte block header of each row (x in words)
                     if constexpr (Q8) tma_load_2d(dst + G::WCODES, smap, (kc * 4) & ~7, tile * TM, &full_w[rw.s], pol);
+                    if constexpr (G::K4) tma_load_2d(dst + G::WCODES, smap, kc * 4, tile * TM, &full_w[rw.s], pol);
                     rw.next(NW);
                 }
             })
@@ -473,7 +479,38 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                 tc_fence_after();
                 const uint8_t *row = wst + (size_t)sw * WS + r * 128;
                 const uint32_t tcol = tmem + lane_addr + T::A0 + sa * G::ACOLS + grp * 32;
-                if constexpr (!Q8) {
+                if constexpr (G::K4) {
+                    // 64 columns = pieces 2g, 2g+1 of the row = sub-blocks 2g, 2g+1 of the
+                    // block, nibbles in element order.  Nibble n of a word is moved to
+                    // mantissa bit 15 (n even) or 19 (n odd) of 1.0f by one of four
+                    // shifts: f = 1 + q * 2^-8 (or 2^-4), and fma(f, S, -S) with
+                    // S = dl * 2^8 (2^4) is dl * q exactly; minus ml is the reference's
+                    // fp32 value, rounded once to half.
+                    const uint4 h = *reinterpret_cast<const uint4 *>(wst + (size_t)sw * WS + G::WCODES + r * 16);
+                    uint32_t o[32];
+#pragma unroll
+                    for (int i = 0; i < 2; ++i) {
+                        float dl, ml;
+                        q4k_scale_min(h, 2 * grp + i, dl, ml);
+                        const float s8 = dl * 256.0f, s4 = dl * 16.0f;
+                        const uint4 w4 = *reinterpret_cast<const uint4 *>(row + (((2 * grp + i) ^ (r & 7)) << 4));
+                        const uint32_t ws4[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                        for (int wd = 0; wd < 4; ++wd) {
+                            const uint32_t wv = ws4[wd];
+                            const uint32_t sh[4] = {wv << 15, wv << 7, wv >> 1, wv >> 9};
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) {
+                                const float fe = __uint_as_float((sh[t] & (0xFu << 15)) | 0x3F800000u);
+                                const float fo = __uint_as_float((sh[t] & (0xFu << 19)) | 0x3F800000u);
+                                const float ve = fmaf(fe, s8, -s8) - ml, vo = fmaf(fo, s4, -s4) - ml;
+                                const __half2 hv = __floats2half2_rn(ve, vo);
+                                o[16 * i + 4 * wd + t] = *reinterpret_cast<const uint32_t *>(&hv);
+                            }
+                        }
+                    }
+                    tmem_st32(tcol, o);
+                } else if constexpr (!Q8) {
                     // 64 columns = 8 words = pieces 2g, 2g+1 of the row
                     const uint4 wa = *reinterpret_cast<const uint4 *>(row + (((2 * grp) ^ (r & 7)) << 4));
                     const uint4 wb = *reinterpret_cast<const uint4 *>(row + (((2 * grp + 1) ^ (r & 7)) << 4));
@@ -851,7 +888,7 @@ bool weight_map(uint32_t type_id, const void *w, uint32_t rows, uint32_t k, CUte
     cuuint32_t box[2], estr[2] = {1, 1};
     CUtensorMapDataType dt;
     // 128 rows x 128 bytes per box, 128B-swizzled (16-byte piece q of row r at q ^ (r % 8))
-    if (type_id == QW35_GF4_TYPE) {
+    if (type_id == QW35_GF4_TYPE || type_id == QW35_Q4_K_TYPE) {  // k/2 bytes of codes per row
         dt = CU_TENSOR_MAP_DATA_TYPE_UINT32;
         dims[0] = k / 8; dims[1] = rows; strides[0] = (cuuint64_t)k / 2;
         box[0] = 32; box[1] = TM;
@@ -888,6 +925,33 @@ bool scale_map(const void *w, uint32_t rows, uint32_t k, CUtensorMap *out) {
     cuuint32_t box[2] = {8, TM}, estr[2] = {1, 1};
     void *base = static_cast<uint8_t *>(const_cast<void *>(w)) + (size_t)rows * k;
     if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+        return false;
+    cache[key] = m;
+    *out = m;
+    return true;
+}
+
+// Tensor map over the Q4_K headers plane ([rows][K/256] x 16 bytes, after the
+// codes plane): boxes of one header (4 words) x 128 rows.
+bool header_map(const void *w, uint32_t rows, uint32_t k, CUtensorMap *out) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void *, uint32_t, uint32_t>, CUtensorMap> cache;
+    std::lock_guard<std::mutex> g(mu);
+    auto key = std::make_tuple(w, rows, k);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return true;
+    }
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    CUtensorMap m;
+    cuuint64_t dims[2] = {k / 64, rows}, strides[1] = {(cuuint64_t)k / 16};
+    cuuint32_t box[2] = {4, TM}, estr[2] = {1, 1};
+    void *base = static_cast<uint8_t *>(const_cast<void *>(w)) + (size_t)rows * (k / 2);
+    if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
            CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
         CUDA_SUCCESS)
         return false;
@@ -948,8 +1012,9 @@ bool dq_supported(const MatvecArgs &a) {
     // TMA needs 16-byte aligned weights; the activation prep reads x and the
     // norm weight 16 bytes at a time
     auto a16 = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
-    // K % 256: GF4 chunks are 256 columns; Q8_0 scale boxes span two 128-column chunks
-    return a.batch >= kDqMinBatch && a.batch <= 64 && (a.type_id == QW35_GF4_TYPE || a.type_id == QW35_Q8_0_TYPE) &&
+    // K % 256: GF4 / Q4_K chunks are 256 columns; Q8_0 scale boxes span two 128-column chunks
+    return a.batch >= kDqMinBatch && a.batch <= 64 &&
+           (a.type_id == QW35_GF4_TYPE || a.type_id == QW35_Q8_0_TYPE || a.type_id == QW35_Q4_K_TYPE) &&
            a.k % 256 == 0 &&
            a16(a.w0) && a16(a.w1) && a16(a.x) && a16(a.norm_w) && encode_fn() != nullptr &&
            !getenv("QW35_NO_TCGEN05");
@@ -1071,10 +1136,14 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
     if (!weight_map(a.type_id, a.w0, a.rows, a.k, &m0)) return cudaErrorInvalidValue;
     if (dual && !weight_map(a.type_id, a.w1, a.rows, a.k, &m1)) return cudaErrorInvalidValue;
     if (!dual) m1 = m0;
-    CUtensorMap s0 = m0, s1 = m1;  // scales maps (Q8_0 only; unused otherwise)
+    CUtensorMap s0 = m0, s1 = m1;  // scales (Q8_0) / headers (Q4_K) maps; unused for GF4
     if (a.type_id == QW35_Q8_0_TYPE) {
         if (!scale_map(a.w0, a.rows, a.k, &s0)) return cudaErrorInvalidValue;
         if (dual && !scale_map(a.w1, a.rows, a.k, &s1)) return cudaErrorInvalidValue;
+        if (!dual) s1 = s0;
+    } else if (a.type_id == QW35_Q4_K_TYPE) {
+        if (!header_map(a.w0, a.rows, a.k, &s0)) return cudaErrorInvalidValue;
+        if (dual && !header_map(a.w1, a.rows, a.k, &s1)) return cudaErrorInvalidValue;
         if (!dual) s1 = s0;
     }
     const size_t extra = (mode == 2) ? (size_t)2 * B * rows * 4 : (mode == 3 && !a.y) ? (size_t)B * rows * 4 : 0;
@@ -1088,7 +1157,7 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
     float *ext = reinterpret_cast<float *>(base + lay.ext);
 
     const int tiles = (rows + TM - 1) / TM;
-    const int nch = K / (a.type_id == QW35_GF4_TYPE ? DqGeo<QW35_GF4_TYPE>::KC : DqGeo<QW35_Q8_0_TYPE>::KC);
+    const int nch = K / (a.type_id == QW35_Q8_0_TYPE ? DqGeo<QW35_Q8_0_TYPE>::KC : DqGeo<QW35_GF4_TYPE>::KC);
     // logits (mode 3) are stored, never accumulated: whole tiles per CTA
     const int gran = mode == 3 ? nch : 1;
     DqParams p{};
@@ -1146,6 +1215,10 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
         if (NP == 16) e = dq_dispatch_mode<QW35_GF4_TYPE, 16>(dmode, exact, m0, m1, s0, s1, y0m, y1m, p, st);
         else if (NP == 32) e = dq_dispatch_mode<QW35_GF4_TYPE, 32>(dmode, exact, m0, m1, s0, s1, y0m, y1m, p, st);
         else e = dq_dispatch_mode<QW35_GF4_TYPE, 64>(dmode, exact, m0, m1, s0, s1, y0m, y1m, p, st);
+    } else if (a.type_id == QW35_Q4_K_TYPE) {
+        if (NP == 16) e = dq_dispatch_mode<QW35_Q4_K_TYPE, 16>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
+        else if (NP == 32) e = dq_dispatch_mode<QW35_Q4_K_TYPE, 32>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
+        else e = dq_dispatch_mode<QW35_Q4_K_TYPE, 64>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
     } else {
         if (NP == 16) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 16>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
         else if (NP == 32) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 32>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);

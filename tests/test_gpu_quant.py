@@ -167,7 +167,7 @@ def test_no_device_wait_timed_out():
 
 
 # ---- batched (B >= 16) tensor-core path -----------------------------------------
-@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE])
+@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE])
 @pytest.mark.parametrize("b", [3, 8, 16, 32, 64, 20])
 @pytest.mark.parametrize("shape", [(12288, 4096), (4096, 12288), (333, 1280)])
 def test_batched_matvec_parity(t, b, shape):
@@ -175,14 +175,14 @@ def test_batched_matvec_parity(t, b, shape):
     raw, w = make(t, rows, k, 20)
     x = np.random.default_rng(21).standard_normal((b, k)).astype(np.float32)
     y = ops.matvec(t, w, torch.from_numpy(x).cuda(), rows, k).cpu().numpy()
-    ref = O.matvec(Q.dequant(t, raw, rows, k, gf4_half=True), x)
+    ref = O.matvec(Q.dequant(t, raw, rows, k, tiled=True), x)
     assert relerr(y, ref) < TOL
     if t == Q.GF4_TYPE:  # exact mode too
         ye = ops.matvec(t, w, torch.from_numpy(x).cuda(), rows, k, exact=True).cpu().numpy()
         assert relerr(ye, O.matvec(Q.dequant(t, raw, rows, k, gf4_exact=True), x)) < TOL
 
 
-@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE])
+@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE])
 def test_batched_accumulate_swiglu_and_head(t):
     rows, k, b = 4096, 4096, 32
     raw, w = make(t, rows, k, 22)
@@ -191,11 +191,11 @@ def test_batched_accumulate_swiglu_and_head(t):
     base = rng.standard_normal((b, rows)).astype(np.float32)
     y = torch.from_numpy(base.copy()).cuda()
     ops.matvec(t, w, torch.from_numpy(x).cuda(), rows, k, y=y, accumulate=True)
-    deq = Q.dequant(t, raw, rows, k, gf4_half=True)
+    deq = Q.dequant(t, raw, rows, k, tiled=True)
     assert relerr(y.cpu().numpy(), base + O.matvec(deq, x)) < TOL
     raw2, w2 = make(t, rows, k, 24)
     h = ops.gate_up_swiglu(t, w, w2, torch.from_numpy(x).cuda(), rows, k).cpu().numpy()
-    assert relerr(h, O.gate_up_swiglu(deq, Q.dequant(t, raw2, rows, k, gf4_half=True), x)) < TOL
+    assert relerr(h, O.gate_up_swiglu(deq, Q.dequant(t, raw2, rows, k, tiled=True), x)) < TOL
     tok, val, logits = ops.argmax_head(t, w, torch.from_numpy(x).cuda(), rows, k, want_logits=True)
     lg = logits.cpu().numpy()
     assert relerr(lg, O.matvec(deq, x)) < TOL
@@ -225,25 +225,32 @@ def _random_words_all_scales(rng, rows, k):
     return ((w & np.uint32(0xFFFFFF00)) | sb).view(np.uint8).reshape(-1)
 
 
-@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE])
+@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE])
 @pytest.mark.parametrize("exact", [False, True])
 def test_batched_path_weights_bit_exact(t, exact):
     """One-hot activation rows make y[b][r] = W[r][k_b] a single exact product,
     so the tensor-core path's decoded weights are compared bit for bit with the
-    oracle (GF4 element 4 rounded to half as the reference's tiled path does)."""
-    if t == Q.Q8_0_TYPE and exact:
-        pytest.skip("one Q8_0 mode")
+    oracle (GF4 element 4 and Q4_K weights rounded to half as the reference's
+    tiled path does)."""
+    if t != Q.GF4_TYPE and exact:
+        pytest.skip("one mode")
     rows, k, b = 333, 256, 64
     rng = np.random.default_rng(31)
     if t == Q.GF4_TYPE:
         raw = _random_words_all_scales(rng, rows, k)
+    elif t == Q.Q4_K_TYPE:  # d, dmin over a wide range, both signs
+        raw = Q.gen_weight(rng, t, rows, k)
+        blocks = raw.reshape(-1, 144)
+        for off in (0, 2):
+            v = (rng.standard_normal(blocks.shape[0]) * 10.0 ** rng.integers(-4, 1, size=blocks.shape[0]))
+            blocks[:, off:off + 2] = v.astype(np.float16).view(np.uint8).reshape(-1, 2)
     else:
         raw = Q.gen_weight(rng, t, rows, k)
         blocks = raw.reshape(-1, 34)
         d = rng.standard_normal(blocks.shape[0]).astype(np.float16) * np.float16(4)
         blocks[:, 0:2] = d.view(np.uint8).reshape(-1, 2)
     w = ops.upload(t, raw, rows, k)
-    deq = Q.dequant(t, raw, rows, k, gf4_exact=exact, gf4_half=not exact).astype(np.float32)
+    deq = Q.dequant(t, raw, rows, k, gf4_exact=exact, tiled=True).astype(np.float32)
     for k0 in range(0, k, b):
         x = np.zeros((b, k), dtype=np.float32)
         x[np.arange(b), k0 + np.arange(b)] = 1.0
