@@ -16,10 +16,11 @@ from . import quants as Q
 
 
 class OracleModel:
-    def __init__(self, synth, gf4_exact: bool = False, window: int = 0, sink: int = 0, gf4_half: bool = False):
-        """gf4_half: GF4 weights as the reference's multi-token path rounds them
-        (element 4 of each word to half) -- the semantics of batches >= 16."""
-        self.gf4_half = gf4_half
+    def __init__(self, synth, gf4_exact: bool = False, window: int = 0, sink: int = 0, tiled: bool = False):
+        """tiled: weights as the reference's multi-token (tiled) path rounds them
+        to half (GF4 element 4, Q4_K values) -- the semantics of the batched
+        tensor-core path (3 or more rows)."""
+        self.tiled = tiled
         self.m = synth
         self.cfg = synth.cfg
         self.gf4_exact = gf4_exact
@@ -50,7 +51,7 @@ class OracleModel:
             if t == Q.F32_TYPE:
                 self._cache[name] = raw.view(np.float32).reshape(r, k) if r > 1 else raw.view(np.float32)
             else:
-                self._cache[name] = Q.dequant(t, raw, r, k, gf4_exact=self.gf4_exact, gf4_half=self.gf4_half)
+                self._cache[name] = Q.dequant(t, raw, r, k, gf4_exact=self.gf4_exact, tiled=self.tiled)
         return self._cache[name]
 
     def embed(self, token: int) -> np.ndarray:

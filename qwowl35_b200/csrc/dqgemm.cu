@@ -813,6 +813,12 @@ __global__ void dq_swiglu_kernel(const float *g, const float *u, float *h, size_
         h[i] = silu_f(g[i]) * u[i];
 }
 
+cudaError_t swiglu_run(const float *gate, const float *up, float *h, size_t n, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    dq_swiglu_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256, 0, st>>>(gate, up, h, n);
+    return cudaGetLastError();
+}
+
 // lowest-id argmax of each logits row (one CTA of 1024 threads per row)
 __global__ void __launch_bounds__(1024) dq_argmax_rows_kernel(const float *logits, int V, uint32_t *tok, float *val) {
     __shared__ float sv[32];

@@ -26,6 +26,8 @@ struct MatvecArgs {
 };
 
 cudaError_t matvec_run(const MatvecArgs &a, cudaStream_t st);
+// h = silu(gate) * up, elementwise over n floats (h may alias gate)
+cudaError_t swiglu_run(const float *gate, const float *up, float *h, size_t n, cudaStream_t st);
 size_t argmax_workspace_bytes(uint32_t rows, uint32_t batch);
 cudaError_t argmax_head_run(const MatvecArgs &a, uint32_t *tok, float *val, void *ws, size_t ws_bytes,
                             cudaStream_t st);

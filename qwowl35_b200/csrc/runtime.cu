@@ -125,6 +125,24 @@ struct Loader {
         ck(cudaDeviceSynchronize(), "repack sync");
         return dt;
     }
+    // A fused projection as runs of consecutive same-type tensors, each run
+    // concatenated into one matrix (the reference's GGUFs mix types inside
+    // a projection group, e.g. a Q6_K attn_v beside Q4_K attn_q / attn_k).
+    std::vector<ProjPart> matrix_parts(const std::vector<std::string> &names, uint64_t k_expect) {
+        std::vector<ProjPart> parts;
+        uint32_t off = 0;
+        for (size_t i = 0; i < names.size();) {
+            size_t j = i + 1;
+            while (j < names.size() && get(names[j]).d->type_id == get(names[i]).d->type_id) ++j;
+            ProjPart pp;
+            pp.w = matrix_cat(std::vector<std::string>(names.begin() + i, names.begin() + j), k_expect);
+            pp.out_off = off;
+            off += pp.w.rows;
+            parts.push_back(pp);
+            i = j;
+        }
+        return parts;
+    }
     DevTensor matrix(const std::string &name, uint64_t k, uint64_t rows_expect) {
         DevTensor t = matrix_cat({name}, k);
         if (rows_expect && t.rows != rows_expect)
@@ -172,20 +190,20 @@ std::shared_ptr<ModelStore> load_model(const void *map, uint64_t map_size, const
         lw.post_norm = L.f32(p + "post_attention_norm.weight", H);
         if (lw.attn) {
             lw.slot = ms->n_attn++;
-            DevTensor q = L.matrix_cat({p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"}, H);
-            if (q.rows != 16 * 512 + 1024 + 1024) fail("%sattn_q/k/v have %u rows, expected 10240", p.c_str(), q.rows);
-            lw.proj.push_back({q, 0});
-            lw.proj_rows = q.rows;
+            lw.proj = L.matrix_parts({p + "attn_q.weight", p + "attn_k.weight", p + "attn_v.weight"}, H);
+            lw.proj_rows = lw.proj.back().out_off + lw.proj.back().w.rows;
+            if (lw.proj_rows != 16 * 512 + 1024 + 1024)
+                fail("%sattn_q/k/v have %u rows, expected 10240", p.c_str(), lw.proj_rows);
             lw.q_norm = L.f32(p + "attn_q_norm.weight", 256);
             lw.k_norm = L.f32(p + "attn_k_norm.weight", 256);
             lw.out = L.matrix(p + "attn_output.weight", 4096, H);
         } else {
             lw.slot = ms->n_delta++;
-            DevTensor d = L.matrix_cat({p + "attn_qkv.weight", p + "attn_gate.weight", p + "ssm_beta.weight",
-                                        p + "ssm_alpha.weight"}, H);
-            if (d.rows != 8192 + 4096 + 32 + 32) fail("%sdelta projections have %u rows, expected 12352", p.c_str(), d.rows);
-            lw.proj.push_back({d, 0});
-            lw.proj_rows = d.rows;
+            lw.proj = L.matrix_parts({p + "attn_qkv.weight", p + "attn_gate.weight", p + "ssm_beta.weight",
+                                      p + "ssm_alpha.weight"}, H);
+            lw.proj_rows = lw.proj.back().out_off + lw.proj.back().w.rows;
+            if (lw.proj_rows != 8192 + 4096 + 32 + 32)
+                fail("%sdelta projections have %u rows, expected 12352", p.c_str(), lw.proj_rows);
             lw.conv_w = L.f32(p + "ssm_conv1d.weight", 8192ull * 4);
             lw.dt = L.f32(p + "ssm_dt.bias", 32);
             lw.a = L.f32(p + "ssm_a", 32);
@@ -194,8 +212,8 @@ std::shared_ptr<ModelStore> load_model(const void *map, uint64_t map_size, const
         }
         lw.gate = L.matrix(p + "ffn_gate.weight", H, F);
         lw.up = L.matrix(p + "ffn_up.weight", H, F);
-        if (lw.gate.type_id != lw.up.type_id) fail("%sffn_gate/ffn_up types differ", p.c_str());
         lw.down = L.matrix(p + "ffn_down.weight", F, H);
+        if (lw.proj.size() > 1 || lw.gate.type_id != lw.up.type_id) ms->mixed = true;
         ms->layers.push_back(lw);
     }
     return ms;

@@ -41,7 +41,7 @@ struct ProjPart {  // one matvec of a (possibly concatenated) projection
 struct LayerW {
     bool attn = false;
     const float *attn_norm = nullptr, *post_norm = nullptr;
-    std::vector<ProjPart> proj;     // delta: qkv|z|beta|alpha ; attn: q|k|v
+    std::vector<ProjPart> proj;     // delta: qkv|z|beta|alpha ; attn: q|k|v (one part per run of one type)
     uint32_t proj_rows = 0;
     DevTensor out;                  // ssm_out / attn_output
     DevTensor gate, up, down;
@@ -64,6 +64,7 @@ struct ModelStore {
     std::vector<void *> allocations;
     uint64_t bytes = 0;
     int n_delta = 0, n_attn = 0;
+    bool mixed = false;  // some projection has parts of different types, or gate/up types differ
     ~ModelStore();
 };
 
@@ -112,6 +113,7 @@ struct Runtime {
     cudaEvent_t in_done = nullptr;
     float *act = nullptr, *proj = nullptr, *core = nullptr, *hbuf = nullptr, *qbuf = nullptr, *gbuf = nullptr;
     float *logits = nullptr;
+    float *mixed_tmp = nullptr;  // [max_seqs][max(proj_stride, ffn)], only for mixed-type models
     uint32_t *d_argmax_tok = nullptr;
     float *d_argmax_val = nullptr;
     uint32_t *h_argmax_tok = nullptr;

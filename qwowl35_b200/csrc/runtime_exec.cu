@@ -38,6 +38,34 @@ static void mv(Runtime *rt, const DevTensor &w, const void *x, const float *norm
     ck(matvec_run(a, rt->stream), "matvec");
 }
 
+// A projection of several parts (runs of one weight type): each part's
+// matvec writes [n][part rows] into scratch, and one strided 2-D copy places
+// it at its offset in the [n][proj_rows] projection output.
+static void proj_mv(Runtime *rt, const LayerW &lw, int n) {
+    if (lw.proj.size() == 1) {
+        mv(rt, lw.proj[0].w, rt->act, lw.attn_norm, rt->proj, n, 0);
+        return;
+    }
+    for (const ProjPart &pp : lw.proj) {
+        mv(rt, pp.w, rt->act, lw.attn_norm, rt->mixed_tmp, n, 0);
+        ck(cudaMemcpy2DAsync(rt->proj + pp.out_off, (size_t)lw.proj_rows * 4, rt->mixed_tmp, (size_t)pp.w.rows * 4,
+                             (size_t)pp.w.rows * 4, (size_t)n, cudaMemcpyDeviceToDevice, rt->stream),
+           "projection part copy");
+    }
+}
+
+// gate/up + SwiGLU: one fused launch when both have one type, else two
+// matvecs and an elementwise SwiGLU.
+static void ffn_gate_up(Runtime *rt, const LayerW &lw, int n) {
+    if (lw.gate.type_id == lw.up.type_id) {
+        mv(rt, lw.gate, rt->act, lw.post_norm, rt->hbuf, n, 2, &lw.up);
+        return;
+    }
+    mv(rt, lw.gate, rt->act, lw.post_norm, rt->hbuf, n, 0);
+    mv(rt, lw.up, rt->act, lw.post_norm, rt->mixed_tmp, n, 0);
+    ck(swiglu_run(rt->hbuf, rt->mixed_tmp, rt->hbuf, (size_t)n * lw.gate.rows, rt->stream), "swiglu");
+}
+
 static void encode_step(Runtime *rt, int n, int mode, int maxlen) {
     ModelStore &ms = *rt->model;
     cudaStream_t st = rt->stream;
@@ -47,13 +75,12 @@ static void encode_step(Runtime *rt, int n, int mode, int maxlen) {
     ck(embed_rows(ms.tok_embd.type_id, ms.tok_embd.ptr, ms.tok_embd.rows, rt->d_tok, n, 4096, rt->act, st), "embed");
     const size_t nd = (size_t)std::max(ms.n_delta, 1);
     for (const LayerW &lw : ms.layers) {
-        const DevTensor &pw = lw.proj[0].w;
-        mv(rt, pw, rt->act, lw.attn_norm, rt->proj, n, 0);
+        proj_mv(rt, lw, n);
         if (!lw.attn) {
             DeltaNetArgs d;
             d.n_seq = n;
             d.proj = rt->proj;
-            d.proj_stride = (int)pw.rows;
+            d.proj_stride = (int)lw.proj_rows;
             d.conv_w = lw.conv_w;
             d.dt = lw.dt;
             d.a = lw.a;
@@ -72,7 +99,7 @@ static void encode_step(Runtime *rt, int n, int mode, int maxlen) {
             AttnPreArgs pa;
             pa.n_seq = n;
             pa.qkv = rt->proj;
-            pa.qkv_stride = (int)pw.rows;
+            pa.qkv_stride = (int)lw.proj_rows;
             pa.q_norm_w = lw.q_norm;
             pa.k_norm_w = lw.k_norm;
             pa.rope_freq = rt->rope_freq;
@@ -106,7 +133,7 @@ static void encode_step(Runtime *rt, int n, int mode, int maxlen) {
             ck(attn_decode_run(aa, st), "attention");
         }
         mv(rt, lw.out, rt->core, nullptr, rt->act, n, 1);
-        mv(rt, lw.gate, rt->act, lw.post_norm, rt->hbuf, n, 2, &lw.up);
+        ffn_gate_up(rt, lw, n);
         mv(rt, lw.down, rt->hbuf, nullptr, rt->act, n, 1);
     }
     if (mode == QW35_LOGITS_ARGMAX) {

@@ -50,7 +50,7 @@ Runtime::~Runtime() {
     if (stream) cudaStreamSynchronize(stream);
     for (auto &kv : graphs) cudaGraphExecDestroy(kv.second);
     void *dev_ptrs[] = {conv_state, ssm_state, d_chunk_table, d_in, act, proj, core, hbuf, qbuf, gbuf,
-                        logits, d_argmax_tok, d_argmax_val, argmax_ws, attn_ws, rope_freq};
+                        logits, d_argmax_tok, d_argmax_val, argmax_ws, attn_ws, rope_freq, mixed_tmp};
     for (void *p : dev_ptrs)
         if (p) cudaFree(p);
     for (void *p : arenas) cudaFree(p);
@@ -125,6 +125,7 @@ Runtime *create_runtime(std::shared_ptr<ModelStore> ms, uint32_t ctx, uint32_t v
     rt->qbuf = dmalloc<float>((size_t)S * H);
     rt->gbuf = dmalloc<float>((size_t)S * H);
     rt->logits = dmalloc<float>((size_t)S * vocab);
+    if (rt->model->mixed) rt->mixed_tmp = dmalloc<float>((size_t)S * std::max<uint32_t>(rt->proj_stride, F));
     rt->d_argmax_tok = dmalloc<uint32_t>(S);
     rt->d_argmax_val = dmalloc<float>(S);
     rt->argmax_ws_bytes = argmax_workspace_bytes(vocab, S);

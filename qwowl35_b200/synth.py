@@ -4,14 +4,15 @@ There is no network for checkpoints, so benchmarks and tests decode through
 a random-init model written exactly the way the reference's loader hands
 tensors to the runtime (qw35-server/src/metal/bridge.rs:260-338): one host
 mapping, a table of ``qw35_metal_tensor_desc`` (dims[0] = K), GGUF type ids
-(100 GF4, 8 Q8_0, 12 Q4_K, 0 f32) and the reference's tensor names
+(100 GF4, 8 Q8_0, 12 Q4_K, 13 Q5_K, 14 Q6_K, 0 f32) and the reference's tensor names
 (qw35-server/src/graph.rs:173-210).
 
 Value distributions follow the benchmark configs: GF4 words carry uniform
 3-bit codes and an e5m2 scale of |N(0, 0.02)|; Q8_0 blocks carry uniform
 int8 codes in [-127, 127] and d = |N(0, 0.02)| / 127 (so the block maximum,
 like the GF4 group maximum, is |N(0, 0.02)|); Q4_K blocks carry uniform
-codes/6-bit scales and d, dmin = |N(0, 0.02)| / 64.  Norm weights are
+codes/6-bit scales and d, dmin = |N(0, 0.02)| / 64 (Q5_K: / 128); Q6_K blocks
+carry uniform codes and int8 scales and d = |N(0, 0.02)| / 4096.  Norm weights are
 |N(1, 0.1)|, ssm_a = -exp(N(0, 0.5)), ssm_dt.bias ~ N(0, 1),
 ssm_conv1d ~ N(0, 0.3).
 
@@ -27,7 +28,7 @@ import numpy as np
 
 from ._lib import Hparams, TensorDesc
 
-GF4, Q8_0, Q4_K, F32 = 100, 8, 12, 0
+GF4, Q8_0, Q4_K, Q5_K, Q6_K, F32 = 100, 8, 12, 13, 14, 0
 ALIGN = 32  # GGUF general.alignment
 
 
@@ -44,6 +45,9 @@ class ModelConfig:
     interval: int = 4
     eps: float = 1e-6
     rope_base: float = 1.0e7
+    # per-tensor type overrides by name suffix (e.g. {"attn_v.weight": Q6_K}),
+    # for the mixed-type layouts of the reference's source GGUFs
+    overrides: dict = field(default_factory=dict)
 
     def hparams(self, window: int = 0, sink: int = 0) -> Hparams:
         h = Hparams()
@@ -100,6 +104,8 @@ def tensor_plan(cfg: ModelConfig) -> list[tuple[str, int, tuple[int, int]]]:
               (p + "ffn_up.weight", cfg.ffn_type, (H, F)),
               (p + "ffn_down.weight", cfg.ffn_type, (F, H))]
     t += [("output_norm.weight", F32, (H, 1)), ("output.weight", cfg.head_type, (H, cfg.vocab))]
+    if cfg.overrides:
+        t = [(n, next((v for s, v in cfg.overrides.items() if n.endswith(s)), ty), dims) for n, ty, dims in t]
     return t
 
 
@@ -110,6 +116,10 @@ def nbytes(type_id: int, k: int, rows: int) -> int:
         return rows * k // 32 * 34
     if type_id == Q4_K:
         return rows * k // 256 * 144
+    if type_id == Q5_K:
+        return rows * k // 256 * 176
+    if type_id == Q6_K:
+        return rows * k // 256 * 210
     return rows * k * 4
 
 
@@ -177,13 +187,20 @@ def gen_tensor(g: _Gen, type_id: int, k: int, rows: int, name: str):
             q = raw[:, 2:]
             q[q == 0x80] = 0x81
         return raw.reshape(-1)
-    if type_id == Q4_K:
+    if type_id in (Q4_K, Q5_K):
         nb = rows * k // 256
-        raw = g.bytes(n).reshape(nb, 144)
+        raw = g.bytes(n).reshape(nb, 144 if type_id == Q4_K else 176)
         for off in (0, 2):
-            d = _f16_bits(g, abs(g.normal(nb, 0.0, 0.02)) / 64.0)
+            d = _f16_bits(g, abs(g.normal(nb, 0.0, 0.02)) / (64.0 if type_id == Q4_K else 128.0))
             raw[:, off:off + 2] = d.view(np.uint8).reshape(nb, 2) if isinstance(raw, np.ndarray) \
                 else d.view(g.torch.uint8).reshape(nb, 2)
+        return raw.reshape(-1)
+    if type_id == Q6_K:
+        nb = rows * k // 256
+        raw = g.bytes(n).reshape(nb, 210)
+        d = _f16_bits(g, abs(g.normal(nb, 0.0, 0.02)) / 4096.0)
+        raw[:, 208:210] = d.view(np.uint8).reshape(nb, 2) if isinstance(raw, np.ndarray) \
+            else d.view(g.torch.uint8).reshape(nb, 2)
         return raw.reshape(-1)
     # f32 tensors
     cnt = rows * k

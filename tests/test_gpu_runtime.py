@@ -188,3 +188,49 @@ def test_seq_fork_continues_identically(small):
     assert relerr(out[1], out[0].astype(np.float64)) < TOL
     assert relerr(out[2], out[0].astype(np.float64)) < TOL
     rt.close()
+
+
+# ---- mixed weight types, as in the reference's source GGUFs --------------------
+@pytest.fixture(scope="module")
+def mixed():
+    """Q4_K projections with a Q6_K attn_v, Q5_K attn_gate / ssm_out and Q8_0
+    ssm_beta / ssm_alpha (so both projection groups split into runs of one
+    type), a GF4 ffn_gate beside a Q4_K ffn_up, Q6_K ffn_down and head, Q4_K
+    embedding."""
+    cfg = synth.ModelConfig(layers=4, ffn=1024, vocab=4096, proj_type=synth.Q4_K, head_type=synth.Q6_K,
+                            embd_type=synth.Q4_K,
+                            overrides={"attn_v.weight": synth.Q6_K, "attn_gate.weight": synth.Q5_K,
+                                       "ssm_out.weight": synth.Q5_K, "ssm_beta.weight": synth.Q8_0,
+                                       "ssm_alpha.weight": synth.Q8_0, "ffn_up.weight": synth.Q4_K,
+                                       "ffn_down.weight": synth.Q6_K})
+    return synth.build(cfg, seed=5)
+
+
+def test_mixed_type_model_matches_oracle(mixed):
+    rt = Runtime(mixed, ctx=512)
+    orc = OracleModel(mixed)
+    for pos, tok in enumerate(TOKENS[:5]):
+        rt.eval_token(tok, pos, LogitsMode.FULL)
+        e = relerr(rt.copy_logits(), orc.step(tok, pos))
+        assert e < TOL, (pos, e)
+    rt.eval_token(TOKENS[5], 5, LogitsMode.ARGMAX)
+    t, _ = rt.argmax()
+    ref = orc.step(TOKENS[5], 5)
+    top2 = np.sort(ref)[-2:]
+    if top2[1] - top2[0] > 1e-3 * np.abs(ref).max():
+        assert t == int(np.argmax(ref))
+    rt.close()
+
+
+def test_mixed_type_model_batch_of_three_matches_oracle(mixed):
+    seqs = [[3, 9, 27, 81], [100, 200, 300, 400], [4095, 0, 1, 2]]
+    out = None
+    rt = Runtime(mixed, ctx=512, max_seqs=4)
+    ids = [0] + [rt.seq_alloc() for _ in range(2)]
+    orcs = [OracleModel(mixed, tiled=True) for _ in seqs]
+    for pos in range(4):
+        rt.eval_batch(ids, [s[pos] for s in seqs], [pos] * 3, LogitsMode.FULL)
+        out = rt.copy_logits_batch(3)
+        for i, s in enumerate(seqs):
+            assert relerr(out[i], orcs[i].step(s[pos], pos)) < TOL, (pos, i)
+    rt.close()
