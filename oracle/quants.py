@@ -256,9 +256,11 @@ def dequant(type_id: int, raw: np.ndarray, rows: int, k: int, gf4_exact: bool = 
     """Dequantised weights [rows, k] float32.
 
     ``tiled=True`` gives the weights of the reference's multi-row (tiled)
-    path, which dequantises into half tiles (``qw35_tiled_mm.metal:197-213``):
-    GF4 element 4 rounded to half (``gf4_half``, unless ``gf4_exact``) and
-    Q4_K's fp32 ``dl*q - ml`` rounded to half (``qw35_matvec.metal:20-38``).
+    path, which dequantises into half tiles (``qw35_tiled_mm.metal:197-255``):
+    GF4 element 4 rounded to half (``gf4_half``, unless ``gf4_exact``) and the
+    K-quants' fp32 values rounded to half (Q4_K ``dl*q - ml``,
+    ``qw35_matvec.metal:20-38``; Q5_K the same with the fifth bit, :40-64;
+    Q6_K ``d*sc*(q - 32)``, exact in fp32, :66-98).
     """
     if type_id == GF4_TYPE:
         return gf4_dequant(np.asarray(raw).view(np.uint32).reshape(rows, k // 8), exact=gf4_exact,
@@ -268,10 +270,9 @@ def dequant(type_id: int, raw: np.ndarray, rows: int, k: int, gf4_exact: bool = 
     if type_id == Q4_K_TYPE:
         w = q4_k_dequant(raw, rows, k)
         return w.astype(np.float16).astype(np.float32) if tiled else w
-    if type_id == Q5_K_TYPE:
-        return q5_k_dequant(raw, rows, k)
-    if type_id == Q6_K_TYPE:
-        return q6_k_dequant(raw, rows, k)
+    if type_id in (Q5_K_TYPE, Q6_K_TYPE):
+        w = (q5_k_dequant if type_id == Q5_K_TYPE else q6_k_dequant)(raw, rows, k)
+        return w.astype(np.float16).astype(np.float32) if tiled else w
     if type_id == F32_TYPE:
         return np.asarray(raw).view(np.float32).reshape(rows, k)
     raise ValueError(f"unsupported type {type_id}")

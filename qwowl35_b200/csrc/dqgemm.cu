@@ -59,6 +59,8 @@ constexpr int TM = 128;  // weight rows per tile (MMA M = TMEM lanes)
 template <int CODEC> struct DqGeo {
     static constexpr bool Q8 = CODEC == QW35_Q8_0_TYPE;
     static constexpr bool K4 = CODEC == QW35_Q4_K_TYPE;  // one 256-column block per row per chunk
+    static constexpr bool K5 = CODEC == QW35_Q5_K_TYPE;
+    static constexpr bool K6 = CODEC == QW35_Q6_K_TYPE;
     static constexpr int KC = Q8 ? 128 : 256;
     static constexpr int DEC = Q8 ? 8 : 16;                       // decode warps
     static constexpr int EPI = 4;                                 // epilogue warps
@@ -67,7 +69,14 @@ template <int CODEC> struct DqGeo {
     static constexpr int GK = KC / NG;                            // K columns per group (64)
     static constexpr int ACOLS = 128;                             // TMEM columns of one A tile
     static constexpr uint32_t WCODES = 128u * 128u;               // codes bytes of a stage
-    static constexpr uint32_t WS = WCODES + ((Q8 || K4) ? 128u * 16u : 0u);  // + 8 scales / a header per row
+    // extra boxes after the codes, 128 rows each: Q8_0 8 scales (16 B); Q4_K
+    // the block header (16 B); Q5_K the header + 8 high-bit words (32 B); Q6_K
+    // 16 int8 scales (16 B), 16 bytes around the block's f16 d, and 16 words of
+    // high bit pairs (64 B)
+    static constexpr uint32_t HDR = 128u * 16u;                    // offset of a second 16-byte box
+    static constexpr uint32_t HB = K5 ? 128u * 16u : 128u * 32u;   // offset of the high-bit box
+    static constexpr uint32_t WS = WCODES + ((Q8 || K4) ? 128u * 16u
+                                             : K5 ? 128u * 48u : K6 ? 128u * 96u : 0u);
 };
 
 enum DqMode { DQ_STORE = 0, DQ_ACCUM = 1, DQ_DUAL = 2 };
@@ -284,7 +293,8 @@ template <int CODEC, int NP, int MODE, bool EXACT>
 __global__ void __launch_bounds__(DqGeo<CODEC>::THREADS, 1)
 dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUtensorMap map1,
           const __grid_constant__ CUtensorMap smap0, const __grid_constant__ CUtensorMap smap1,
-          const __grid_constant__ CUtensorMap ymap0, const __grid_constant__ CUtensorMap ymap1, DqParams p, int SX,
+          const __grid_constant__ CUtensorMap ymap0, const __grid_constant__ CUtensorMap ymap1,
+          const __grid_constant__ CUtensorMap hmap0, const __grid_constant__ CUtensorMap hmap1, DqParams p, int SX,
           int NW) {
     using G = DqGeo<CODEC>;
     using T = DqTmem<CODEC, NP>;
@@ -363,6 +373,8 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
             DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
                 const CUtensorMap *map = m ? &map1 : &map0;
                 const CUtensorMap *smap = m ? &smap1 : &smap0;
+                const CUtensorMap *hmap = m ? &hmap1 : &hmap0;
+                (void)hmap;
                 for (int kc = c0; kc < c1 && !*abort_flag; ++kc, ++c) {
                     if (c >= NW) dq_wait(&empty_w[rw.s], rw.ph ^ 1u, abort_flag, 8u);
                     if (*abort_flag) break;
@@ -374,7 +386,16 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                     // Q8_0: the 8 block scales (16 B) of each row around this chunk's 4;
                     // Q4_K: the chunk's 16-byte block header of each row (x in words)
                     if constexpr (Q8) tma_load_2d(dst + G::WCODES, smap, (kc * 4) & ~7, tile * TM, &full_w[rw.s], pol);
-                    if constexpr (G::K4) tma_load_2d(dst + G::WCODES, smap, kc * 4, tile * TM, &full_w[rw.s], pol);
+                    if constexpr (G::K4 || G::K5) tma_load_2d(dst + G::WCODES, smap, kc * 4, tile * TM, &full_w[rw.s], pol);
+                    // Q5_K / Q6_K: the chunk's high code bits (8 / 16 words per row)
+                    if constexpr (G::K5) tma_load_2d(dst + G::WCODES + G::HB, hmap, kc * 8, tile * TM, &full_w[rw.s], pol);
+                    if constexpr (G::K6) {
+                        // int8 scales (16 per block), then the 16 bytes holding d of blocks
+                        // kc & ~7 .. kc | 7 (the d array starts k/16 bytes into the row)
+                        tma_load_2d(dst + G::WCODES, smap, kc * 4, tile * TM, &full_w[rw.s], pol);
+                        tma_load_2d(dst + G::WCODES + G::HDR, smap, p.K / 64 + (kc >> 3) * 4, tile * TM, &full_w[rw.s], pol);
+                        tma_load_2d(dst + G::WCODES + G::HB, hmap, kc * 16, tile * TM, &full_w[rw.s], pol);
+                    }
                     rw.next(NW);
                 }
             })
@@ -479,31 +500,58 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                 tc_fence_after();
                 const uint8_t *row = wst + (size_t)sw * WS + r * 128;
                 const uint32_t tcol = tmem + lane_addr + T::A0 + sa * G::ACOLS + grp * 32;
-                if constexpr (G::K4) {
-                    // 64 columns = pieces 2g, 2g+1 of the row = sub-blocks 2g, 2g+1 of the
-                    // block, nibbles in element order.  Nibble n of a word is moved to
-                    // mantissa bit 15 (n even) or 19 (n odd) of 1.0f by one of four
-                    // shifts: f = 1 + q * 2^-8 (or 2^-4), and fma(f, S, -S) with
-                    // S = dl * 2^8 (2^4) is dl * q exactly; minus ml is the reference's
-                    // fp32 value, rounded once to half.
-                    const uint4 h = *reinterpret_cast<const uint4 *>(wst + (size_t)sw * WS + G::WCODES + r * 16);
+                if constexpr (G::K4 || G::K5 || G::K6) {
+                    // K-quants: 64 columns = pieces 2g, 2g+1 of the row (32 weights each).
+                    // Low nibbles plus, for Q5_K / Q6_K, the high bits (stored in nibble
+                    // slots) are merged into bytes with one bit-select each (even
+                    // elements: slot bits moved up by 4; odd: in place), then each byte
+                    // enters the mantissa of 2^23 by one PRMT.  Value = the reference's
+                    // fp32 dl*q - ml (Q4_K, Q5_K: dl*q is exact, one rounding) or
+                    // d*sc*(q - 32) (Q6_K, exact), rounded once to half.
+                    const uint8_t *aux = wst + (size_t)sw * WS + G::WCODES;
                     uint32_t o[32];
 #pragma unroll
                     for (int i = 0; i < 2; ++i) {
-                        float dl, ml;
-                        q4k_scale_min(h, 2 * grp + i, dl, ml);
-                        const float s8 = dl * 256.0f, s4 = dl * 16.0f;
-                        const uint4 w4 = *reinterpret_cast<const uint4 *>(row + (((2 * grp + i) ^ (r & 7)) << 4));
+                        const int pc = 2 * grp + i;  // piece = 32 elements of the block
+                        const uint4 w4 = *reinterpret_cast<const uint4 *>(row + ((pc ^ (r & 7)) << 4));
                         const uint32_t ws4[4] = {w4.x, w4.y, w4.z, w4.w};
+                        float mul[4], sub4[4];  // per word: value = mul * (byte float) - sub
+                        uint32_t hp[4];          // per word: high parts in nibble slots (bits 0-1 of a slot)
+                        if constexpr (G::K4 || G::K5) {
+                            float dl, ml;
+                            q4k_scale_min(*reinterpret_cast<const uint4 *>(aux + r * 16), pc, dl, ml);
+                            const uint32_t hb = G::K5 ? *reinterpret_cast<const uint32_t *>(aux + G::HB + r * 32 + pc * 4) : 0u;
+#pragma unroll
+                            for (int wd = 0; wd < 4; ++wd) {
+                                mul[wd] = dl;
+                                sub4[wd] = ml;
+                                hp[wd] = (hb >> wd) & 0x11111111u;
+                            }
+                        } else {
+                            const uint32_t sc2 = *reinterpret_cast<const unsigned short *>(aux + r * 16 + pc * 2);
+                            const float d = __half2float(__ushort_as_half(
+                                *reinterpret_cast<const unsigned short *>(aux + G::HDR + r * 16 + (kc & 7) * 2)));
+                            const uint2 hb = *reinterpret_cast<const uint2 *>(aux + G::HB + r * 64 + pc * 8);
+                            const float d0 = d * (float)(int8_t)(sc2 & 0xffu), d1 = d * (float)(int8_t)(sc2 >> 8);
+                            mul[0] = d0; mul[1] = d0; mul[2] = d1; mul[3] = d1;
+                            hp[0] = hb.x & 0x33333333u; hp[1] = (hb.x >> 2) & 0x33333333u;
+                            hp[2] = hb.y & 0x33333333u; hp[3] = (hb.y >> 2) & 0x33333333u;
+                            sub4[0] = sub4[1] = sub4[2] = sub4[3] = 0.0f;
+                        }
+                        // byte-float offset: 2^23 (+ 32 for Q6_K's code bias)
+                        constexpr float kOff = G::K6 ? 8388640.0f : 8388608.0f;
 #pragma unroll
                         for (int wd = 0; wd < 4; ++wd) {
                             const uint32_t wv = ws4[wd];
-                            const uint32_t sh[4] = {wv << 15, wv << 7, wv >> 1, wv >> 9};
+                            // bytes of ce: elements 0,2,4,6; of co: elements 1,3,5,7
+                            const uint32_t ce = (wv & 0x0F0F0F0Fu) | ((hp[wd] << 4) & 0xF0F0F0F0u);
+                            const uint32_t co = ((wv >> 4) & 0x0F0F0F0Fu) | (hp[wd] & 0xF0F0F0F0u);
 #pragma unroll
                             for (int t = 0; t < 4; ++t) {
-                                const float fe = __uint_as_float((sh[t] & (0xFu << 15)) | 0x3F800000u);
-                                const float fo = __uint_as_float((sh[t] & (0xFu << 19)) | 0x3F800000u);
-                                const float ve = fmaf(fe, s8, -s8) - ml, vo = fmaf(fo, s4, -s4) - ml;
+                                const float qe = __uint_as_float(__byte_perm(ce, 0x4B000000u, 0x7540u | t)) - kOff;
+                                const float qo = __uint_as_float(__byte_perm(co, 0x4B000000u, 0x7540u | t)) - kOff;
+                                const float ve = G::K6 ? mul[wd] * qe : fmaf(mul[wd], qe, -sub4[wd]);
+                                const float vo = G::K6 ? mul[wd] * qo : fmaf(mul[wd], qo, -sub4[wd]);
                                 const __half2 hv = __floats2half2_rn(ve, vo);
                                 o[16 * i + 4 * wd + t] = *reinterpret_cast<const uint32_t *>(&hv);
                             }
@@ -894,9 +942,11 @@ bool weight_map(uint32_t type_id, const void *w, uint32_t rows, uint32_t k, CUte
     cuuint32_t box[2], estr[2] = {1, 1};
     CUtensorMapDataType dt;
     // 128 rows x 128 bytes per box, 128B-swizzled (16-byte piece q of row r at q ^ (r % 8))
-    if (type_id == QW35_GF4_TYPE || type_id == QW35_Q4_K_TYPE) {  // k/2 bytes of codes per row
+    if (type_id != QW35_Q8_0_TYPE) {  // k/2 bytes of nibbles per row (Q5_K / Q6_K: then the high bits)
         dt = CU_TENSOR_MAP_DATA_TYPE_UINT32;
-        dims[0] = k / 8; dims[1] = rows; strides[0] = (cuuint64_t)k / 2;
+        dims[0] = k / 8; dims[1] = rows;
+        strides[0] = type_id == QW35_Q5_K_TYPE ? (cuuint64_t)k / 2 + k / 8
+                   : type_id == QW35_Q6_K_TYPE ? (cuuint64_t)k / 2 + k / 4 : (cuuint64_t)k / 2;
         box[0] = 32; box[1] = TM;
     } else {
         dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
@@ -939,13 +989,15 @@ bool scale_map(const void *w, uint32_t rows, uint32_t k, CUtensorMap *out) {
     return true;
 }
 
-// Tensor map over the Q4_K headers plane ([rows][K/256] x 16 bytes, after the
-// codes plane): boxes of one header (4 words) x 128 rows.
-bool header_map(const void *w, uint32_t rows, uint32_t k, CUtensorMap *out) {
+// Unswizzled uint32 tensor map over a [rows][dim0 words] region at `base`
+// with a row pitch of `pitch` bytes, boxes of box0 words x 128 rows (cached:
+// weights are immutable).  Serves the K-quant side planes: Q4_K / Q5_K block
+// headers, Q6_K scales and d, Q5_K / Q6_K high bits.
+bool plain_map(const void *base, uint64_t dim0, uint32_t rows, uint64_t pitch, uint32_t box0, CUtensorMap *out) {
     static std::mutex mu;
-    static std::map<std::tuple<const void *, uint32_t, uint32_t>, CUtensorMap> cache;
+    static std::map<std::tuple<const void *, uint64_t, uint32_t, uint64_t, uint32_t>, CUtensorMap> cache;
     std::lock_guard<std::mutex> g(mu);
-    auto key = std::make_tuple(w, rows, k);
+    auto key = std::make_tuple(base, dim0, rows, pitch, box0);
     auto it = cache.find(key);
     if (it != cache.end()) {
         *out = it->second;
@@ -954,16 +1006,33 @@ bool header_map(const void *w, uint32_t rows, uint32_t k, CUtensorMap *out) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     CUtensorMap m;
-    cuuint64_t dims[2] = {k / 64, rows}, strides[1] = {(cuuint64_t)k / 16};
-    cuuint32_t box[2] = {4, TM}, estr[2] = {1, 1};
-    void *base = static_cast<uint8_t *>(const_cast<void *>(w)) + (size_t)rows * (k / 2);
-    if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
-        CUDA_SUCCESS)
+    cuuint64_t dims[2] = {dim0, rows}, strides[1] = {pitch};
+    cuuint32_t box[2] = {box0, TM}, estr[2] = {1, 1};
+    if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void *>(base), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
         return false;
     cache[key] = m;
     *out = m;
     return true;
+}
+
+// Side-plane maps of a K-quant weight: s = headers (Q4_K / Q5_K, one 16-byte
+// box per block) or the Q6_K scales row (16-byte boxes); h = high bits (Q5_K
+// 8 words, Q6_K 16 words per block).
+bool kquant_maps(uint32_t type_id, const void *w, uint32_t rows, uint32_t k, CUtensorMap *s, CUtensorMap *h) {
+    const uint8_t *b = static_cast<const uint8_t *>(w);
+    if (type_id == QW35_Q4_K_TYPE) return plain_map(b + (size_t)rows * (k / 2), k / 64, rows, k / 16, 4, s);
+    if (type_id == QW35_Q5_K_TYPE) {
+        const uint64_t cr = k / 2 + k / 8;
+        return plain_map(b + (size_t)rows * cr, k / 64, rows, k / 16, 4, s) &&
+               plain_map(b + k / 2, k / 32, rows, cr, 8, h);
+    }
+    if (type_id == QW35_Q6_K_TYPE) {
+        const uint64_t cr = k / 2 + k / 4, sr = q6k_scale_row(k);
+        return plain_map(b + (size_t)rows * cr, sr / 4, rows, sr, 4, s) && plain_map(b + k / 2, k / 16, rows, cr, 16, h);
+    }
+    return false;
 }
 
 // Tensor map over an output y [B][rows] f32 (x = row, y = batch column): boxes
@@ -1018,9 +1087,10 @@ bool dq_supported(const MatvecArgs &a) {
     // TMA needs 16-byte aligned weights; the activation prep reads x and the
     // norm weight 16 bytes at a time
     auto a16 = [](const void *p) { return ((uintptr_t)p & 15u) == 0; };
-    // K % 256: GF4 / Q4_K chunks are 256 columns; Q8_0 scale boxes span two 128-column chunks
+    // K % 256: GF4 / K-quant chunks are 256 columns; Q8_0 scale boxes span two 128-column chunks
     return a.batch >= kDqMinBatch && a.batch <= 64 &&
-           (a.type_id == QW35_GF4_TYPE || a.type_id == QW35_Q8_0_TYPE || a.type_id == QW35_Q4_K_TYPE) &&
+           (a.type_id == QW35_GF4_TYPE || a.type_id == QW35_Q8_0_TYPE || a.type_id == QW35_Q4_K_TYPE ||
+            a.type_id == QW35_Q5_K_TYPE || a.type_id == QW35_Q6_K_TYPE) &&
            a.k % 256 == 0 &&
            a16(a.w0) && a16(a.w1) && a16(a.x) && a16(a.norm_w) && encode_fn() != nullptr &&
            !getenv("QW35_NO_TCGEN05");
@@ -1051,10 +1121,12 @@ cudaError_t dq_reserve(int max_batch, uint32_t max_k, uint32_t max_rows_out) {
     return scratch_get(dq_scratch_bytes(max_batch, max_k, max_rows_out), &p, nullptr);
 }
 
+struct DqMaps {
+    CUtensorMap m0, m1, s0, s1, y0, y1, h0, h1;  // codes, side planes, outputs, high bits (per matrix)
+};
+
 template <int CODEC, int NP, int MODE, bool EXACT>
-static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, const CUtensorMap &s0,
-                             const CUtensorMap &s1, const CUtensorMap &y0, const CUtensorMap &y1, DqParams p,
-                             cudaStream_t st) {
+static cudaError_t dq_launch(const DqMaps &M, DqParams p, cudaStream_t st) {
     auto kern = dq_kernel<CODEC, NP, MODE, EXACT>;
     // SX activation stages (two when they are 64 KB), then as many weight stages as fit
     // stages <= 176 KB (+ 16 KB epilogue staging), so a 128-thread activation
@@ -1062,7 +1134,8 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, const
     constexpr uint32_t budget = 176u * 1024u;
     constexpr uint32_t xs = dq_xstage<CODEC, NP>(), ws = DqGeo<CODEC>::WS;
     int SX = xs >= 65536u ? 2 : 3;
-    int NW = std::min(4, (int)((budget - SX * xs) / ws));
+    // (at least two weight stages: Q6_K's 28 KB stages then pass the budget)
+    int NW = std::max(2, std::min(4, (int)((budget - SX * xs) / ws)));
     static const int env_sx = getenv("QW35_DQ_SX") ? atoi(getenv("QW35_DQ_SX")) : 0;  // tuning experiments
     static const int env_nw = getenv("QW35_DQ_NW") ? atoi(getenv("QW35_DQ_NW")) : 0;
     if (env_sx >= 2 && env_nw >= 2 && env_sx * xs + env_nw * ws <= budget) {
@@ -1096,7 +1169,7 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, const
     attrs[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = getenv("QW35_NO_PDL") ? 0 : 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, m0, m1, s0, s1, y0, y1, p, SX, NW);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, M.m0, M.m1, M.s0, M.s1, M.y0, M.y1, M.h0, M.h1, p, SX, NW);
     if (p.trace) {
         unsigned long long h[256 * 10];
         cudaMemcpy(h, trace, sizeof(h), cudaMemcpyDeviceToHost);
@@ -1120,17 +1193,24 @@ static cudaError_t dq_launch(const CUtensorMap &m0, const CUtensorMap &m1, const
 }
 
 template <int CODEC, int NP>
-static cudaError_t dq_dispatch_mode(int mode, bool exact, const CUtensorMap &m0, const CUtensorMap &m1,
-                                    const CUtensorMap &s0, const CUtensorMap &s1, const CUtensorMap &y0,
-                                    const CUtensorMap &y1, const DqParams &p, cudaStream_t st) {
-    if (CODEC == QW35_GF4_TYPE && !exact) {
-        if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, false>(m0, m1, s0, s1, y0, y1, p, st);
-        if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, false>(m0, m1, s0, s1, y0, y1, p, st);
-        return dq_launch<CODEC, NP, DQ_DUAL, false>(m0, m1, s0, s1, y0, y1, p, st);
+static cudaError_t dq_dispatch_mode(int mode, bool exact, const DqMaps &M, const DqParams &p, cudaStream_t st) {
+    if constexpr (CODEC == QW35_GF4_TYPE) {
+        if (!exact) {
+            if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, false>(M, p, st);
+            if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, false>(M, p, st);
+            return dq_launch<CODEC, NP, DQ_DUAL, false>(M, p, st);
+        }
     }
-    if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, true>(m0, m1, s0, s1, y0, y1, p, st);
-    if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, true>(m0, m1, s0, s1, y0, y1, p, st);
-    return dq_launch<CODEC, NP, DQ_DUAL, true>(m0, m1, s0, s1, y0, y1, p, st);
+    if (mode == DQ_STORE) return dq_launch<CODEC, NP, DQ_STORE, true>(M, p, st);
+    if (mode == DQ_ACCUM) return dq_launch<CODEC, NP, DQ_ACCUM, true>(M, p, st);
+    return dq_launch<CODEC, NP, DQ_DUAL, true>(M, p, st);
+}
+
+template <int CODEC>
+static cudaError_t dq_dispatch_np(int NP, int mode, bool exact, const DqMaps &M, const DqParams &p, cudaStream_t st) {
+    if (NP == 16) return dq_dispatch_mode<CODEC, 16>(mode, exact, M, p, st);
+    if (NP == 32) return dq_dispatch_mode<CODEC, 32>(mode, exact, M, p, st);
+    return dq_dispatch_mode<CODEC, 64>(mode, exact, M, p, st);
 }
 
 // mode: 0 store, 1 accumulate, 2 swiglu pair, 3 logits for the argmax head
@@ -1138,19 +1218,24 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
     const int B = a.batch, NP = dq_np(B);
     const int K = (int)a.k, rows = (int)a.rows;
     const bool dual = mode == 2;
-    CUtensorMap m0, m1;
+    DqMaps M;
+    CUtensorMap &m0 = M.m0, &m1 = M.m1;
     if (!weight_map(a.type_id, a.w0, a.rows, a.k, &m0)) return cudaErrorInvalidValue;
     if (dual && !weight_map(a.type_id, a.w1, a.rows, a.k, &m1)) return cudaErrorInvalidValue;
     if (!dual) m1 = m0;
-    CUtensorMap s0 = m0, s1 = m1;  // scales (Q8_0) / headers (Q4_K) maps; unused for GF4
+    // side planes: Q8_0 scales, K-quant headers / scales and high bits (unused maps stay copies)
+    M.s0 = M.h0 = m0;
+    M.s1 = M.h1 = m1;
     if (a.type_id == QW35_Q8_0_TYPE) {
-        if (!scale_map(a.w0, a.rows, a.k, &s0)) return cudaErrorInvalidValue;
-        if (dual && !scale_map(a.w1, a.rows, a.k, &s1)) return cudaErrorInvalidValue;
-        if (!dual) s1 = s0;
-    } else if (a.type_id == QW35_Q4_K_TYPE) {
-        if (!header_map(a.w0, a.rows, a.k, &s0)) return cudaErrorInvalidValue;
-        if (dual && !header_map(a.w1, a.rows, a.k, &s1)) return cudaErrorInvalidValue;
-        if (!dual) s1 = s0;
+        if (!scale_map(a.w0, a.rows, a.k, &M.s0)) return cudaErrorInvalidValue;
+        if (dual && !scale_map(a.w1, a.rows, a.k, &M.s1)) return cudaErrorInvalidValue;
+    } else if (a.type_id != QW35_GF4_TYPE) {
+        if (!kquant_maps(a.type_id, a.w0, a.rows, a.k, &M.s0, &M.h0)) return cudaErrorInvalidValue;
+        if (dual && !kquant_maps(a.type_id, a.w1, a.rows, a.k, &M.s1, &M.h1)) return cudaErrorInvalidValue;
+    }
+    if (!dual) {
+        M.s1 = M.s0;
+        M.h1 = M.h0;
     }
     const size_t extra = (mode == 2) ? (size_t)2 * B * rows * 4 : (mode == 3 && !a.y) ? (size_t)B * rows * 4 : 0;
     const DqScratch lay = dq_scratch_layout(B, a.k, a.rows, extra);
@@ -1191,7 +1276,8 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
     // outputs that split tiles add into start at zero
     const bool zero = dmode != DQ_ACCUM && gran < nch;
     // TMA bulk reductions need 16-byte aligned outputs with 16-byte row strides
-    CUtensorMap y0m = m0, y1m = m0;
+    CUtensorMap &y0m = M.y0, &y1m = M.y1;
+    y0m = y1m = m0;
     p.red_tma = (rows % 4 == 0) && ((uintptr_t)y0 & 15u) == 0 && (!dual || ((uintptr_t)y1 & 15u) == 0) &&
                 out_map(y0, rows, B, &y0m) && (!dual || out_map(y1, rows, B, &y1m));
     if (!dual) y1m = y0m;
@@ -1217,18 +1303,13 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const bool exact = (a.flags & QW35_MV_GF4_EXACT) != 0;
-    if (a.type_id == QW35_GF4_TYPE) {
-        if (NP == 16) e = dq_dispatch_mode<QW35_GF4_TYPE, 16>(dmode, exact, m0, m1, s0, s1, y0m, y1m, p, st);
-        else if (NP == 32) e = dq_dispatch_mode<QW35_GF4_TYPE, 32>(dmode, exact, m0, m1, s0, s1, y0m, y1m, p, st);
-        else e = dq_dispatch_mode<QW35_GF4_TYPE, 64>(dmode, exact, m0, m1, s0, s1, y0m, y1m, p, st);
-    } else if (a.type_id == QW35_Q4_K_TYPE) {
-        if (NP == 16) e = dq_dispatch_mode<QW35_Q4_K_TYPE, 16>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
-        else if (NP == 32) e = dq_dispatch_mode<QW35_Q4_K_TYPE, 32>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
-        else e = dq_dispatch_mode<QW35_Q4_K_TYPE, 64>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
-    } else {
-        if (NP == 16) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 16>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
-        else if (NP == 32) e = dq_dispatch_mode<QW35_Q8_0_TYPE, 32>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
-        else e = dq_dispatch_mode<QW35_Q8_0_TYPE, 64>(dmode, true, m0, m1, s0, s1, y0m, y1m, p, st);
+    switch (a.type_id) {
+        case QW35_GF4_TYPE: e = dq_dispatch_np<QW35_GF4_TYPE>(NP, dmode, exact, M, p, st); break;
+        case QW35_Q8_0_TYPE: e = dq_dispatch_np<QW35_Q8_0_TYPE>(NP, dmode, true, M, p, st); break;
+        case QW35_Q4_K_TYPE: e = dq_dispatch_np<QW35_Q4_K_TYPE>(NP, dmode, true, M, p, st); break;
+        case QW35_Q5_K_TYPE: e = dq_dispatch_np<QW35_Q5_K_TYPE>(NP, dmode, true, M, p, st); break;
+        case QW35_Q6_K_TYPE: e = dq_dispatch_np<QW35_Q6_K_TYPE>(NP, dmode, true, M, p, st); break;
+        default: return cudaErrorInvalidValue;
     }
     if (e != cudaSuccess) return e;
     if (mode == 2) {

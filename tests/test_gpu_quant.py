@@ -167,7 +167,7 @@ def test_no_device_wait_timed_out():
 
 
 # ---- batched (B >= 16) tensor-core path -----------------------------------------
-@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE])
+@pytest.mark.parametrize("t", CODECS)
 @pytest.mark.parametrize("b", [3, 8, 16, 32, 64, 20])
 @pytest.mark.parametrize("shape", [(12288, 4096), (4096, 12288), (333, 1280)])
 def test_batched_matvec_parity(t, b, shape):
@@ -182,7 +182,7 @@ def test_batched_matvec_parity(t, b, shape):
         assert relerr(ye, O.matvec(Q.dequant(t, raw, rows, k, gf4_exact=True), x)) < TOL
 
 
-@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE])
+@pytest.mark.parametrize("t", CODECS)
 def test_batched_accumulate_swiglu_and_head(t):
     rows, k, b = 4096, 4096, 32
     raw, w = make(t, rows, k, 22)
@@ -225,7 +225,7 @@ def _random_words_all_scales(rng, rows, k):
     return ((w & np.uint32(0xFFFFFF00)) | sb).view(np.uint8).reshape(-1)
 
 
-@pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE])
+@pytest.mark.parametrize("t", CODECS)
 @pytest.mark.parametrize("exact", [False, True])
 def test_batched_path_weights_bit_exact(t, exact):
     """One-hot activation rows make y[b][r] = W[r][k_b] a single exact product,
@@ -238,12 +238,17 @@ def test_batched_path_weights_bit_exact(t, exact):
     rng = np.random.default_rng(31)
     if t == Q.GF4_TYPE:
         raw = _random_words_all_scales(rng, rows, k)
-    elif t == Q.Q4_K_TYPE:  # d, dmin over a wide range, both signs
+    elif t in (Q.Q4_K_TYPE, Q.Q5_K_TYPE):  # d, dmin over a wide range, both signs
         raw = Q.gen_weight(rng, t, rows, k)
-        blocks = raw.reshape(-1, 144)
+        blocks = raw.reshape(-1, Q.BLOCK[t][1])
         for off in (0, 2):
             v = (rng.standard_normal(blocks.shape[0]) * 10.0 ** rng.integers(-4, 1, size=blocks.shape[0]))
             blocks[:, off:off + 2] = v.astype(np.float16).view(np.uint8).reshape(-1, 2)
+    elif t == Q.Q6_K_TYPE:  # d over a wide range, both signs (scales are signed too)
+        raw = Q.gen_weight(rng, t, rows, k)
+        blocks = raw.reshape(-1, 210)
+        v = rng.standard_normal(blocks.shape[0]) * 10.0 ** rng.integers(-5, 0, size=blocks.shape[0])
+        blocks[:, 208:210] = v.astype(np.float16).view(np.uint8).reshape(-1, 2)
     else:
         raw = Q.gen_weight(rng, t, rows, k)
         blocks = raw.reshape(-1, 34)
