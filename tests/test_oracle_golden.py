@@ -106,6 +106,32 @@ def test_q6_k_code_order_follows_the_block_layout():
     np.testing.assert_array_equal(Q.q6_k_codes(blk[None]), want[None])
 
 
+def test_q5_k_code_order_follows_the_block_layout():
+    # code of element 32j + l: nibble of qs[32(j//2) + l] (high for odd j) + 16 * bit j of qh[l]
+    blk = np.zeros(176, dtype=np.uint8)
+    want = (np.arange(256) * 7) % 32
+    for e in range(256):
+        j, l = divmod(e, 32)
+        blk[48 + 32 * (j // 2) + l] |= (want[e] & 15) << (4 * (j % 2))
+        blk[16 + l] |= (want[e] >> 4) << j
+    np.testing.assert_array_equal(Q.q5_k_codes(blk[None]), want[None])
+
+
+@pytest.mark.parametrize("t", [Q.Q4_K_TYPE, Q.Q5_K_TYPE, Q.Q6_K_TYPE])
+def test_tiled_semantics_round_k_quants_to_half(t):
+    rng = np.random.default_rng(4)
+    raw = Q.gen_weight(rng, t, 4, 512)
+    w, wt = Q.dequant(t, raw, 4, 512), Q.dequant(t, raw, 4, 512, tiled=True)
+    np.testing.assert_array_equal(wt, w.astype(np.float16).astype(np.float32))
+    assert np.any(wt != w)  # the fp32 values are not all halves
+
+
+def test_q8_0_tiled_semantics_keep_fp32():
+    rng = np.random.default_rng(5)
+    raw = Q.gen_weight(rng, Q.Q8_0_TYPE, 4, 256)
+    np.testing.assert_array_equal(Q.dequant(Q.Q8_0_TYPE, raw, 4, 256, tiled=True), Q.dequant(Q.Q8_0_TYPE, raw, 4, 256))
+
+
 @pytest.mark.parametrize("t", [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE, Q.Q5_K_TYPE, Q.Q6_K_TYPE])
 def test_generators_row_bytes(t):
     rng = np.random.default_rng(1)
