@@ -196,6 +196,59 @@ def gqa_decode(q, gate, K, V, window: int = 0, sink: int = 0, scale: float = 1.0
     return out
 
 
+# --------------------------------------------------------------------------
+# q8_0 KV cache (qw35_attention.metal:425-793)
+# --------------------------------------------------------------------------
+def q8_0_kv_quantize(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """fp32 rows [..., 32n] -> (d f16 [..., n], qs int8 [..., 32n]), one block
+    per 32 values (qw35_q8_0_quantize_block, qw35_attention.metal:429-440):
+    d = amax / 127 in fp32, id = 1 / d (0 for an all-zero block), qs =
+    clamp(round(x * id), -127, 127) with rounding half away from zero; the
+    codes use the fp32 d, the block stores half(d).  IEEE fp32 division and
+    product here; the reference's shaders are built with Metal's default fast
+    math (qw35-server/build.rs:150-156 passes no -fno-fast-math), so a value
+    that lands exactly on a .5 boundary may round differently there."""
+    x = np.asarray(x, dtype=np.float32)
+    b = x.reshape(x.shape[:-1] + (-1, 32))
+    amax = np.max(np.abs(b), axis=-1)
+    d = (amax / np.float32(127.0)).astype(np.float32)
+    safe = np.where(d != 0, d, np.float32(1.0)).astype(np.float32)
+    inv = np.where(d != 0, np.float32(1.0) / safe, np.float32(0.0)).astype(np.float32)
+    y = (b * inv[..., None]).astype(np.float32).astype(F64)  # fp32 product, exact in f64
+    q = np.sign(y) * np.floor(np.abs(y) + 0.5)               # round half away from zero
+    qs = np.clip(q, -127, 127).astype(np.int8).reshape(x.shape)
+    return d.astype(np.float16), qs
+
+
+def q8_0_kv_dequant(d: np.ndarray, qs: np.ndarray) -> np.ndarray:
+    """float(half d) * qs per block (qw35_q8_0_dequant_qi times the block's d,
+    qw35_attention.metal:442-445, :670-682), fp64."""
+    qs = np.asarray(qs)
+    b = qs.reshape(qs.shape[:-1] + (-1, 32)).astype(F64)
+    return (b * np.asarray(d, dtype=np.float16).astype(F64)[..., None]).reshape(qs.shape)
+
+
+def attn_preprocess_q8_0(q_full, k, v, q_norm_w, k_norm_w, pos, freq, eps=1e-6):
+    """q8_0 twin of attn_preprocess (qw35_attention.metal:452-533): K after
+    norm + RoPE and V quantised per 32-value block -> (q, gate, (kd, kqs), (vd, vqs)).
+    K is formed in fp64 and rounded to fp32 before quantisation (the kernel
+    forms it in fp32, so a code can differ by one where the two fp32 values
+    differ in the last place)."""
+    q_full = np.asarray(q_full, dtype=F64).reshape(N_HEAD, 2 * HD)
+    q = _norm_rope(q_full[:, :HD], q_norm_w, pos, freq, eps)
+    gate = q_full[:, HD:]
+    kk = _norm_rope(np.asarray(k, dtype=F64).reshape(N_KV, HD), k_norm_w, pos, freq, eps).astype(np.float32)
+    vv = np.asarray(v, dtype=np.float32).reshape(N_KV, HD)
+    return q, gate, q8_0_kv_quantize(kk), q8_0_kv_quantize(vv)
+
+
+def gqa_decode_q8_0(q, gate, Kq, Vq, window: int = 0, sink: int = 0, scale: float = 1.0 / 16.0):
+    """Decode attention over a q8_0 KV cache (qw35_attention_gqa_flash_decode_q8_0_f32,
+    qw35_attention.metal:625-690): Kq / Vq = (d [L, 4, 8] f16, qs [L, 4, 256] int8),
+    dequantised per block, then gqa_decode."""
+    return gqa_decode(q, gate, q8_0_kv_dequant(*Kq), q8_0_kv_dequant(*Vq), window, sink, scale)
+
+
 def kv_address(chunk_table: np.ndarray, t: int, chunk: int = CHUNK):
     """Chunk-table indexing: position t lives in chunk chunk_table[t // chunk] at row t % chunk."""
     return int(chunk_table[t // chunk]), t % chunk

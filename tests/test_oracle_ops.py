@@ -50,3 +50,54 @@ def test_rope_freqs_ladder():
     f = O.rope_freqs(1.0e7)
     assert f.dtype == np.float32 and f[0] == 1.0 and len(f) == 32
     assert np.all(np.diff(f) < 0)
+
+
+# ---- q8_0 KV cache (qw35_attention.metal:425-793) ------------------------------
+def test_q8_0_kv_quantize_known_blocks():
+    x = np.zeros((3, 32), dtype=np.float32)
+    x[1, :] = np.arange(-16, 16, dtype=np.float32) * 8.0      # amax 128 -> d = 128/127
+    x[2, 0], x[2, 1], x[2, 2], x[2, 3] = 127.0, 2.5, -2.5, 0.49999997
+    d, qs = O.q8_0_kv_quantize(x)
+    assert d[0] == 0 and not qs[0].any()                       # all-zero block
+    assert qs[1, 0] == -127 and qs[1, 31] == round(120 * 127 / 128)
+    assert d[2] == np.float16(1.0)
+    assert list(qs[2, :4]) == [127, 3, -3, 0]                   # half away from zero; 0.49999997 -> 0
+
+
+def test_q8_0_kv_codes_use_the_fp32_scale_and_store_half():
+    rng = np.random.default_rng(0)
+    x = rng.normal(0, 1, size=(64, 32)).astype(np.float32)
+    d, qs = O.q8_0_kv_quantize(x)
+    d32 = np.max(np.abs(x), axis=1) / np.float32(127.0)
+    assert d.shape == (64, 1) and np.any(d[:, 0].astype(np.float32) != d32)  # half(d) differs from the fp32 d
+    ref = np.clip(np.round(x.astype(np.float64) / d32[:, None].astype(np.float64)), -127, 127)
+    assert np.max(np.abs(qs.astype(np.float64) - ref)) <= 1     # ties / reciprocal rounding only
+    deq = O.q8_0_kv_dequant(d, qs)
+    assert np.max(np.abs(deq - x) / np.max(np.abs(x), axis=1, keepdims=True)) < 1.0 / 127 + 1e-3
+
+
+def test_gqa_decode_q8_0_close_to_f16_cache():
+    rng = np.random.default_rng(1)
+    L = 300
+    K = rng.normal(0, 1, size=(L, 4, 256)).astype(np.float32)
+    V = rng.normal(0, 1, size=(L, 4, 256)).astype(np.float32)
+    q, gate = rng.normal(0, 1, size=(16, 256)), rng.normal(0, 1, size=(16, 256))
+    ref = O.gqa_decode(q, gate, K.astype(np.float16), V.astype(np.float16))
+    got = O.gqa_decode_q8_0(q, gate, O.q8_0_kv_quantize(K), O.q8_0_kv_quantize(V))
+    assert np.max(np.abs(got - ref)) / np.max(np.abs(ref)) < 0.05
+    kd, kq = O.q8_0_kv_quantize(K)
+    assert kd.shape == (L, 4, 8) and kq.shape == (L, 4, 256) and kq.dtype == np.int8
+
+
+def test_attn_preprocess_q8_0_matches_f16_twin_up_to_quantisation():
+    rng = np.random.default_rng(2)
+    qf, k, v = rng.normal(0, 1, (16, 512)), rng.normal(0, 1, (4, 256)), rng.normal(0, 1, (4, 256))
+    qn, kn = np.abs(rng.normal(1, 0.1, 256)), np.abs(rng.normal(1, 0.1, 256))
+    fr = O.rope_freqs()
+    q16, g16, k16, v16 = O.attn_preprocess(qf, k, v, qn, kn, 7, fr)
+    q8, g8, (kd, kq), (vd, vq) = O.attn_preprocess_q8_0(qf, k, v, qn, kn, 7, fr)
+    np.testing.assert_array_equal(q8, q16)
+    np.testing.assert_array_equal(g8, g16)
+    kdq = O.q8_0_kv_dequant(kd, kq)
+    assert np.max(np.abs(kdq - k16.astype(np.float64))) <= np.max(np.abs(k16.astype(np.float64))) / 127 + 1e-2
+    np.testing.assert_array_equal(O.q8_0_kv_quantize(v.astype(np.float32))[1], vq)
