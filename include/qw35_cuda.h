@@ -113,6 +113,22 @@ int qw35_cuda_gqa_decode(uint32_t n_seq, const float *q, const float *gate, cons
                          uint64_t v_off, int32_t window, int32_t sink, float *out, void *workspace,
                          uint64_t workspace_bytes, void *stream, char *err, uintptr_t err_len);
 
+// q8_0 KV twins (qw35_attn_decode_preprocess_q8_0_f32 and
+// qw35_attention_gqa_flash_decode[_split]_q8_0_f32, qw35_attention.metal:425-793):
+// same arguments, planes of [4 kv heads][256 pos][8 blocks {f16 d; int8 qs[32]}]
+// (272 bytes per head-row).  The preprocess quantises each 32-value block of
+// K (after norm + RoPE) and V as the reference does: d = amax / 127, codes
+// round(x / d) clamped to +-127, d stored as f16.
+int qw35_cuda_attn_preprocess_q8_0(uint32_t n_seq, const float *qkv, uint32_t qkv_stride, const float *q_norm_w,
+                                   const float *k_norm_w, const float *rope_freq, const int32_t *pos,
+                                   const uint64_t *chunk_ptrs, uint32_t max_chunks, uint64_t k_off, uint64_t v_off,
+                                   float *q_out, float *gate_out, float eps, void *stream, char *err,
+                                   uintptr_t err_len);
+int qw35_cuda_gqa_decode_q8_0(uint32_t n_seq, const float *q, const float *gate, const int32_t *seq_len,
+                              uint32_t max_len, const uint64_t *chunk_ptrs, uint32_t max_chunks, uint64_t k_off,
+                              uint64_t v_off, int32_t window, int32_t sink, float *out, void *workspace,
+                              uint64_t workspace_bytes, void *stream, char *err, uintptr_t err_len);
+
 // Allocation-free twin of qw35_cuda_gqa_decode (no counterpart in the
 // reference).  For callers that cannot allocate device memory where they
 // decode (their GPU memory belongs to another allocator, or a cudaMalloc and

@@ -16,11 +16,14 @@ from . import quants as Q
 
 
 class OracleModel:
-    def __init__(self, synth, gf4_exact: bool = False, window: int = 0, sink: int = 0, tiled: bool = False):
+    def __init__(self, synth, gf4_exact: bool = False, window: int = 0, sink: int = 0, tiled: bool = False,
+                 kv_q8: bool = False):
         """tiled: weights as the reference's multi-token (tiled) path rounds them
-        to half (GF4 element 4, Q4_K values) -- the semantics of the batched
-        tensor-core path (3 or more rows)."""
+        to half (GF4 element 4, K-quant values) -- the semantics of the batched
+        tensor-core path (3 or more rows).  kv_q8: the KV cache holds q8_0
+        blocks (kv_cache_type 1, qw35_attention.metal:425-793)."""
         self.tiled = tiled
+        self.kv_q8 = kv_q8
         self.m = synth
         self.cfg = synth.cfg
         self.gf4_exact = gf4_exact
@@ -71,8 +74,13 @@ class OracleModel:
                 q_full = O.matvec(self.w(p + "attn_q.weight"), xn[None])[0]
                 kk = O.matvec(self.w(p + "attn_k.weight"), xn[None])[0]
                 vv = O.matvec(self.w(p + "attn_v.weight"), xn[None])[0]
-                q, gate, krow, vrow = O.attn_preprocess(q_full, kk, vv, self.w(p + "attn_q_norm.weight"),
-                                                        self.w(p + "attn_k_norm.weight"), pos, self.freq, eps)
+                if self.kv_q8:
+                    q, gate, kb, vb = O.attn_preprocess_q8_0(q_full, kk, vv, self.w(p + "attn_q_norm.weight"),
+                                                             self.w(p + "attn_k_norm.weight"), pos, self.freq, eps)
+                    krow, vrow = O.q8_0_kv_dequant(*kb), O.q8_0_kv_dequant(*vb)
+                else:
+                    q, gate, krow, vrow = O.attn_preprocess(q_full, kk, vv, self.w(p + "attn_q_norm.weight"),
+                                                            self.w(p + "attn_k_norm.weight"), pos, self.freq, eps)
                 self.k[il].append(krow)
                 self.v[il].append(vrow)
                 assert len(self.k[il]) == pos + 1, "oracle positions must be contiguous"

@@ -86,9 +86,13 @@ _SIGS = {
     "qw35_cuda_deltanet_core": (C.c_int, [C.c_uint32, vp, vp, vp, vp, vp, vp, vp, vp, cp, up]),
     "qw35_cuda_attn_preprocess": (C.c_int, [C.c_uint32, vp, C.c_uint32, vp, vp, vp, vp, vp, C.c_uint32,
                                             C.c_uint64, C.c_uint64, vp, vp, C.c_float, vp, cp, up]),
+    "qw35_cuda_attn_preprocess_q8_0": (C.c_int, [C.c_uint32, vp, C.c_uint32, vp, vp, vp, vp, vp, C.c_uint32,
+                                                 C.c_uint64, C.c_uint64, vp, vp, C.c_float, vp, cp, up]),
     "qw35_cuda_gqa_workspace_bytes": (C.c_uint64, [C.c_uint32, C.c_uint32]),
     "qw35_cuda_gqa_decode": (C.c_int, [C.c_uint32, vp, vp, vp, C.c_uint32, vp, C.c_uint32, C.c_uint64,
                                        C.c_uint64, C.c_int32, C.c_int32, vp, vp, C.c_uint64, vp, cp, up]),
+    "qw35_cuda_gqa_decode_q8_0": (C.c_int, [C.c_uint32, vp, vp, vp, C.c_uint32, vp, C.c_uint32, C.c_uint64,
+                                            C.c_uint64, C.c_int32, C.c_int32, vp, vp, C.c_uint64, vp, cp, up]),
     "qw35_cuda_gqa_noalloc_max_bytes": (C.c_uint64, []),
     "qw35_cuda_gqa_decode_noalloc": (C.c_int, [C.c_uint32, vp, vp, vp, C.c_uint32, vp, C.c_uint32, C.c_uint64,
                                                C.c_uint64, C.c_int32, C.c_int32, vp, vp, cp, up]),

@@ -2,6 +2,7 @@
 //
 // Reference:
 //   qw35_attn_decode_preprocess_f32        qw35_attention.metal:29-112
+//   q8_0 KV twins (quantize / decode)      qw35_attention.metal:425-793
 //   qw35_attention_gqa_flash_decode_f32    qw35_attention.metal:211-292
 //   ..._split_f32 (8-way split-K + merge)  qw35_attention.metal:302-414
 //   dispatch / split threshold             Qw35MetalRuntime+Attention.m:80-111
@@ -35,8 +36,42 @@ constexpr int ASPLIT = 256;  // positions per split (4 warps x 64): ~2 waves of 
 constexpr int QFULL = AH * AHD * 2;  // q | gate per head
 constexpr int ASTG = 3;     // cp.async stages per warp in the split kernel (8 positions each)
 constexpr size_t ASMEM = (size_t)4 * ASTG * 2 * 8 * 32 * 16;  // 48 KiB of K/V staging per CTA
+// q8_0 planes: per warp a ring of raw q8_0 rows plus one dequantised f16 stage
+constexpr size_t ARAWQ8 = (size_t)ASTG * 2 * 8 * kKvQ8Row;             // 13,056 B
+constexpr size_t ASMEM_Q8 = (size_t)4 * (ARAWQ8 + 2 * 8 * 32 * 16);    // 84,992 B
 
-// ---- preprocess: RMS norm + NeoX RoPE + f16 KV write -------------------------
+// One q8_0 block of 32 values held 8 per lane by 4 consecutive lanes (lane % 4
+// = the lane's quarter): qw35_q8_0_quantize_block (qw35_attention.metal:429-440).
+// d = amax / 127 in fp32, codes round(x * (1 / d)) (half away from zero)
+// clamped to +-127 with the fp32 d, the block stores half(d).  `blk` points at
+// the block's 34 bytes {f16 d; int8 qs[32]}; every lane of the warp calls this.
+__device__ __forceinline__ void q8_block_store(const float *x, uint8_t *blk, int lane) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(x[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float d = amax / 127.0f;
+    const float id = d != 0.0f ? 1.0f / d : 0.0f;
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float y = __fmul_rn(x[i], id);  // a plain product, as the reference (no contraction)
+        int q = (int)roundf(y);
+        q = q < -127 ? -127 : (q > 127 ? 127 : q);
+        packed[i >> 2] |= ((uint32_t)q & 0xffu) << (8 * (i & 3));
+    }
+    // the block starts 2 bytes before the codes; codes of quarter j at 2 + 8 j:
+    // even addresses, so 16-bit stores
+    unsigned short *qd = reinterpret_cast<unsigned short *>(blk + 2 + 8 * (lane & 3));
+    qd[0] = (unsigned short)(packed[0] & 0xffffu);
+    qd[1] = (unsigned short)(packed[0] >> 16);
+    qd[2] = (unsigned short)(packed[1] & 0xffffu);
+    qd[3] = (unsigned short)(packed[1] >> 16);
+    if ((lane & 3) == 0) *reinterpret_cast<unsigned short *>(blk) = __half_as_ushort(__float2half_rn(d));
+}
+
+// ---- preprocess: RMS norm + NeoX RoPE + f16 (or q8_0) KV write ----------------
 __global__ void __launch_bounds__(256) attn_pre_kernel(AttnPreArgs p) {
     const int seq = blockIdx.x;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -76,6 +111,17 @@ __global__ void __launch_bounds__(256) attn_pre_kernel(AttnPreArgs p) {
             float *go = p.gate_out + ((size_t)seq * AH + h) * AHD + d0;
 #pragma unroll
             for (int i = 0; i < 8; ++i) { qo[i] = o[i]; go[i] = x[AHD + d0 + i]; }
+        } else if (p.kv_q8) {
+            // q8_0 rows: lanes 4b..4b+3 hold block b (dims 32b..32b+31) of the head row
+            const size_t trow = p.slots ? (size_t)p.slots[seq] : (size_t)seq;
+            const uint64_t base = p.chunk_ptrs[trow * p.max_chunks + pos / ACHUNK];
+            const size_t row = ((size_t)h * ACHUNK + (pos % ACHUNK)) * kKvQ8Row + 34 * (lane >> 2);
+            const float *vs = src + QFULL + AKV * AHD + h * AHD + d0;
+            float vv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) vv[i] = vs[i];
+            q8_block_store(o, reinterpret_cast<uint8_t *>(base + p.k_off + row), lane);
+            q8_block_store(vv, reinterpret_cast<uint8_t *>(base + p.v_off + row), lane);
         } else {
             const size_t trow = p.slots ? (size_t)p.slots[seq] : (size_t)seq;
             const uint64_t base = p.chunk_ptrs[trow * p.max_chunks + pos / ACHUNK];
@@ -165,6 +211,13 @@ __device__ __forceinline__ void split_h2(float a, float b, uint32_t &hi, uint32_
 // cache's f16.  Lane (g = lane/4, t = lane%4) holds the scores of position
 // g for heads 2t, 2t+1 and O^T rows (dims) 16 j + g, + 8 for the same heads;
 // lanes with t >= 2 carry the padding.
+// Q8: the planes hold q8_0 rows (272 B per head-row); each warp stages the raw
+// rows with cp.async and, per step, turns them into the same swizzled f16
+// tile (half(d * q): the exact product rounded once), so the MMA core is
+// unchanged.  The reference computes these products in fp32
+// (qw35_attention.metal:665-682); the half rounding stays far inside the
+// 1e-3 bar.
+template <bool Q8>
 __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_max) {
     const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -208,8 +261,28 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_
     // row's 16-byte piece c stored at c ^ (row % 8) so ldmatrix reads hit eight
     // distinct bank groups (cp.async, zero-filled past i1).
     extern __shared__ __align__(16) uint4 ring[];  // [4 warps][ASTG][2][8 rows][32 pieces]
-    uint4 *wring = ring + (size_t)wid * ASTG * 2 * 8 * 32;
+    // (Q8: [4 warps] x {raw [ASTG][2][8 rows][272 B], f16 tile [2][8 rows][32 pieces]})
+    uint4 *wring = Q8 ? ring + (size_t)wid * ((ARAWQ8 + 2 * 8 * 32 * 16) / 16) : ring + (size_t)wid * ASTG * 2 * 8 * 32;
+    uint8_t *wraw = reinterpret_cast<uint8_t *>(wring);
+    uint4 *wtile = wring + ARAWQ8 / 16;
     auto issue = [&](int ib, int stage) {
+        if constexpr (Q8) {
+            // 2 x 8 rows of 17 16-byte pieces; pieces past i1 are zero-filled
+            uint8_t *dst = wraw + (size_t)stage * 2 * 8 * kKvQ8Row;
+            for (int q = lane; q < 2 * 8 * 17; q += 32) {
+                const int kv = q >= 8 * 17 ? 1 : 0;
+                const int rem = q - kv * 8 * 17;
+                const int r = rem / 17, pc = rem - r * 17;
+                const int idx = ib + r;
+                const bool ok = idx < i1;
+                const int pos = ok ? (idx < sk ? idx : rstart + (idx - sk)) : 0;
+                const uint64_t base = ctab[ok ? pos / ACHUNK : 0];
+                const size_t off = ((size_t)kvh * ACHUNK + (size_t)(pos % ACHUNK)) * kKvQ8Row + (size_t)pc * 16;
+                cp_async16(dst + (kv * 8 + r) * kKvQ8Row + pc * 16,
+                           reinterpret_cast<const void *>(base + (kv ? p.v_off : p.k_off) + off), ok);
+            }
+            return;
+        }
         uint4 *dst = wring + (size_t)stage * 2 * 8 * 32;
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
@@ -241,6 +314,31 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_
         cp_async_wait<ASTG - 1>();  // this block's group has landed
         __syncwarp();
         const uint4 *ks = wring + (size_t)stage * 2 * 8 * 32;
+        if constexpr (Q8) {
+            // raw rows -> f16 tile: lane = 16-byte piece (dims 8 lane .. +7) = quarter
+            // lane % 4 of block lane / 4; q + 1152 - 1152 in half is exact, times
+            // the block's half d in one HMUL2 (the exact product rounded once)
+            const uint8_t *rs = wraw + (size_t)stage * 2 * 8 * kKvQ8Row + 34 * (lane >> 2);
+            const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6480));  // 1152
+#pragma unroll
+            for (int kr = 0; kr < 16; ++kr) {  // K rows 0-7, then V rows 0-7
+                const uint8_t *blk = rs + kr * kKvQ8Row;
+                const __half2 d2 = __half2half2(__ushort_as_half(*reinterpret_cast<const unsigned short *>(blk)));
+                const unsigned short *qd = reinterpret_cast<const unsigned short *>(blk + 2 + 8 * (lane & 3));
+                uint32_t hw[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint32_t two = (uint32_t)qd[u] ^ 0x8080u;  // biased codes q + 128
+                    const uint32_t v = __byte_perm(two, 0x64646464u, 0x4140u);  // halves 1024 + (q + 128)
+                    const __half2 h = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&v), off), d2);
+                    hw[u] = *reinterpret_cast<const uint32_t *>(&h);
+                }
+                const int r = kr & 7;
+                wtile[(kr >> 3) * 8 * 32 + r * 32 + (lane ^ r)] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            }
+            __syncwarp();
+            ks = wtile;
+        }
         const uint4 *vs = ks + 8 * 32;
 
         // S^T (16 x 8) = K (16 x 256) Q^T (256 x 8): A rows = positions (rows 8-15 repeat 0-7)
@@ -390,13 +488,24 @@ cudaError_t attn_decode_run(const AttnArgs &a, cudaStream_t st) {
     const int ns = (a.max_len + ASPLIT - 1) / ASPLIT;
     dim3 g1(ns, AKV, a.n_seq);
     cudaError_t e0;
-    static bool attr = false;
-    if (!attr) {
-        e0 = cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ASMEM);
-        if (e0 != cudaSuccess) return e0;
-        attr = true;
+    static bool attr = false, attr_q8 = false;
+    if (a.kv_q8) {
+        if (!attr_q8) {
+            e0 = cudaFuncSetAttribute(attn_split_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)ASMEM_Q8);
+            if (e0 != cudaSuccess) return e0;
+            attr_q8 = true;
+        }
+        attn_split_kernel<true><<<g1, 128, ASMEM_Q8, st>>>(a, ns);
+    } else {
+        if (!attr) {
+            e0 = cudaFuncSetAttribute(attn_split_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)ASMEM);
+            if (e0 != cudaSuccess) return e0;
+            attr = true;
+        }
+        attn_split_kernel<false><<<g1, 128, ASMEM, st>>>(a, ns);
     }
-    attn_split_kernel<<<g1, 128, ASMEM, st>>>(a, ns);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     dim3 g2(AH, a.n_seq);

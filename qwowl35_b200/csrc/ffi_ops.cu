@@ -187,7 +187,7 @@ int qw35_cuda_deltanet_core(uint32_t n_seq, const uint16_t *q, const uint16_t *k
     return cuda_ok(qw35::deltanet_core_run(a, (cudaStream_t)stream), "deltanet_core", err, err_len);
 }
 
-int qw35_cuda_attn_preprocess(uint32_t n_seq, const float *qkv, uint32_t qkv_stride, const float *q_norm_w,
+static int attn_pre_impl(int kv_q8, uint32_t n_seq, const float *qkv, uint32_t qkv_stride, const float *q_norm_w,
                               const float *k_norm_w, const float *rope_freq, const int32_t *pos,
                               const uint64_t *chunk_ptrs, uint32_t max_chunks, uint64_t k_off, uint64_t v_off,
                               float *q_out, float *gate_out, float eps, void *stream, char *err,
@@ -202,15 +202,33 @@ int qw35_cuda_attn_preprocess(uint32_t n_seq, const float *qkv, uint32_t qkv_str
     a.n_seq = (int)n_seq; a.qkv = qkv; a.qkv_stride = (int)qkv_stride; a.q_norm_w = q_norm_w;
     a.k_norm_w = k_norm_w; a.rope_freq = rope_freq; a.pos = pos; a.chunk_ptrs = chunk_ptrs;
     a.max_chunks = (int)max_chunks; a.k_off = (long long)k_off; a.v_off = (long long)v_off;
-    a.q_out = q_out; a.gate_out = gate_out; a.eps = eps;
+    a.q_out = q_out; a.gate_out = gate_out; a.eps = eps; a.kv_q8 = kv_q8;
     return cuda_ok(qw35::attn_preprocess_run(a, (cudaStream_t)stream), "attn_preprocess", err, err_len);
+}
+
+int qw35_cuda_attn_preprocess(uint32_t n_seq, const float *qkv, uint32_t qkv_stride, const float *q_norm_w,
+                              const float *k_norm_w, const float *rope_freq, const int32_t *pos,
+                              const uint64_t *chunk_ptrs, uint32_t max_chunks, uint64_t k_off, uint64_t v_off,
+                              float *q_out, float *gate_out, float eps, void *stream, char *err,
+                              uintptr_t err_len) {
+    return attn_pre_impl(0, n_seq, qkv, qkv_stride, q_norm_w, k_norm_w, rope_freq, pos, chunk_ptrs, max_chunks, k_off,
+                         v_off, q_out, gate_out, eps, stream, err, err_len);
+}
+
+int qw35_cuda_attn_preprocess_q8_0(uint32_t n_seq, const float *qkv, uint32_t qkv_stride, const float *q_norm_w,
+                                   const float *k_norm_w, const float *rope_freq, const int32_t *pos,
+                                   const uint64_t *chunk_ptrs, uint32_t max_chunks, uint64_t k_off, uint64_t v_off,
+                                   float *q_out, float *gate_out, float eps, void *stream, char *err,
+                                   uintptr_t err_len) {
+    return attn_pre_impl(1, n_seq, qkv, qkv_stride, q_norm_w, k_norm_w, rope_freq, pos, chunk_ptrs, max_chunks, k_off,
+                         v_off, q_out, gate_out, eps, stream, err, err_len);
 }
 
 uint64_t qw35_cuda_gqa_workspace_bytes(uint32_t n_seq, uint32_t max_len) {
     return qw35::attn_workspace_bytes((int)n_seq, (int)max_len);
 }
 
-int qw35_cuda_gqa_decode(uint32_t n_seq, const float *q, const float *gate, const int32_t *seq_len,
+static int gqa_decode_impl(int kv_q8, uint32_t n_seq, const float *q, const float *gate, const int32_t *seq_len,
                          uint32_t max_len, const uint64_t *chunk_ptrs, uint32_t max_chunks, uint64_t k_off,
                          uint64_t v_off, int32_t window, int32_t sink, float *out, void *workspace,
                          uint64_t workspace_bytes, void *stream, char *err, uintptr_t err_len) {
@@ -228,8 +246,24 @@ int qw35_cuda_gqa_decode(uint32_t n_seq, const float *q, const float *gate, cons
     a.n_seq = (int)n_seq; a.q = q; a.gate = gate; a.seq_len = seq_len; a.chunk_ptrs = chunk_ptrs;
     a.max_chunks = (int)max_chunks; a.k_off = (long long)k_off; a.v_off = (long long)v_off;
     a.window = window; a.sink = sink < 0 ? 0 : sink; a.max_len = (int)max_len; a.out = out;
-    a.ws = workspace; a.ws_bytes = workspace_bytes;
+    a.ws = workspace; a.ws_bytes = workspace_bytes; a.kv_q8 = kv_q8;
     return cuda_ok(qw35::attn_decode_run(a, (cudaStream_t)stream), "gqa_decode", err, err_len);
+}
+
+int qw35_cuda_gqa_decode(uint32_t n_seq, const float *q, const float *gate, const int32_t *seq_len,
+                         uint32_t max_len, const uint64_t *chunk_ptrs, uint32_t max_chunks, uint64_t k_off,
+                         uint64_t v_off, int32_t window, int32_t sink, float *out, void *workspace,
+                         uint64_t workspace_bytes, void *stream, char *err, uintptr_t err_len) {
+    return gqa_decode_impl(0, n_seq, q, gate, seq_len, max_len, chunk_ptrs, max_chunks, k_off, v_off, window, sink, out,
+                           workspace, workspace_bytes, stream, err, err_len);
+}
+
+int qw35_cuda_gqa_decode_q8_0(uint32_t n_seq, const float *q, const float *gate, const int32_t *seq_len,
+                              uint32_t max_len, const uint64_t *chunk_ptrs, uint32_t max_chunks, uint64_t k_off,
+                              uint64_t v_off, int32_t window, int32_t sink, float *out, void *workspace,
+                              uint64_t workspace_bytes, void *stream, char *err, uintptr_t err_len) {
+    return gqa_decode_impl(1, n_seq, q, gate, seq_len, max_len, chunk_ptrs, max_chunks, k_off, v_off, window, sink, out,
+                           workspace, workspace_bytes, stream, err, err_len);
 }
 
 uint64_t qw35_cuda_gqa_noalloc_max_bytes(void) { return qw35::attn_noalloc_limit(); }

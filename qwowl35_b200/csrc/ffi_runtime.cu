@@ -65,8 +65,10 @@ void *create(const void *map, uint64_t size, const qw35_metal_tensor_desc *tenso
         set_err(err, len, "invalid runtime creation inputs");
         return nullptr;
     }
-    if (kv_type != 0) {
-        set_err(err, len, "kv_cache_type q8_0 is not implemented by the CUDA runtime (use 0 = f16)");
+    // q8_0 KV (kv_type 1): built, enabled by QW35_KV_Q8=1 until it has run on a GPU
+    if (kv_type > 1 || (kv_type == 1 && getenv("QW35_KV_Q8") == nullptr)) {
+        set_err(err, len, kv_type > 1 ? "invalid kv_cache_type (0 = f16, 1 = q8_0)"
+                                      : "kv_cache_type q8_0 is not enabled in this build (set QW35_KV_Q8=1; 0 = f16)");
         return nullptr;
     }
     int ndev = 0;
@@ -77,7 +79,7 @@ void *create(const void *map, uint64_t size, const qw35_metal_tensor_desc *tenso
     }
     try {
         auto ms = qw35::shared_model(map, size, tensors, count, *hp, vocab);
-        Runtime *rt = qw35::create_runtime(ms, ctx, vocab, prefill_chunk, max_seqs);
+        Runtime *rt = qw35::create_runtime(ms, ctx, vocab, prefill_chunk, max_seqs, kv_type);
         std::lock_guard<std::mutex> g(g_mu);
         g_live.insert(rt);
         return rt;

@@ -91,8 +91,13 @@ struct AttnPreArgs {
     float *q_out = nullptr;        // [n][16][256]
     float *gate_out = nullptr;     // [n][16][256]
     float eps = 1e-6f;
+    int kv_q8 = 0;                 // 1: the planes hold q8_0 rows (kKvQ8Row bytes per head-row)
 };
 cudaError_t attn_preprocess_run(const AttnPreArgs &a, cudaStream_t st);
+
+// q8_0 KV rows: 8 blocks {f16 d; int8 qs[32]} per 256-dim head row
+// (qw35_attention.metal:425-445); a plane is [4 kv heads][256 pos][272 B].
+constexpr int kKvQ8Row = 8 * 34;
 
 struct AttnArgs {
     int n_seq = 0;
@@ -110,6 +115,7 @@ struct AttnArgs {
     int out_stride = 4096;
     void *ws = nullptr;
     size_t ws_bytes = 0;
+    int kv_q8 = 0;                 // 1: q8_0 planes (see kKvQ8Row)
 };
 size_t attn_workspace_bytes(int n_seq, int max_len);
 cudaError_t attn_decode_run(const AttnArgs &a, cudaStream_t st);

@@ -94,6 +94,7 @@ struct Runtime {
 
     // KV chunk pool
     size_t chunk_bytes = 0, plane_bytes = 0;
+    int kv_q8 = 0;                               // kv_cache_type 1: q8_0 planes
     uint32_t max_chunks = 0;                     // per sequence (ctx ceiling / 256)
     uint32_t table_chunks = 0;                   // columns of the device chunk table
     std::vector<void *> arenas;
@@ -160,7 +161,7 @@ std::shared_ptr<ModelStore> load_model(const void *map, uint64_t map_size, const
 std::shared_ptr<ModelStore> shared_model(const void *map, uint64_t map_size, const qw35_metal_tensor_desc *descs,
                                          uintptr_t n, const qw35_metal_hparams &hp, uint32_t vocab);
 Runtime *create_runtime(std::shared_ptr<ModelStore> ms, uint32_t ctx, uint32_t vocab, uint32_t prefill_chunk,
-                        uint32_t max_seqs);
+                        uint32_t max_seqs, uint32_t kv_type = 0);
 void rt_enqueue_step(Runtime *rt, uint32_t n, const uint32_t *seq_ids, const uint32_t *tokens,
                      const uint32_t *pos, int mode);
 void rt_wait(Runtime *rt);

@@ -112,6 +112,7 @@ static void encode_step(Runtime *rt, int n, int mode, int maxlen) {
             pa.q_out = rt->qbuf;
             pa.gate_out = rt->gbuf;
             pa.eps = eps;
+            pa.kv_q8 = rt->kv_q8;
             ck(attn_preprocess_run(pa, st), "attn preprocess");
             AttnArgs aa;
             aa.n_seq = n;
@@ -130,6 +131,7 @@ static void encode_step(Runtime *rt, int n, int mode, int maxlen) {
             aa.out_stride = 4096;
             aa.ws = rt->attn_ws;
             aa.ws_bytes = rt->attn_ws_bytes;
+            aa.kv_q8 = rt->kv_q8;
             ck(attn_decode_run(aa, st), "attention");
         }
         mv(rt, lw.out, rt->core, nullptr, rt->act, n, 1);

@@ -71,7 +71,7 @@ static T *dmalloc(size_t count) {
 }
 
 Runtime *create_runtime(std::shared_ptr<ModelStore> ms, uint32_t ctx, uint32_t vocab, uint32_t prefill_chunk,
-                        uint32_t max_seqs) {
+                        uint32_t max_seqs, uint32_t kv_type) {
     if (ctx == 0) fail("ctx must be positive");
     if (ctx > kMaxCtx) fail("--ctx %u exceeds the maximum %u tokens the KV cache can address", ctx, kMaxCtx);
     if (max_seqs == 0 || max_seqs > 1024) fail("max_seqs must be in [1, 1024]");
@@ -100,7 +100,10 @@ Runtime *create_runtime(std::shared_ptr<ModelStore> ms, uint32_t ctx, uint32_t v
     rt->slot_used.assign(S, false);
     rt->slot_used[0] = true;  // slot 0 backs the single-sequence qw35_metal_* surface
 
-    rt->plane_bytes = 4ull * kChunk * 256 * 2;
+    // one attention layer's K (or V) plane of a chunk: [4 kv heads][256 pos][256 dims]
+    // f16, or q8_0 rows of kKvQ8Row bytes (reference bridge.rs:31-42, kv_cache_type)
+    rt->kv_q8 = kv_type == 1 ? 1 : 0;
+    rt->plane_bytes = rt->kv_q8 ? 4ull * kChunk * kKvQ8Row : 4ull * kChunk * 256 * 2;
     rt->chunk_bytes = (size_t)ms->n_attn * 2 * rt->plane_bytes;
     rt->table_chunks = kMaxCtx / kChunk;
     rt->seq_chunks.assign(S, {});

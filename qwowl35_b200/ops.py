@@ -117,11 +117,12 @@ def deltanet_core(q, k, v, beta, g, state):
     return y
 
 
-def attn_preprocess(qkv, q_norm_w, k_norm_w, rope_freq, pos, chunk_ptrs, k_off, v_off, eps=1e-6):
+def attn_preprocess(qkv, q_norm_w, k_norm_w, rope_freq, pos, chunk_ptrs, k_off, v_off, eps=1e-6, kv_q8=False):
+    """kv_q8: the planes hold q8_0 rows (272 bytes per head-row) instead of f16."""
     n = qkv.shape[0]
     q = torch.empty((n, 16, 256), dtype=torch.float32, device=qkv.device)
     gate = torch.empty_like(q)
-    call("qw35_cuda_attn_preprocess", n, _p(_dev(qkv)), qkv.shape[1], _p(_dev(q_norm_w)), _p(_dev(k_norm_w)),
+    call("qw35_cuda_attn_preprocess_q8_0" if kv_q8 else "qw35_cuda_attn_preprocess", n, _p(_dev(qkv)), qkv.shape[1], _p(_dev(q_norm_w)), _p(_dev(k_norm_w)),
          _p(_dev(rope_freq)), _p(_dev(pos)), _p(_dev(chunk_ptrs)), chunk_ptrs.shape[1], k_off, v_off, _p(q), _p(gate),
          float(eps), _stream())
     return q, gate
@@ -131,12 +132,13 @@ def gqa_workspace(n: int, max_len: int, device="cuda"):
     return torch.empty(int(lib().qw35_cuda_gqa_workspace_bytes(n, max_len)), dtype=torch.uint8, device=device)
 
 
-def gqa_decode(q, gate, seq_len, max_len, chunk_ptrs, k_off, v_off, window=0, sink=0, ws=None, out=None):
+def gqa_decode(q, gate, seq_len, max_len, chunk_ptrs, k_off, v_off, window=0, sink=0, ws=None, out=None,
+               kv_q8=False):
     n = q.shape[0]
     if out is None:
         out = torch.empty((n, 4096), dtype=torch.float32, device=q.device)
     if ws is None:
         ws = gqa_workspace(n, max_len, q.device)
-    call("qw35_cuda_gqa_decode", n, _p(_dev(q)), _p(gate), _p(_dev(seq_len)), max_len, _p(_dev(chunk_ptrs)),
+    call("qw35_cuda_gqa_decode_q8_0" if kv_q8 else "qw35_cuda_gqa_decode", n, _p(_dev(q)), _p(gate), _p(_dev(seq_len)), max_len, _p(_dev(chunk_ptrs)),
          chunk_ptrs.shape[1], k_off, v_off, window, sink, _p(out), _p(ws), ws.numel(), _stream())
     return out

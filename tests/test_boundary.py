@@ -131,3 +131,16 @@ def test_warm_model_views_touches_pages():
 @pytest.mark.skipif(lib().qw35_metal_has_device() != 0, reason="a GPU is present")
 def test_no_device_reported_without_gpu():
     assert lib().qw35_cuda_device_count() == 0
+
+
+def test_kv_cache_type_gate_needs_no_gpu(monkeypatch):
+    """kv_cache_type 1 (q8_0) is refused unless QW35_KV_Q8 is set; other values always."""
+    from qwowl35_b200 import synth
+    from qwowl35_b200._lib import Qw35Error
+    from qwowl35_b200.runtime import Runtime
+    m = synth.build(synth.ModelConfig(layers=4, ffn=512, vocab=512), seed=0)
+    monkeypatch.delenv("QW35_KV_Q8", raising=False)
+    with pytest.raises(Qw35Error, match="not enabled"):
+        Runtime(m, ctx=64, kv_cache_type=1)
+    with pytest.raises(Qw35Error, match="invalid kv_cache_type"):
+        Runtime(m, ctx=64, kv_cache_type=2)

@@ -109,3 +109,101 @@ def test_kv_chunk_address_math():
     assert O.kv_address(table, 255) == (7, 255)
     assert O.kv_address(table, 256) == (3, 0)
     assert O.kv_address(table, 700) == (9, 188)
+
+
+# ---- q8_0 KV cache (kv_cache_type 1, qw35_attention.metal:425-793) -----------------
+# The q8_0 kernels are enabled by QW35_KV_Q8=1 until they have run on a B200.
+KVQ8 = pytest.mark.skipif(not __import__("os").environ.get("QW35_KV_Q8"),
+                          reason="q8_0 KV kernels not yet enabled (QW35_KV_Q8=1)")
+ROWQ8 = 8 * 34
+PLANEQ8 = 4 * 256 * ROWQ8  # bytes of one K (or V) q8_0 plane in a chunk
+
+
+def make_pool_q8(rng, lens, layers=1):
+    """Chunks of `layers` x (K plane, V plane) of valid q8_0 rows, shuffled in the pool."""
+    nchunks = [(L + 255) // 256 for L in lens]
+    total = sum(nchunks)
+    per_chunk = layers * 2 * PLANEQ8
+    host = rng.integers(-127, 128, size=(total * per_chunk // 34, 34)).astype(np.int8).view(np.uint8)
+    host[:, 0:2] = (np.abs(rng.normal(0, 0.02, size=(host.shape[0], 1)))).astype(np.float16).view(np.uint8)
+    pool = torch.from_numpy(host.reshape(-1).copy()).cuda()
+    perm = rng.permutation(total)
+    table = np.zeros((len(lens), max(nchunks)), dtype=np.uint64)
+    base, i = pool.data_ptr(), 0
+    for s, c in enumerate(nchunks):
+        for j in range(c):
+            table[s, j] = base + int(perm[i]) * per_chunk
+            i += 1
+    return pool, table, per_chunk
+
+
+def gather_kv_q8(host, block_ids, L, layer, per_chunk):
+    """(d [L,4,8] f16, qs [L,4,256] int8) for K and V of one sequence."""
+    out = []
+    for plane in (0, 1):
+        d = np.empty((L, 4, 8), np.float16)
+        qs = np.empty((L, 4, 256), np.int8)
+        for t in range(L):
+            c = int(block_ids[t // 256])
+            off = c * per_chunk + (layer * 2 + plane) * PLANEQ8
+            rows = host[off:off + PLANEQ8].reshape(4, 256, 8, 34)[:, t % 256]
+            d[t] = rows[:, :, 0:2].copy().view(np.float16)[..., 0]
+            qs[t] = rows[:, :, 2:].copy().view(np.int8).reshape(4, 256)
+        out.append((d, qs))
+    return out
+
+
+@KVQ8
+@pytest.mark.parametrize("lens,window,sink", [([1], 0, 0), ([300], 0, 0), ([1025, 7, 3000], 0, 0),
+                                              ([4096, 2048], 512, 4)])
+def test_gqa_decode_q8_0_matches_oracle(lens, window, sink):
+    rng = np.random.default_rng(sum(lens) + 1)
+    layers, layer = 2, 1
+    pool, table, per_chunk = make_pool_q8(rng, lens, layers)
+    n = len(lens)
+    q = rng.normal(0, 1, (n, 16, 256)).astype(np.float32)
+    gate = rng.normal(0, 1, (n, 16, 256)).astype(np.float32)
+    from qwowl35_b200 import ops
+    k_off = layer * 2 * PLANEQ8
+    out = ops.gqa_decode(torch.from_numpy(q).cuda(), torch.from_numpy(gate).cuda(),
+                         torch.tensor(lens, dtype=torch.int32, device="cuda"), max(lens),
+                         torch.from_numpy(table.view(np.int64)).cuda(), k_off, k_off + PLANEQ8, window, sink,
+                         kv_q8=True).cpu().numpy()
+    host = pool.cpu().numpy()
+    blocks = (table.astype(np.int64) - pool.data_ptr()) // per_chunk
+    for s, L in enumerate(lens):
+        Kq, Vq = gather_kv_q8(host, blocks[s], L, layer, per_chunk)
+        ref = O.gqa_decode_q8_0(q[s], gate[s], Kq, Vq, window, sink)
+        assert relerr(out[s].reshape(16, 256), ref) < TOL
+
+
+@KVQ8
+def test_preprocess_q8_0_quantises_like_the_reference():
+    rng = np.random.default_rng(8)
+    lens = [600, 257]
+    pool, table, per_chunk = make_pool_q8(rng, lens, 1)
+    n = len(lens)
+    pos = np.array([599, 256], dtype=np.int32)
+    qkv = rng.normal(0, 1, (n, 10240)).astype(np.float32)
+    qkv[0, 9216:9216 + 32] = 0.0                                       # an all-zero V block
+    qn = np.abs(rng.normal(1, 0.1, 256)).astype(np.float32)
+    kn = np.abs(rng.normal(1, 0.1, 256)).astype(np.float32)
+    freq = O.rope_freqs(1.0e7)
+    from qwowl35_b200 import ops
+    q, gate = ops.attn_preprocess(torch.from_numpy(qkv).cuda(), torch.from_numpy(qn).cuda(),
+                                  torch.from_numpy(kn).cuda(), torch.from_numpy(freq).cuda(),
+                                  torch.from_numpy(pos).cuda(), torch.from_numpy(table.view(np.int64)).cuda(),
+                                  0, PLANEQ8, kv_q8=True)
+    torch.cuda.synchronize()
+    host = pool.cpu().numpy()
+    blocks = (table.astype(np.int64) - pool.data_ptr()) // per_chunk
+    for s in range(n):
+        rq, rg, (rkd, rkq), (rvd, rvq) = O.attn_preprocess_q8_0(qkv[s, :8192], qkv[s, 8192:9216], qkv[s, 9216:],
+                                                                qn, kn, int(pos[s]), freq)
+        assert relerr(q[s].cpu().numpy(), rq) < 1e-5
+        (kd, kq), (vd, vq) = gather_kv_q8(host, blocks[s], int(pos[s]) + 1, 0, per_chunk)
+        t = int(pos[s])
+        np.testing.assert_array_equal(vq[t], rvq)                       # V: the same fp32 input, exact
+        np.testing.assert_array_equal(vd[t].view(np.uint16), rvd.view(np.uint16))
+        assert np.abs(kq[t].astype(np.int32) - rkq.astype(np.int32)).max() <= 1   # K: fp32 vs f64 norm/RoPE
+        assert np.abs(kd[t].view(np.int16).astype(np.int32) - rkd.view(np.int16).astype(np.int32)).max() <= 1

@@ -154,8 +154,8 @@ def test_host_side_guards(small):
     with pytest.raises(Qw35Error):
         rt.seq_alloc()           # only one slot
     rt.close()
-    with pytest.raises(Qw35Error, match="not implemented"):
-        Runtime(small, ctx=64, kv_cache_type=1)
+    with pytest.raises(Qw35Error, match="invalid kv_cache_type"):
+        Runtime(small, ctx=64, kv_cache_type=2)
 
 
 def test_window_and_sink_match_oracle(small):
@@ -233,4 +233,17 @@ def test_mixed_type_model_batch_of_three_matches_oracle(mixed):
         out = rt.copy_logits_batch(3)
         for i, s in enumerate(seqs):
             assert relerr(out[i], orcs[i].step(s[pos], pos)) < TOL, (pos, i)
+    rt.close()
+
+
+@pytest.mark.skipif(not __import__("os").environ.get("QW35_KV_Q8"),
+                    reason="q8_0 KV kernels not yet enabled (QW35_KV_Q8=1)")
+def test_q8_0_kv_cache_matches_oracle(small):
+    from qwowl35_b200.runtime import KvCacheType
+    rt = Runtime(small, ctx=512, kv_cache_type=KvCacheType.Q8_0)
+    orc = OracleModel(small, kv_q8=True)
+    for pos, tok in enumerate(TOKENS):
+        rt.eval_token(tok, pos, LogitsMode.FULL)
+        e = relerr(rt.copy_logits(), orc.step(tok, pos))
+        assert e < TOL, (pos, e)
     rt.close()
