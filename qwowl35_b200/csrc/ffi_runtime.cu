@@ -1,6 +1,7 @@
 // ffi_runtime.cu -- extern "C" runtime surface: the reference's qw35_metal_*
 // functions (qw35-server/src/metal/bridge/Qw35FFI.m:201-431 is the code they
 // replace) and the batched qw35_cuda_runtime_* extensions.
+#include <algorithm>
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -219,9 +220,18 @@ int qw35_metal_runtime_eval_tokens(void *runtime, const uint32_t *tokens, uintpt
         if (!tokens || len == 0) qw35::fail("empty token run");
         if (len > rt->prefill_chunk) qw35::fail("token run longer than the prefill chunk");
         if ((uint64_t)pos0 + len > rt->ctx) qw35::fail("requested position exceeds allocated context");
-        // Chunked prefill kernels are outside this library's scope: a run is
-        // evaluated as consecutive decode steps, the head only on the last.
         const uint32_t seq = 0;
+        if (rt->batched_prefill && len > 1) {
+            // one pass per run of up to rt->rows tokens (QW35_PREFILL=1): weights are
+            // read once per run instead of once per token; the head only on the last
+            for (uintptr_t i = 0; i < len; i += rt->rows) {
+                const uint32_t m = (uint32_t)std::min<uintptr_t>(rt->rows, len - i);
+                qw35::rt_enqueue_prefill(rt, seq, tokens + i, m, pos0 + (uint32_t)i,
+                                         i + m == len ? logits_mode : QW35_LOGITS_NONE);
+            }
+            return;
+        }
+        // otherwise a run is evaluated as consecutive decode steps, the head only on the last
         for (uintptr_t i = 0; i < len; ++i) {
             const uint32_t pos = pos0 + (uint32_t)i;
             const int mode = i + 1 == len ? logits_mode : QW35_LOGITS_NONE;

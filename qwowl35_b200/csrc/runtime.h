@@ -70,10 +70,12 @@ struct ModelStore {
 
 struct StepKey {
     int n, mode, maxlen;
+    int prefill = 0;  // 1: the n rows are consecutive positions of one sequence
     bool operator<(const StepKey &o) const {
         if (n != o.n) return n < o.n;
         if (mode != o.mode) return mode < o.mode;
-        return maxlen < o.maxlen;
+        if (maxlen != o.maxlen) return maxlen < o.maxlen;
+        return prefill < o.prefill;
     }
 };
 
@@ -83,6 +85,8 @@ struct Runtime {
     qw35_metal_hparams hp{};
     uint32_t ctx = 0, vocab = 0, prefill_chunk = 1;
     uint32_t max_seqs = 1;
+    uint32_t rows = 1;             // rows of the step buffers: max_seqs, or a longer prefill run
+    bool batched_prefill = false;  // eval_tokens runs a token run as one batched pass (QW35_PREFILL=1)
     int attn_window = 0, attn_sink = 0;
     cudaStream_t stream = nullptr;
     std::string deferred_error;
@@ -164,6 +168,9 @@ Runtime *create_runtime(std::shared_ptr<ModelStore> ms, uint32_t ctx, uint32_t v
                         uint32_t max_seqs, uint32_t kv_type = 0);
 void rt_enqueue_step(Runtime *rt, uint32_t n, const uint32_t *seq_ids, const uint32_t *tokens,
                      const uint32_t *pos, int mode);
+// tokens[0..len) of one sequence at positions pos0.. as one pass (len <= rt->rows);
+// the head runs on the last token only
+void rt_enqueue_prefill(Runtime *rt, uint32_t seq, const uint32_t *tokens, uint32_t len, uint32_t pos0, int mode);
 void rt_wait(Runtime *rt);
 void rt_release_kv(Runtime *rt, uint32_t slot, size_t keep);
 void rt_ensure_kv(Runtime *rt, uint32_t slot, uint64_t positions);

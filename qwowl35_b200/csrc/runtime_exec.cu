@@ -66,12 +66,15 @@ static void ffn_gate_up(Runtime *rt, const LayerW &lw, int n) {
     ck(swiglu_run(rt->hbuf, rt->mixed_tmp, rt->hbuf, (size_t)n * lw.gate.rows, rt->stream), "swiglu");
 }
 
-static void encode_step(Runtime *rt, int n, int mode, int maxlen) {
+// prefill: the n rows are positions pos0 .. pos0 + n - 1 of ONE sequence.
+// Matvecs, attention preprocess and attention then run over all n rows at
+// once (row t attends to positions <= pos0 + t, whose K/V the preprocess has
+// just written); the DeltaNet recurrence runs row by row (n launches of one
+// sequence, in order), and the head only on the last row.
+static void encode_step(Runtime *rt, int n, int mode, int maxlen, bool prefill = false) {
     ModelStore &ms = *rt->model;
     cudaStream_t st = rt->stream;
     const float eps = rt->hp.rms_epsilon;
-    const int S = (int)rt->max_seqs;
-    (void)S;
     ck(embed_rows(ms.tok_embd.type_id, ms.tok_embd.ptr, ms.tok_embd.rows, rt->d_tok, n, 4096, rt->act, st), "embed");
     const size_t nd = (size_t)std::max(ms.n_delta, 1);
     for (const LayerW &lw : ms.layers) {
@@ -93,7 +96,18 @@ static void encode_step(Runtime *rt, int n, int mode, int maxlen) {
             d.out = rt->core;
             d.out_stride = 4096;
             d.eps = eps;
-            ck(deltanet_step_run(d, st), "deltanet");
+            if (!prefill) {
+                ck(deltanet_step_run(d, st), "deltanet");
+            } else {
+                for (int t = 0; t < n; ++t) {  // the recurrence is sequential over the run
+                    DeltaNetArgs dt = d;
+                    dt.n_seq = 1;
+                    dt.proj = rt->proj + (size_t)t * lw.proj_rows;
+                    dt.slots = rt->d_slot + t;
+                    dt.out = rt->core + (size_t)t * 4096;
+                    ck(deltanet_step_run(dt, st), "deltanet");
+                }
+            }
         } else {
             const long long k_off = (long long)lw.slot * 2 * (long long)rt->plane_bytes;
             AttnPreArgs pa;
@@ -138,20 +152,23 @@ static void encode_step(Runtime *rt, int n, int mode, int maxlen) {
         ffn_gate_up(rt, lw, n);
         mv(rt, lw.down, rt->hbuf, nullptr, rt->act, n, 1);
     }
+    // head: every row, or the last row of a prefill run
+    const float *hx = prefill ? rt->act + (size_t)(n - 1) * 4096 : rt->act;
+    const int hn = prefill ? 1 : n;
     if (mode == QW35_LOGITS_ARGMAX) {
         MatvecArgs a;
         a.type_id = ms.output.type_id;
         a.w0 = ms.output.ptr;
-        a.x = rt->act;
+        a.x = hx;
         a.norm_w = ms.output_norm;
         a.eps = eps;
         a.rows = ms.output.rows;
         a.k = ms.output.k;
-        a.batch = n;
+        a.batch = hn;
         ck(argmax_head_run(a, rt->d_argmax_tok, rt->d_argmax_val, rt->argmax_ws, rt->argmax_ws_bytes, st),
            "argmax head");
     } else if (mode == QW35_LOGITS_FULL) {
-        mv(rt, ms.output, rt->act, ms.output_norm, rt->logits, n, 0);
+        mv(rt, ms.output, hx, ms.output_norm, rt->logits, hn, 0);
     }
 }
 
@@ -161,46 +178,33 @@ static int len_bucket(uint32_t maxpos_plus1, uint32_t cap) {
     return (int)std::min(b, cap);
 }
 
-void rt_enqueue_step(Runtime *rt, uint32_t n, const uint32_t *seq_ids, const uint32_t *tokens, const uint32_t *pos,
-                     int mode) {
-    if (n == 0 || n > rt->max_seqs) fail("batch size %u outside [1, %u]", n, rt->max_seqs);
-    if (mode < 0 || mode > 2) fail("invalid logits mode %d", mode);
-    if (!tokens || !pos) fail("null token/position array");
-    uint32_t maxp = 0;
-    for (uint32_t i = 0; i < n; ++i) {
-        const uint32_t s = seq_ids ? seq_ids[i] : i;
-        if (s >= rt->max_seqs || !rt->slot_used[s]) fail("sequence %u is not allocated", s);
-        for (uint32_t j = 0; j < i; ++j)
-            if ((seq_ids ? seq_ids[j] : j) == s) fail("sequence %u appears twice in one batch", s);
-        if (pos[i] >= rt->ctx) fail("requested position exceeds allocated context");
-        if (tokens[i] >= rt->vocab) fail("token id is outside the Qw35 vocabulary");
-        maxp = std::max(maxp, pos[i] + 1);
-    }
-    for (uint32_t i = 0; i < n; ++i) rt_ensure_kv(rt, seq_ids ? seq_ids[i] : i, (uint64_t)pos[i] + 1);
-
-    // inputs -> pinned staging (reused once the previous step's copy finished) -> device
+// inputs -> pinned staging (reused once the previous step's copy finished) -> device
+template <typename SlotOf>
+static void stage_inputs(Runtime *rt, uint32_t n, SlotOf slot_of, const uint32_t *tokens, const uint32_t *pos) {
     ck(cudaEventSynchronize(rt->in_done), "input staging");
-    const uint32_t S = rt->max_seqs;
+    const uint32_t R = rt->rows;
     for (uint32_t i = 0; i < n; ++i) {
-        rt->h_pack[i] = (int32_t)(seq_ids ? seq_ids[i] : i);
-        rt->h_pack[S + i] = (int32_t)pos[i];
-        rt->h_pack[2 * S + i] = (int32_t)pos[i] + 1;
-        rt->h_pack[3 * S + i] = (int32_t)tokens[i];
+        rt->h_pack[i] = (int32_t)slot_of(i);
+        rt->h_pack[R + i] = (int32_t)pos[i];
+        rt->h_pack[2 * R + i] = (int32_t)pos[i] + 1;
+        rt->h_pack[3 * R + i] = (int32_t)tokens[i];
     }
-    ck(cudaMemcpyAsync(rt->d_in, rt->h_pack, 16ull * S, cudaMemcpyHostToDevice, rt->stream), "input copy");
+    ck(cudaMemcpyAsync(rt->d_in, rt->h_pack, 16ull * R, cudaMemcpyHostToDevice, rt->stream), "input copy");
     ck(cudaEventRecord(rt->in_done, rt->stream), "event");
+}
 
-    const int maxlen = len_bucket(maxp, rt->table_chunks * QW35_KV_CHUNK);
+// Encode (or replay the CUDA graph of) one step and queue the argmax readback.
+static void run_step(Runtime *rt, uint32_t n, int mode, int maxlen, bool prefill) {
     if (!rt->use_graphs) {
-        encode_step(rt, (int)n, mode, maxlen);
+        encode_step(rt, (int)n, mode, maxlen, prefill);
     } else {
-        StepKey key{(int)n, mode, maxlen};
+        StepKey key{(int)n, mode, maxlen, prefill ? 1 : 0};
         auto it = rt->graphs.find(key);
         if (it == rt->graphs.end()) {
             cudaGraph_t g = nullptr;
             ck(cudaStreamBeginCapture(rt->stream, cudaStreamCaptureModeThreadLocal), "begin capture");
             try {
-                encode_step(rt, (int)n, mode, maxlen);
+                encode_step(rt, (int)n, mode, maxlen, prefill);
             } catch (...) {
                 cudaStreamEndCapture(rt->stream, &g);
                 if (g) cudaGraphDestroy(g);
@@ -226,12 +230,49 @@ void rt_enqueue_step(Runtime *rt, uint32_t n, const uint32_t *seq_ids, const uin
         ck(cudaGraphLaunch(it->second, rt->stream), "graph launch");
         rt->last_kernels = rt->graph_kernels[key];
     }
+    const uint32_t nout = prefill ? 1 : n;  // rows the head ran on
     if (mode == QW35_LOGITS_ARGMAX) {
-        ck(cudaMemcpyAsync(rt->h_argmax_tok, rt->d_argmax_tok, 4ull * n, cudaMemcpyDeviceToHost, rt->stream), "d2h");
-        ck(cudaMemcpyAsync(rt->h_argmax_val, rt->d_argmax_val, 4ull * n, cudaMemcpyDeviceToHost, rt->stream), "d2h");
+        ck(cudaMemcpyAsync(rt->h_argmax_tok, rt->d_argmax_tok, 4ull * nout, cudaMemcpyDeviceToHost, rt->stream), "d2h");
+        ck(cudaMemcpyAsync(rt->h_argmax_val, rt->d_argmax_val, 4ull * nout, cudaMemcpyDeviceToHost, rt->stream), "d2h");
     }
-    rt->last_n = (int)n;
+    rt->last_n = (int)nout;
     rt->last_mode = mode;
+}
+
+void rt_enqueue_step(Runtime *rt, uint32_t n, const uint32_t *seq_ids, const uint32_t *tokens, const uint32_t *pos,
+                     int mode) {
+    if (n == 0 || n > rt->max_seqs) fail("batch size %u outside [1, %u]", n, rt->max_seqs);
+    if (mode < 0 || mode > 2) fail("invalid logits mode %d", mode);
+    if (!tokens || !pos) fail("null token/position array");
+    uint32_t maxp = 0;
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint32_t s = seq_ids ? seq_ids[i] : i;
+        if (s >= rt->max_seqs || !rt->slot_used[s]) fail("sequence %u is not allocated", s);
+        for (uint32_t j = 0; j < i; ++j)
+            if ((seq_ids ? seq_ids[j] : j) == s) fail("sequence %u appears twice in one batch", s);
+        if (pos[i] >= rt->ctx) fail("requested position exceeds allocated context");
+        if (tokens[i] >= rt->vocab) fail("token id is outside the Qw35 vocabulary");
+        maxp = std::max(maxp, pos[i] + 1);
+    }
+    for (uint32_t i = 0; i < n; ++i) rt_ensure_kv(rt, seq_ids ? seq_ids[i] : i, (uint64_t)pos[i] + 1);
+
+    stage_inputs(rt, n, [&](uint32_t i) { return seq_ids ? seq_ids[i] : i; }, tokens, pos);
+    run_step(rt, n, mode, len_bucket(maxp, rt->table_chunks * QW35_KV_CHUNK), false);
+}
+
+void rt_enqueue_prefill(Runtime *rt, uint32_t seq, const uint32_t *tokens, uint32_t len, uint32_t pos0, int mode) {
+    if (len == 0 || len > rt->rows) fail("prefill run of %u tokens outside [1, %u]", len, rt->rows);
+    if (mode < 0 || mode > 2) fail("invalid logits mode %d", mode);
+    if (!tokens) fail("null token array");
+    if (seq >= rt->max_seqs || !rt->slot_used[seq]) fail("sequence %u is not allocated", seq);
+    if ((uint64_t)pos0 + len > rt->ctx) fail("requested position exceeds allocated context");
+    for (uint32_t i = 0; i < len; ++i)
+        if (tokens[i] >= rt->vocab) fail("token id is outside the Qw35 vocabulary");
+    rt_ensure_kv(rt, seq, (uint64_t)pos0 + len);
+    std::vector<uint32_t> pos(len);
+    for (uint32_t i = 0; i < len; ++i) pos[i] = pos0 + i;
+    stage_inputs(rt, len, [&](uint32_t) { return seq; }, tokens, pos.data());
+    run_step(rt, len, mode, len_bucket(pos0 + len, rt->table_chunks * QW35_KV_CHUNK), true);
 }
 
 }  // namespace qw35

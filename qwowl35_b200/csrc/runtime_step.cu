@@ -111,32 +111,38 @@ Runtime *create_runtime(std::shared_ptr<ModelStore> ms, uint32_t ctx, uint32_t v
     rt->d_chunk_table = dmalloc<uint64_t>((size_t)S * rt->table_chunks);
     ck(cudaMemset(rt->d_chunk_table, 0, (size_t)S * rt->table_chunks * 8), "memset");
 
-    rt->d_in = dmalloc<int32_t>(4ull * S);
+    // step buffers hold max_seqs rows, or a batched prefill run (<= 64 tokens) when longer
+    rt->batched_prefill = getenv("QW35_PREFILL") != nullptr;
+    const uint32_t R = rt->batched_prefill ? std::max<uint32_t>(S, std::min<uint32_t>(rt->prefill_chunk, 64)) : S;
+    rt->rows = R;
+    rt->d_in = dmalloc<int32_t>(4ull * R);
     rt->d_slot = rt->d_in;
-    rt->d_pos = rt->d_in + S;
-    rt->d_len = rt->d_in + 2 * S;
-    rt->d_tok = reinterpret_cast<uint32_t *>(rt->d_in + 3 * S);
-    ck(cudaMallocHost(reinterpret_cast<void **>(&rt->h_pack), 16ull * S), "cudaMallocHost");
+    rt->d_pos = rt->d_in + R;
+    rt->d_len = rt->d_in + 2 * R;
+    rt->d_tok = reinterpret_cast<uint32_t *>(rt->d_in + 3 * R);
+    ck(cudaMallocHost(reinterpret_cast<void **>(&rt->h_pack), 16ull * R), "cudaMallocHost");
     ck(cudaMallocHost(reinterpret_cast<void **>(&rt->h_argmax_tok), 4ull * S), "cudaMallocHost");
     ck(cudaMallocHost(reinterpret_cast<void **>(&rt->h_argmax_val), 4ull * S), "cudaMallocHost");
 
     rt->proj_stride = std::max(kDeltaProj, kAttnProj);
-    rt->act = dmalloc<float>((size_t)S * H);
-    rt->proj = dmalloc<float>((size_t)S * rt->proj_stride);
-    rt->core = dmalloc<float>((size_t)S * H);
-    rt->hbuf = dmalloc<float>((size_t)S * F);
-    rt->qbuf = dmalloc<float>((size_t)S * H);
-    rt->gbuf = dmalloc<float>((size_t)S * H);
+    rt->act = dmalloc<float>((size_t)R * H);
+    rt->proj = dmalloc<float>((size_t)R * rt->proj_stride);
+    rt->core = dmalloc<float>((size_t)R * H);
+    rt->hbuf = dmalloc<float>((size_t)R * F);
+    rt->qbuf = dmalloc<float>((size_t)R * H);
+    rt->gbuf = dmalloc<float>((size_t)R * H);
     rt->logits = dmalloc<float>((size_t)S * vocab);
-    if (rt->model->mixed) rt->mixed_tmp = dmalloc<float>((size_t)S * std::max<uint32_t>(rt->proj_stride, F));
+    if (rt->model->mixed) rt->mixed_tmp = dmalloc<float>((size_t)R * std::max<uint32_t>(rt->proj_stride, F));
     rt->d_argmax_tok = dmalloc<uint32_t>(S);
     rt->d_argmax_val = dmalloc<float>(S);
     rt->argmax_ws_bytes = argmax_workspace_bytes(vocab, S);
     rt->argmax_ws = dmalloc<uint8_t>(rt->argmax_ws_bytes);
-    rt->attn_ws_bytes = attn_workspace_bytes((int)S, (int)kMaxCtx);
+    rt->attn_ws_bytes = attn_workspace_bytes((int)R, (int)kMaxCtx);
     rt->attn_ws = dmalloc<uint8_t>(rt->attn_ws_bytes);
 
     // scratch of the batched tensor-core matvec, reserved before any graph capture
+    // (a prefill run of R rows runs the head on its last row only)
+    if (R >= (uint32_t)kDqMinBatch) ck(dq_reserve((int)R, 12288, F), "reserve matvec scratch");
     if (S >= (uint32_t)kDqMinBatch) ck(dq_reserve((int)S, 12288, std::max<uint32_t>(vocab, F)), "reserve matvec scratch");
 
     // RoPE ladder freq[i] = base^(-2i/n_rot) in fp32 (Qw35MetalRuntime.m:772-795)

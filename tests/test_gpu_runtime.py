@@ -247,3 +247,26 @@ def test_q8_0_kv_cache_matches_oracle(small):
         e = relerr(rt.copy_logits(), orc.step(tok, pos))
         assert e < TOL, (pos, e)
     rt.close()
+
+
+@pytest.mark.skipif(not __import__("os").environ.get("QW35_PREFILL"),
+                    reason="batched prefill not yet enabled (QW35_PREFILL=1)")
+def test_batched_prefill_matches_oracle(small):
+    # 7 tokens in one pass: batch-7 matvecs (tensor-core path, the reference's
+    # tiled-path weight semantics), 7 attention rows over one sequence, the
+    # DeltaNet recurrence row by row; logits of the last token
+    rt = Runtime(small, ctx=512, prefill_chunk=8)
+    rt.eval_prefill_chunk(TOKENS, 0, LogitsMode.FULL)
+    got = rt.copy_logits()
+    orc = OracleModel(small, tiled=True)
+    for pos, tok in enumerate(TOKENS):
+        ref = orc.step(tok, pos)
+    assert relerr(got, ref) < TOL
+    # decoding continues from the prefilled state and KV
+    rt.eval_token(11, len(TOKENS), LogitsMode.FULL)
+    single = Runtime(small, ctx=512)
+    for pos, tok in enumerate(TOKENS + [11]):
+        single.eval_token(tok, pos, LogitsMode.FULL)
+    assert relerr(rt.copy_logits(), single.copy_logits().astype(np.float64)) < TOL
+    rt.close()
+    single.close()
