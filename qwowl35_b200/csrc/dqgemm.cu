@@ -3,9 +3,8 @@
 //
 // Y[b][r] (+)= sum_k W[r][k] * X[b][k] for a decode batch of B sequences.  The
 // CUDA-core matvec (matvec.cu) decodes the weights once per pair of batch
-// rows; from 3 rows on, decoding them ONCE per launch (here) into an f16 tile
-// into an f16 tile and multiplied against all B activation rows by
-// tcgen05.mma.  Reference semantics: the reference engine has no batched
+// rows; from 3 rows on, they are decoded ONCE per launch (here) into an f16
+// tile and multiplied against all B activation rows by tcgen05.mma.  Reference semantics: the reference engine has no batched
 // decode; its multi-token path (qw35_kernel_mul_mm, qw35_tiled_mm.metal:36-255)
 // dequantises weights to half (qw35_dequantize_gf4, qw35_gf4.metal:42-58) and
 // keeps activations in f32 (:197-200).  This kernel does the same: GF4
@@ -16,19 +15,20 @@
 // Q8_0 weights are not exact in f16 once multiplied by their block scale, so
 // each q * d (times a per-row power of two) is split into hi + lo halves and
 // both go through the tensor core (the epilogue removes the power of two).
-// Q4_K weights become half(d*sc*q - dmin*m), computed in fp32 and rounded
-// once: the reference's tiled path (qw35_dequantize_q4_k into half,
-// qw35_matvec.metal:20-38, instantiated for half tiles at
-// qw35_tiled_mm.metal:204-213).
+// K-quant weights become their fp32 values rounded once to half: Q4_K / Q5_K
+// half(d*sc*q - dmin*m), Q6_K half(d*sc*(q - 32)) -- the reference's tiled
+// path (qw35_dequantize_q4_k / _q5_k / _q6_k into half, qw35_matvec.metal:20-98,
+// instantiated for half tiles at qw35_tiled_mm.metal:204-255).
 //
 // CTA: warp 0 weight TMA producer, warp 1 MMA issuer (+ TMEM owner), warp 2
 // activation producer, then decode warps (thread = weight row, writing the
 // decoded f16 tile into TMEM with tcgen05.st), then epilogue warps.  Tiles are
 // 128 weight rows x NP batch columns (B padded to 16/32/64); K streams in
-// chunks of one 16 KB weight box (256 GF4 / 128 Q8_0 columns).  The sequence of
-// (matrix, tile, chunk) is split evenly over a persistent grid (stream-K:
-// partial tiles accumulate atomically).  Every wait is bounded (pipe.cuh).  No
-// cluster multicast is used.
+// chunks of one 16 KB weight box (256 GF4 / K-quant columns, 128 Q8_0 columns)
+// plus the codec's side boxes.  The sequence of (matrix, tile, chunk) is split
+// evenly over a persistent grid (stream-K: the CTAs sharing a tile add their
+// partial tiles into the output by TMA bulk reductions).  Every wait is
+// bounded (pipe.cuh).  No cluster multicast is used.
 #include <cuda.h>
 
 #include <cstdio>
@@ -50,11 +50,11 @@ namespace qw35 {
 constexpr int TM = 128;  // weight rows per tile (MMA M = TMEM lanes)
 
 // Per-codec geometry.  A weight chunk is 128 rows x 128 bytes of codes (one
-// 16 KB TMA box, 128B-swizzled): 256 K columns of GF4 or 128 of Q8_0; Q8_0
-// stages also carry the chunk's block scales (a second 2 KB box).  The
-// decoded f16 tile lives in TMEM (128 lanes x 128 32-bit columns: GF4 256
-// columns of K; Q8_0 hi and lo halves of 128) and feeds tcgen05.mma as
-// operand A.  Decode warps come in groups of four (one per TMEM lane
+// 16 KB TMA box, 128B-swizzled): 256 K columns of GF4 / K-quant nibbles or 128
+// of Q8_0; the other codecs' stages also carry side boxes (Q8_0 block scales,
+// K-quant headers / scales / high bits).  The decoded f16 tile lives in TMEM
+// (128 lanes x 128 32-bit columns: 256 columns of K; Q8_0 hi and lo halves
+// of 128) and feeds tcgen05.mma as operand A.  Decode warps come in groups of four (one per TMEM lane
 // quarter); the groups split a chunk's K range.
 template <int CODEC> struct DqGeo {
     static constexpr bool Q8 = CODEC == QW35_Q8_0_TYPE;

@@ -32,7 +32,7 @@ size_t argmax_workspace_bytes(uint32_t rows, uint32_t batch);
 cudaError_t argmax_head_run(const MatvecArgs &a, uint32_t *tok, float *val, void *ws, size_t ws_bytes,
                             cudaStream_t st);
 
-// tcgen05 batched path (dqgemm.cu): kDqMinBatch <= B <= 64, GF4 / Q8_0, k % 256 == 0,
+// tcgen05 batched path (dqgemm.cu): kDqMinBatch <= B <= 64, every codec, k % 256 == 0,
 // 16-byte aligned weights, activations and norm weight.
 constexpr int kDqMinBatch = 3;  // from 3 rows the CUDA-core path needs 2+ weight passes
 bool dq_supported(const MatvecArgs &a);

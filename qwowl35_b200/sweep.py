@@ -4,7 +4,7 @@
 
 For every codec x shape x batch: y[B][rows] = W x^T through the public ops API
 (``ops.matvec``; 1-2 rows run the CUDA-core kernels, 3-64 rows the tcgen05
-dequant-GEMM for GF4 / Q8_0 / Q4_K), x fp16 N(0, 1), weights drawn with the
+dequant-GEMM), x fp16 N(0, 1), weights drawn with the
 synthetic model's code and scale distributions (qwowl35_b200.synth).  Each
 point replays a CUDA graph of launches over rotating weight copies whose total
 exceeds twice the 126 MB L2, so every launch streams its weights from HBM;

@@ -166,7 +166,7 @@ def test_no_device_wait_timed_out():
     assert lib().qw35_cuda_device_error() == 0
 
 
-# ---- batched (B >= 16) tensor-core path -----------------------------------------
+# ---- batched (B >= 3) tensor-core path ------------------------------------------
 @pytest.mark.parametrize("t", CODECS)
 @pytest.mark.parametrize("b", [3, 8, 16, 32, 64, 20])
 @pytest.mark.parametrize("shape", [(12288, 4096), (4096, 12288), (333, 1280)])
