@@ -481,6 +481,20 @@ def main():
                             "traffic": NCU_TRAFFIC.get(dom[0]),
                             "bytes_per_launch": dom[1], "us_per_launch": dom[2] * 1e6}
         line["kernels"] = table
+        # GEMV half of the metric: batch-1 matvec HBM throughput of the FFN
+        # up-projection shape per codec (qwowl35_b200.sweep, x fp16)
+        try:
+            from qwowl35_b200 import ops as _ops, sweep
+            g = synth._Gen(11, device)
+            pts = []
+            for name, t in (("gf4", _ops.GF4), ("q8_0", _ops.Q8_0), ("q4_k", _ops.Q4_K)):
+                pts += sweep.point(name, t, 12288, 4096, [1], g, device, peak)
+            line["gemv"] = {"shape": "K 4096 -> rows 12288, batch 1, x fp16", "unit": "GB/s",
+                            "peak": peak, "peak_kind": kind,
+                            "rows": [{"codec": r["codec"], "gbs": r["gbs"], "us": r["us"], "frac": r["frac"],
+                                      "frac_of_8tbs": round(r["gbs"] / 8000.0, 3)} for r in pts]}
+        except Exception as exc:  # the GEMV table never blocks the bench line
+            line["gemv"] = {"error": str(exc)[:200]}
     if rank == 0 and world == 1 and not args.no_cpu:
         t, sample = cpu_token_seconds(ctx=args.ctx_fill, head_frac=64)
         line["cpu_baseline"] = {"value": 1.0 / t, "unit": "tok/s", "cores": cpu_cores(), "kind": "port",

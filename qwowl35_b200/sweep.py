@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import os
 import sys
 
 import torch
@@ -51,13 +52,31 @@ def graph_us(fns, reps: int = 3) -> float:
 
 
 def hbm_peak() -> tuple[float, str]:
-    import os
     p = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
     try:
         with open(p) as f:
             return float(json.load(f)["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         return 6650.0, "fallback"
+
+
+def point(name: str, t: int, rows: int, k: int, batches, gen, dev, peak: float) -> list[dict]:
+    """Time ops.matvec for one codec and shape at each batch size (see the module doc)."""
+    wb = ops.weight_bytes(t, rows, k)
+    ncopy = max(2, min(64, (2 * L2) // wb + 1))
+    ws = [ops.repack(t, synth.gen_tensor(gen, t, k, rows, "weight"), rows, k) for _ in range(ncopy)]
+    out = []
+    for B in batches:
+        x = torch.randn(B, k, device=dev).to(torch.float16)
+        y = torch.empty(B, rows, device=dev)
+        fns = [(lambda w=w: ops.matvec(t, w, x, rows, k, y=y)) for w in ws] * max(1, 16 // ncopy)
+        us = graph_us(fns)
+        gbs = (wb + B * k * 2 + B * rows * 4) / us / 1e3
+        out.append(dict(codec=name, rows=rows, k=k, batch=B, us=round(us, 2), gbs=round(gbs, 1),
+                        frac=round(gbs / peak, 3), weight_bytes=wb))
+    del ws
+    torch.cuda.empty_cache()
+    return out
 
 
 def main(argv: list[str]) -> int:
@@ -72,24 +91,11 @@ def main(argv: list[str]) -> int:
     batches = [int(b) for b in a.batches.split(",")]
     rows_out = []
     for name in a.codecs.split(","):
-        t = CODECS[name]
         for rows, k in SHAPES:
-            wb = ops.weight_bytes(t, rows, k)
-            ncopy = max(2, min(64, (2 * L2) // wb + 1))
-            ws = [ops.repack(t, synth.gen_tensor(gen, t, k, rows, "weight"), rows, k) for _ in range(ncopy)]
-            for B in batches:
-                x = torch.randn(B, k, device=dev).to(torch.float16)
-                y = torch.empty(B, rows, device=dev)
-                fns = [(lambda w=w: ops.matvec(t, w, x, rows, k, y=y)) for w in ws] * max(1, 16 // ncopy)
-                us = graph_us(fns)
-                alg = wb + B * k * 2 + B * rows * 4
-                gbs = alg / us / 1e3
-                rows_out.append(dict(codec=name, rows=rows, k=k, batch=B, us=round(us, 2), gbs=round(gbs, 1),
-                                     frac=round(gbs / peak, 3), weight_bytes=wb))
-                print(f"{name:5s} {k:6d}->{rows:<6d} B={B:2d}: {us:9.2f} us  {gbs:7.1f} GB/s  {gbs / peak:5.3f} of {kind}",
-                      flush=True)
-            del ws
-            torch.cuda.empty_cache()
+            for r in point(name, CODECS[name], rows, k, batches, gen, dev, peak):
+                rows_out.append(r)
+                print(f"{name:5s} {k:6d}->{rows:<6d} B={r['batch']:2d}: {r['us']:9.2f} us  {r['gbs']:7.1f} GB/s  "
+                      f"{r['frac']:5.3f} of {kind}", flush=True)
     if a.out:
         with open(a.out, "w") as f:
             f.write(f"| codec | K -> rows | batch | us / launch | GB/s (algorithmic) | of {kind} {peak:.0f} GB/s |\n")
