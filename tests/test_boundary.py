@@ -144,3 +144,23 @@ def test_kv_cache_type_gate_needs_no_gpu(monkeypatch):
         Runtime(m, ctx=64, kv_cache_type=1)
     with pytest.raises(Qw35Error, match="invalid kv_cache_type"):
         Runtime(m, ctx=64, kv_cache_type=2)
+
+
+def test_plain_c_consumer_compiles_links_and_runs(tmp_path):
+    """The headers are C11 (what the reference's Rust extern block binds);
+    struct layouts are checked by static asserts, then the library is linked
+    and its GPU-free entry points are called from C."""
+    import os
+    import shutil
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    exe = tmp_path / "abi_consumer"
+    libdir = str(LIB_PATH.parent)
+    r = subprocess.run([gcc, "-std=c11", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(root, "include"),
+                        os.path.join(root, "tests", "c", "abi_consumer.c"), "-L", libdir, "-lqw35cuda",
+                        f"-Wl,-rpath,{libdir}", "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert run.returncode == 0 and "abi ok" in run.stdout, run.stderr
