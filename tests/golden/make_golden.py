@@ -10,6 +10,9 @@ container).  Sources of truth:
   (``Q8_0.quantize_blocks`` / ``dequantize_blocks``, ``Q4_K`` / ``Q5_K`` /
   ``Q6_K.dequantize_blocks``), the third-party library
   the reference's tools call (``qw35_cook_common.py:34-35``, ``:155-179``).
+  Every K-quant and Q8_0 fixture is also checked, bit for bit, against the
+  reference's own call site ``dequantize_chunk`` (``qw35_cook_common.py:155``)
+  on the same rows.
 
 Usage::
 
@@ -92,6 +95,14 @@ def main(ref_root: str) -> None:
     q6[:, 208:210] = rng.normal(0, 0.002, size=(nb, 1)).astype(np.float16).view(np.uint8)
     q6_deq = Q6_K.dequantize_blocks(q6).reshape(16, 1024).astype(np.float32)
     np.savez_compressed(out_dir / "q6_k.npz", raw=q6.reshape(-1), deq=q6_deq)
+
+    # the reference's own call site gives the same values
+    for raw, tid, rows_, deq in ((q8_rand.reshape(16, -1), cc.Q8_0_TYPE, 16, q8_rand_deq),
+                                 (q4.reshape(16, -1), cc.Q4_K_TYPE, 16, q4_deq),
+                                 (q5.reshape(16, -1), cc.Q5_K_TYPE, 16, q5_deq),
+                                 (q6.reshape(16, -1), cc.Q6_K_TYPE, 16, q6_deq)):
+        ref = np.asarray(cc.dequantize_chunk(raw, tid, 0, rows_), dtype=np.float32)
+        assert np.array_equal(ref.view(np.uint32), deq.view(np.uint32)), tid
 
     (out_dir / "PROVENANCE.txt").write_text(
         "Generated by tests/golden/make_golden.py from the reference's tools/qw35_cook_common.py\n"
