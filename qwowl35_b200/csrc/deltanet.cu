@@ -153,6 +153,116 @@ deltanet_step_kernel(DeltaNetArgs p) {
     }
 }
 
+// ---- a run of T tokens of one sequence (prefill) ------------------------------
+// The step kernel's CTA / cluster layout, looping over the run's tokens with
+// the head's 128 x 128 state in registers (read once, written once per run)
+// and the conv windows in registers (q/k windows written back by rank 0 after
+// a cluster barrier, v windows by their own CTA).  Per token t it reads
+// projection row t and writes output row t; the reference's batched prefill
+// recurrence (qw35_ssm_recurrent_step128_batch_rows_f32, qw35_ssm.metal:453-535)
+// likewise walks the rows in order with the state on chip.
+__device__ __forceinline__ void delta_rows_reg(float4 *sv, const float4 kc, const float4 qc, const float *vrow,
+                                               float gate, float beta, float kq, float scale, float *ysm) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    float kd[8], qd[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        kd[i] = sv[i].x * kc.x + sv[i].y * kc.y + sv[i].z * kc.z + sv[i].w * kc.w;
+        qd[i] = sv[i].x * qc.x + sv[i].y * qc.y + sv[i].z * qc.z + sv[i].w * qc.w;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            kd[i] += __shfl_xor_sync(0xffffffffu, kd[i], o);
+            qd[i] += __shfl_xor_sync(0xffffffffu, qd[i], o);
+        }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = wid * 8 + i;
+        const float delta = (vrow[r] - gate * kd[i]) * beta;
+        sv[i].x = sv[i].x * gate + kc.x * delta;
+        sv[i].y = sv[i].y * gate + kc.y * delta;
+        sv[i].z = sv[i].z * gate + kc.z * delta;
+        sv[i].w = sv[i].w * gate + kc.w * delta;
+        if (lane == 0) ysm[r] = (gate * qd[i] + delta * kq) * scale;
+    }
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512)
+deltanet_run_kernel(DeltaNetArgs p, int T) {
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();
+    const int g = blockIdx.y;
+    const int h = g + NQK * rank;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const long long slot = p.slots ? (long long)p.slots[0] : 0;
+
+    __shared__ __align__(16) float qn_s[DS];
+    __shared__ __align__(16) float kn_s[DS];
+    __shared__ float v_s[DS];
+    __shared__ float y_s[DS];
+    __shared__ float red[32];
+
+    float *cs = p.conv_state + slot * p.conv_stride;
+    float *S = p.ssm_state + slot * p.ssm_stride + (size_t)h * DS * DS;
+    float4 sv[8];
+    load_rows(S, sv);
+
+    // conv windows: threads 0..255 the group's q / k channels, 256..383 this head's v channels
+    int ch = -1;
+    float win[3] = {0.f, 0.f, 0.f};
+    float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (tid < 2 * DS) ch = tid < DS ? g * DS + tid : NQK * DS + g * DS + (tid - DS);
+    else if (tid < 3 * DS) ch = 2 * NQK * DS + h * DS + (tid - 2 * DS);
+    if (ch >= 0) {
+        win[0] = cs[ch * 3 + 0]; win[1] = cs[ch * 3 + 1]; win[2] = cs[ch * 3 + 2];
+        cw = reinterpret_cast<const float4 *>(p.conv_w)[ch];
+    }
+    for (int t = 0; t < T; ++t) {
+        const float *proj = p.proj + (size_t)t * p.proj_stride;
+        float q = 0.0f, k = 0.0f;
+        if (ch >= 0) {
+            const float x = proj[ch];
+            const float o = silu_f(win[0] * cw.x + win[1] * cw.y + win[2] * cw.z + x * cw.w);
+            win[0] = win[1]; win[1] = win[2]; win[2] = x;
+            if (tid < DS) q = o;
+            else if (tid < 2 * DS) k = o;
+            else v_s[tid - 2 * DS] = o;
+        }
+        const float q_ss = block_sum(q * q, red);
+        const float k_ss = block_sum(k * k, red);
+        if (tid < DS) qn_s[tid] = q * (1.0f / fmaxf(sqrtf(q_ss), p.eps));
+        else if (tid < 2 * DS) kn_s[tid - DS] = k * (1.0f / fmaxf(sqrtf(k_ss), p.eps));
+        __syncthreads();
+        const float kq = block_sum(tid < DS ? qn_s[tid] * kn_s[tid] : 0.0f, red);
+        const float beta = sigmoid_f(proj[BOFF + h]);
+        const float gate = expf(softplus_f(proj[AOFF + h] + p.dt[h]) * p.a[h]);
+        const float4 kc4 = reinterpret_cast<const float4 *>(kn_s)[lane];
+        const float4 qc4 = reinterpret_cast<const float4 *>(qn_s)[lane];
+        delta_rows_reg(sv, kc4, qc4, v_s, gate, beta, kq, 0.08838834764831845f, y_s);
+        __syncthreads();
+        const float y2 = block_sum(tid < DS ? y_s[tid] * y_s[tid] : 0.0f, red);
+        const float inv = rsqrtf(y2 / (float)DS + p.eps);
+        if (tid < DS) {
+            const float z = proj[ZOFF + h * DS + tid];
+            p.out[(size_t)t * p.out_stride + h * DS + tid] = y_s[tid] * inv * p.norm_w[tid] * silu_f(z);
+        }
+    }
+    // state rows, written once
+#pragma unroll
+    for (int i = 0; i < 8; ++i) __stcs(reinterpret_cast<float4 *>(S + (size_t)(wid * 8 + i) * DS) + lane, sv[i]);
+    // v windows are this head's own; the q / k windows are shared by the pair:
+    // rank 0 writes them once both CTAs have read the old ones (at entry)
+    if (tid >= 2 * DS && ch >= 0) {
+        cs[ch * 3 + 0] = win[0]; cs[ch * 3 + 1] = win[1]; cs[ch * 3 + 2] = win[2];
+    }
+    cluster.sync();
+    if (rank == 0 && tid < 2 * DS) {
+        cs[ch * 3 + 0] = win[0]; cs[ch * 3 + 1] = win[1]; cs[ch * 3 + 2] = win[2];
+    }
+}
+
 // Recurrent core only (config 3 of the benchmark): prepared q/k/v, beta, g.
 __global__ void __launch_bounds__(128) deltanet_core_kernel(DeltaCoreArgs p) {
     const int rb = blockIdx.x & 3;
@@ -189,6 +299,13 @@ cudaError_t deltanet_step_run(const DeltaNetArgs &a, cudaStream_t st) {
     if (a.n_seq > 65535) return cudaErrorInvalidValue;
     dim3 grid(2, NQK, a.n_seq);
     deltanet_step_kernel<<<grid, 512, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t deltanet_run_tokens(const DeltaNetArgs &a, int T, cudaStream_t st) {
+    if (T <= 0) return cudaSuccess;
+    dim3 grid(2, NQK, 1);
+    deltanet_run_kernel<<<grid, 512, 0, st>>>(a, T);
     return cudaGetLastError();
 }
 

@@ -65,6 +65,9 @@ struct DeltaNetArgs {
     float eps = 1e-6f;
 };
 cudaError_t deltanet_step_run(const DeltaNetArgs &a, cudaStream_t st);
+// T consecutive tokens of ONE sequence (slot a.slots[0]): projection row t at
+// a.proj + t * proj_stride, output row t at a.out + t * out_stride
+cudaError_t deltanet_run_tokens(const DeltaNetArgs &a, int T, cudaStream_t st);
 
 struct DeltaCoreArgs {
     int n_seq = 0;

@@ -86,7 +86,8 @@ struct Runtime {
     uint32_t ctx = 0, vocab = 0, prefill_chunk = 1;
     uint32_t max_seqs = 1;
     uint32_t rows = 1;             // rows of the step buffers: max_seqs, or a longer prefill run
-    bool batched_prefill = false;  // eval_tokens runs a token run as one batched pass (QW35_PREFILL=1)
+    bool batched_prefill = false;  // eval_tokens runs a token run as one batched pass (QW35_PREFILL=1 or 2)
+    bool prefill_dn_run = false;   // ... with one DeltaNet launch per layer for the whole run (QW35_PREFILL=2)
     int attn_window = 0, attn_sink = 0;
     cudaStream_t stream = nullptr;
     std::string deferred_error;

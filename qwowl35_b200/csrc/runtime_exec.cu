@@ -98,6 +98,8 @@ static void encode_step(Runtime *rt, int n, int mode, int maxlen, bool prefill =
             d.eps = eps;
             if (!prefill) {
                 ck(deltanet_step_run(d, st), "deltanet");
+            } else if (rt->prefill_dn_run) {
+                ck(deltanet_run_tokens(d, n, st), "deltanet run");  // rows in order, state on chip
             } else {
                 for (int t = 0; t < n; ++t) {  // the recurrence is sequential over the run
                     DeltaNetArgs dt = d;

@@ -113,6 +113,7 @@ Runtime *create_runtime(std::shared_ptr<ModelStore> ms, uint32_t ctx, uint32_t v
 
     // step buffers hold max_seqs rows, or a batched prefill run (<= 64 tokens) when longer
     rt->batched_prefill = getenv("QW35_PREFILL") != nullptr;
+    rt->prefill_dn_run = rt->batched_prefill && strcmp(getenv("QW35_PREFILL"), "2") == 0;
     const uint32_t R = rt->batched_prefill ? std::max<uint32_t>(S, std::min<uint32_t>(rt->prefill_chunk, 64)) : S;
     rt->rows = R;
     rt->d_in = dmalloc<int32_t>(4ull * R);

@@ -250,11 +250,12 @@ def test_q8_0_kv_cache_matches_oracle(small):
 
 
 @pytest.mark.skipif(not __import__("os").environ.get("QW35_PREFILL"),
-                    reason="batched prefill not yet enabled (QW35_PREFILL=1)")
+                    reason="batched prefill not yet enabled (QW35_PREFILL=1 or 2)")
 def test_batched_prefill_matches_oracle(small):
     # 7 tokens in one pass: batch-7 matvecs (tensor-core path, the reference's
     # tiled-path weight semantics), 7 attention rows over one sequence, the
-    # DeltaNet recurrence row by row; logits of the last token
+    # DeltaNet recurrence row by row (QW35_PREFILL=2: one launch per layer with
+    # the state on chip); logits of the last token
     rt = Runtime(small, ctx=512, prefill_chunk=8)
     rt.eval_prefill_chunk(TOKENS, 0, LogitsMode.FULL)
     got = rt.copy_logits()
