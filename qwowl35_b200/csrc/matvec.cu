@@ -466,7 +466,10 @@ static MvGeom mv_geometry(int rows, int K, const void *kern) {
     g.kw = (nchunk + 31) / 32;
     codec_rows(CODEC, K, g.code_row, g.scale_row);
     const uint32_t rb = g.code_row + g.scale_row;
-    if (CODEC == QW35_GF4_TYPE) {
+    // QW35_MV_KQ_WIDE=1 gives the K-quants the same geometry (a tuning switch)
+    static const bool kq_wide = getenv("QW35_MV_KQ_WIDE") != nullptr;
+    const bool kquant = CODEC == QW35_Q4_K_TYPE || CODEC == QW35_Q5_K_TYPE || CODEC == QW35_Q6_K_TYPE;
+    if (CODEC == QW35_GF4_TYPE || (kquant && kq_wide)) {
         // GF4 decode is latency-heavy: ~16 consumer warps keep rows in flight
         // (measured: gate/up pair 31.5 -> 28.2 us at B = 1)
         g.rs = g.kw >= 16 ? 1 : 16 / g.kw;
@@ -477,7 +480,8 @@ static MvGeom mv_geometry(int rows, int K, const void *kern) {
     }
     g.threads = (g.kw * g.rs + 1) * 32;
     g.G = g.G < 1 ? 1 : (g.G > 16 ? 16 : g.G);
-    if (CODEC == QW35_GF4_TYPE && g.G >= g.rs) g.G -= g.G % g.rs;  // whole rounds of the row slots
+    if ((CODEC == QW35_GF4_TYPE || (kquant && kq_wide)) && g.G >= g.rs)
+        g.G -= g.G % g.rs;  // whole rounds of the row slots
     g.stage_bytes = ((uint32_t)g.G * rb + 127u) & ~127u;
     g.smem = (size_t)NM * kStages * g.stage_bytes + (size_t)2 * g.G * B * NM * g.kw * 4 + 64 * 4 +
              2 * kStages * 8 + 16;
