@@ -261,3 +261,26 @@ def test_batched_path_weights_bit_exact(t, exact):
         x[np.arange(b), k0 + np.arange(b)] = 1.0
         y = ops.matvec(t, w, torch.from_numpy(x).cuda(), rows, k, exact=exact).cpu().numpy()
         np.testing.assert_array_equal(y, deq[:, k0:k0 + b].T)
+
+
+@pytest.mark.parametrize("b", [1, 32])
+def test_full_size_q6_k_head_argmax_matches_its_logits(b):
+    """The real model's head shape (Q6_K 248320 x 4096): argmax ids are
+    bit-exact with the lowest-id argmax of the returned logits, at the batch
+    sizes of both matvec paths; a row sample of the logits is checked
+    against the oracle."""
+    from qwowl35_b200 import synth
+    rows, k = 248320, 4096
+    g = synth._Gen(41, torch.device("cuda"))
+    raw = synth.gen_tensor(g, Q.Q6_K_TYPE, k, rows, "weight")
+    w = ops.repack(Q.Q6_K_TYPE, raw, rows, k)
+    x = torch.randn(b, k, device="cuda", generator=torch.Generator(device="cuda").manual_seed(42))
+    tok, val, logits = ops.argmax_head(Q.Q6_K_TYPE, w, x, rows, k, want_logits=True)
+    lg = logits.cpu().numpy()
+    for i in range(b):
+        ref_id, ref_v = O.argmax_lowest(lg[i])
+        assert int(tok[i]) == ref_id and float(val[i]) == ref_v
+    sel = np.arange(0, rows, 997)
+    raw_h = raw.cpu().numpy().reshape(rows, -1)[sel].reshape(-1)
+    ref = O.matvec(Q.dequant(Q.Q6_K_TYPE, raw_h, len(sel), k, tiled=b >= 3), x.cpu().numpy())
+    assert relerr(lg[:, sel], ref) < TOL
