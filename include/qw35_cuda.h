@@ -8,7 +8,10 @@
 // the reference's: return 1 (or a size) on success, 0 on failure with a
 // NUL-terminated message in err[err_len]; device pointers are plain
 // addresses on the current CUDA device; `stream` is a cudaStream_t (NULL =
-// legacy default stream).  Per-op calls are asynchronous on that stream.
+// legacy default stream).  Per-op calls are asynchronous on that stream;
+// a per-op matvec that needs tensor-core scratch takes it from the stream's
+// memory pool (cudaMallocAsync / cudaFreeAsync on `stream`), so it never
+// synchronises the device and never shares scratch with another call.
 #ifndef QW35_CUDA_H
 #define QW35_CUDA_H
 
@@ -140,6 +143,8 @@ int qw35_cuda_gqa_decode_q8_0(uint32_t n_seq, const float *q, const float *gate,
 // qw35_cuda_gqa_noalloc_max_bytes().  The first call on a device looks up the
 // array's device address (make it before any stream capture); all calls share
 // the array, so calls that may run concurrently on the GPU must not overlap.
+// The looked-up address is kept for the life of the process: after a
+// cudaDeviceReset of a device this entry point must not be called on it.
 uint64_t qw35_cuda_gqa_noalloc_max_bytes(void);
 int qw35_cuda_gqa_decode_noalloc(uint32_t n_seq, const float *q, const float *gate, const int32_t *seq_len,
                                  uint32_t max_len, const uint64_t *chunk_ptrs, uint32_t max_chunks, uint64_t k_off,
@@ -182,6 +187,11 @@ uint32_t qw35_cuda_runtime_last_step_kernels(void *runtime);
 // Device bytes held by the runtime's KV chunk pool and by the shared weights.
 uint64_t qw35_cuda_runtime_kv_bytes(void *runtime);
 uint64_t qw35_cuda_runtime_weight_bytes(void *runtime);
+// Device address (and, in *bytes, the size) of the scratch this runtime's
+// tensor-core matvecs use.  Each runtime owns its scratch from create to
+// destroy; its captured step graphs hold this address, which never changes.
+// 0 when no batch of the runtime reaches the tensor-core path.
+uint64_t qw35_cuda_runtime_scratch(void *runtime, uint64_t *bytes);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -112,6 +112,7 @@ _SIGS = {
     "qw35_cuda_runtime_last_step_kernels": (C.c_uint32, [vp]),
     "qw35_cuda_runtime_kv_bytes": (C.c_uint64, [vp]),
     "qw35_cuda_runtime_weight_bytes": (C.c_uint64, [vp]),
+    "qw35_cuda_runtime_scratch": (C.c_uint64, [vp, C.POINTER(C.c_uint64)]),
 }
 
 _lib = None

@@ -488,22 +488,13 @@ cudaError_t attn_decode_run(const AttnArgs &a, cudaStream_t st) {
     const int ns = (a.max_len + ASPLIT - 1) / ASPLIT;
     dim3 g1(ns, AKV, a.n_seq);
     cudaError_t e0;
-    static bool attr = false, attr_q8 = false;
     if (a.kv_q8) {
-        if (!attr_q8) {
-            e0 = cudaFuncSetAttribute(attn_split_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)ASMEM_Q8);
-            if (e0 != cudaSuccess) return e0;
-            attr_q8 = true;
-        }
+        e0 = qw35h::smem_optin((const void *)attn_split_kernel<true>, (int)ASMEM_Q8);
+        if (e0 != cudaSuccess) return e0;
         attn_split_kernel<true><<<g1, 128, ASMEM_Q8, st>>>(a, ns);
     } else {
-        if (!attr) {
-            e0 = cudaFuncSetAttribute(attn_split_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)ASMEM);
-            if (e0 != cudaSuccess) return e0;
-            attr = true;
-        }
+        e0 = qw35h::smem_optin((const void *)attn_split_kernel<false>, (int)ASMEM);
+        if (e0 != cudaSuccess) return e0;
         attn_split_kernel<false><<<g1, 128, ASMEM, st>>>(a, ns);
     }
     cudaError_t e = cudaGetLastError();

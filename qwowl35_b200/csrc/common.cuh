@@ -88,4 +88,6 @@ __device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
 // Host-side helpers shared by the launch wrappers.
 namespace qw35h {
 int sm_count();
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (current device, kernel)
+cudaError_t smem_optin(const void *func, int bytes);
 }

@@ -3,6 +3,8 @@
 // Reference: qw35_get_row_q4_k_f32 / qw35_get_row_q8_0_f32
 // (qw35_matvec.metal:100-149), qw35_rms_norm_weight_f32 (qw35_core.metal:14-48).
 #include <mutex>
+#include <set>
+#include <tuple>
 
 #include "common.cuh"
 #include "ops.h"
@@ -20,6 +22,23 @@ int sm_count() {
         cached[dev] = n > 0 ? n : 1;
     }
     return cached[dev];
+}
+
+// The dynamic shared-memory opt-in is a per-device property of a kernel: it is
+// recorded per (device, kernel) under a lock, so a process that launches on
+// several devices, from several host threads, sets it once on each.
+cudaError_t smem_optin(const void *func, int bytes) {
+    static std::mutex mu;
+    static std::set<std::tuple<int, const void *, int>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> g(mu);
+    const auto key = std::make_tuple(dev, func, bytes);
+    if (done.count(key)) return cudaSuccess;
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.insert(key);
+    return e;
 }
 }  // namespace qw35h
 

@@ -89,20 +89,7 @@ struct DqParams {
     int rows, K, B, tiles;
     int gran, granules;     // schedule: granules of `gran` k-chunks spread over the grid
     int red_tma;            // split tiles add into y by TMA bulk reduction (else per-element atomics)
-    unsigned long long *trace;  // debug: per-chunk event stamps of CTA 0 (QW35_DQ_TRACE), or null
 };
-// trace layout: [chunk][10] = weight issue, decoder sees full_w, decoder done,
-// mma sees full_a, mma committed, activation issue, mma sees full_x, last
-// decoder warp done, MMA loop SM cycles, (unused)
-#define DQ_TRACE(c, slot) \
-    do { if (p.trace && blockIdx.x == 0 && (c) < 255) p.trace[(c) * 10 + (slot)] = globaltimer(); } while (0)
-// kernel-level stamps live in row 255: 0 entry, 1 setup done, 2 activations
-// released (PDL), 3 last epilogue write, 4 max exit over CTAs, 5 ~min entry over
-// CTAs, 6 last accumulator ready, 7 index of the last segment
-#define DQ_STAMP(slot) \
-    do { if (p.trace && blockIdx.x == 0) p.trace[255 * 10 + (slot)] = globaltimer(); } while (0)
-#define DQ_TRACE_MAX(c, slot) \
-    do { if (p.trace && blockIdx.x == 0 && (c) < 255) atomicMax(&p.trace[(c) * 10 + (slot)], globaltimer()); } while (0)
 
 // activation stage: the chunk's 2*NP rows (hi | lo) x KC columns of f16
 template <int CODEC, int NP>
@@ -327,11 +314,6 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nch = p.K / KC;
-    if (p.trace && threadIdx.x == 0) {
-        const unsigned long long t = globaltimer();
-        if (blockIdx.x == 0) p.trace[255 * 10] = t;
-        atomicMax(&p.trace[255 * 10 + 5], ~t);
-    }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NW; ++s) {
@@ -359,7 +341,6 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    if (threadIdx.x == 0) DQ_STAMP(1);
     int gbeg, gend;
     dq_range(p, gbeg, gend);
 
@@ -378,7 +359,6 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                 for (int kc = c0; kc < c1 && !*abort_flag; ++kc, ++c) {
                     if (c >= NW) dq_wait(&empty_w[rw.s], rw.ph ^ 1u, abort_flag, 8u);
                     if (*abort_flag) break;
-                    DQ_TRACE(c, 0);
                     uint8_t *dst = wst + (size_t)rw.s * WS;
                     mbar_arrive_expect_tx(&full_w[rw.s], WS);
                     // x coordinate in elements: 32-bit words (GF4) or bytes (Q8_0)
@@ -406,14 +386,12 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
             // the activation chunks are re-read by every CTA: keep them in L2
             const uint64_t pol = policy_evict_last();
             pdl_wait();  // written by the activation prep, the previous kernel
-            DQ_STAMP(2);
             int c = 0;
             Ring rx;
             DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
                 for (int kc = c0; kc < c1 && !*abort_flag; ++kc, ++c) {
                     if (c >= SX) dq_wait(&free_x[rx.s], rx.ph ^ 1u, abort_flag, 8u);
                     if (*abort_flag) break;
-                    DQ_TRACE(c, 5);
                     mbar_arrive_expect_tx(&full_x[rx.s], XS);
                     bulk_g2s(xst + (size_t)rx.s * XS, p.xprep + (size_t)kc * XS, XS, &full_x[rx.s], pol);
                     rx.next(SX);
@@ -436,17 +414,14 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                 for (int kc = c0; kc < c1; ++kc, ++c) {
                     const int sx = rx.s, sa = ra.s;
                     dq_wait(&full_x[sx], rx.ph, abort_flag, 16u);
-                    if (lane == 0) DQ_TRACE(c, 6);
                     dq_wait(&full_a[sa], ra.ph, abort_flag, 16u);
                     if (*abort_flag) break;
-                    if (lane == 0) DQ_TRACE(c, 3);
                     tc_fence_after();
                     const uint32_t a0 = tmem + T::A0 + sa * G::ACOLS;
                     // descriptor of k-step 0; later k-steps add a compile-time offset
                     // (start address field, 16-byte units; smem addresses stay < 2^18)
                     const uint64_t bd0 = smem_desc_sw128(smem_u32(xst + (size_t)sx * XS));
                     const uint32_t d0 = tmem + ab * RC;
-                    const long long cyc0 = p.trace ? clock64() : 0;
                     if (elect_one()) {
                         tc_mma_f16_ts(d0, a0, bd0, IDESC, kc > c0 ? 1u : 0u);
                         if constexpr (Q8) tc_mma_f16_ts_acc(d0, a0 + 64, bd0, IDESC_HI);
@@ -463,8 +438,6 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                         if (kc + 1 == c1) tc_commit(&acc_full[ab]);
                     }
                     __syncwarp();
-                    if (lane == 0 && p.trace && blockIdx.x == 0 && c < 255) p.trace[c * 10 + 8] = clock64() - cyc0;
-                    if (lane == 0) DQ_TRACE(c, 4);
                     rx.next(SX);
                     ra.next(SA);
                 }
@@ -494,7 +467,6 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
             for (int kc = c0; kc < c1 && !*abort_flag; ++kc, ++c) {
                 const int sw = rw.s, sa = ra.s;
                 dq_wait(&full_w[sw], rw.ph, abort_flag, 32u);
-                if (dw == 0 && lane == 0) DQ_TRACE(c, 1);
                 if (c >= SA) dq_wait(&free_a[sa], ra.ph ^ 1u, abort_flag, 32u);
                 if (*abort_flag) break;
                 tc_fence_after();
@@ -602,9 +574,7 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                 tmem_st_wait();
                 tc_fence_before();
                 __syncwarp();
-                if (dw == 0 && lane == 0) DQ_TRACE(c, 2);
                 if (lane == 0) {
-                    DQ_TRACE_MAX(c, 7);
                     mbar_arrive(&empty_w[sw]);
                     mbar_arrive(&full_a[sa]);
                 }
@@ -629,7 +599,6 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                 const int row = tile * TM + row_in_tile;
                 const int ab = ul & 1;
                 dq_wait(&acc_full[ab], (ul >> 1) & 1, abort_flag, 64u);
-                if (lane == 0 && ew == 0) DQ_STAMP(6);
                 tc_fence_after();
                 float es = 1.0f;  // Q8_0: 2^-e of the row
                 if constexpr (Q8) {
@@ -686,8 +655,6 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                         }
                     }
                 }
-                if (lane == 0 && ew == 0) DQ_STAMP(3);
-                if (lane == 0 && ew == 0 && p.trace && blockIdx.x == 0) p.trace[255 * 10 + 7] = ul;
                 ++ul;
             }
         })
@@ -714,7 +681,6 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem, 512);
-    if (p.trace && threadIdx.x == 0) atomicMax(&p.trace[255 * 10 + 4], globaltimer());
 }
 
 // ---------------------------------------------------------------------------
@@ -1047,38 +1013,6 @@ bool out_map(const void *y, uint32_t rows, uint32_t B, CUtensorMap *out) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Per-device scratch for the activation prep and the two-pass epilogues.
-// Grows only outside stream capture (the runtime reserves it up front).
-struct Scratch {
-    void *ptr = nullptr;
-    size_t bytes = 0;
-};
-std::mutex g_scratch_mu;
-Scratch g_scratch[64];
-
-cudaError_t scratch_get(size_t bytes, void **out, cudaStream_t st) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-    std::lock_guard<std::mutex> g(g_scratch_mu);
-    Scratch &s = g_scratch[dev];
-    if (s.bytes < bytes) {
-        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        if (st) cudaStreamIsCapturing(st, &cs);
-        if (cs != cudaStreamCaptureStatusNone) return cudaErrorStreamCaptureUnsupported;
-        cudaError_t e = cudaDeviceSynchronize();
-        if (e != cudaSuccess) return e;
-        if (s.ptr) cudaFree(s.ptr);
-        s.ptr = nullptr;
-        s.bytes = 0;
-        e = cudaMalloc(&s.ptr, bytes);
-        if (e != cudaSuccess) return e;
-        s.bytes = bytes;
-    }
-    *out = s.ptr;
-    return cudaSuccess;
-}
-
 int dq_np(int B) { return B <= 16 ? 16 : (B <= 32 ? 32 : 64); }
 
 }  // namespace
@@ -1116,11 +1050,6 @@ size_t dq_scratch_bytes(int B, uint32_t k, uint32_t rows_out) {
     return dq_scratch_layout(B, k, rows_out, (size_t)2 * B * rows_out * 4).total;
 }
 
-cudaError_t dq_reserve(int max_batch, uint32_t max_k, uint32_t max_rows_out) {
-    void *p = nullptr;
-    return scratch_get(dq_scratch_bytes(max_batch, max_k, max_rows_out), &p, nullptr);
-}
-
 struct DqMaps {
     CUtensorMap m0, m1, s0, s1, y0, y1, h0, h1;  // codes, side planes, outputs, high bits (per matrix)
 };
@@ -1136,27 +1065,12 @@ static cudaError_t dq_launch(const DqMaps &M, DqParams p, cudaStream_t st) {
     int SX = xs >= 65536u ? 2 : 3;
     // (at least two weight stages: Q6_K's 28 KB stages then pass the budget)
     int NW = std::max(2, std::min(4, (int)((budget - SX * xs) / ws)));
-    static const int env_sx = getenv("QW35_DQ_SX") ? atoi(getenv("QW35_DQ_SX")) : 0;  // tuning experiments
-    static const int env_nw = getenv("QW35_DQ_NW") ? atoi(getenv("QW35_DQ_NW")) : 0;
-    if (env_sx >= 2 && env_nw >= 2 && env_sx * xs + env_nw * ws <= budget) {
-        SX = env_sx;
-        NW = env_nw;
-    }
     using T = DqTmem<CODEC, NP>;
     const size_t smem = 1024 + (size_t)SX * xs + (size_t)NW * ws + 2 * 16 * TM * 4 +
                         (2 * NW + 2 * SX + 2 * T::SA + 4 + 1) * 8 + 16;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    {
+        cudaError_t e = qw35h::smem_optin((const void *)kern, 227 * 1024);
         if (e != cudaSuccess) return e;
-        attr = true;
-    }
-    static unsigned long long *trace = nullptr;
-    static const bool want_trace = getenv("QW35_DQ_TRACE") != nullptr;
-    if (want_trace) {
-        if (!trace) cudaMalloc(&trace, 256 * 10 * 8);
-        cudaMemsetAsync(trace, 0, 256 * 10 * 8, st);
-        p.trace = trace;
     }
     const int grid = std::min(p.granules, qw35h::sm_count());
     cudaLaunchConfig_t cfg{};
@@ -1170,25 +1084,6 @@ static cudaError_t dq_launch(const DqMaps &M, DqParams p, cudaStream_t st) {
     cfg.attrs = attrs;
     cfg.numAttrs = getenv("QW35_NO_PDL") ? 0 : 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, M.m0, M.m1, M.s0, M.s1, M.y0, M.y1, M.h0, M.h1, p, SX, NW);
-    if (p.trace) {
-        unsigned long long h[256 * 10];
-        cudaMemcpy(h, trace, sizeof(h), cudaMemcpyDeviceToHost);
-        const unsigned long long t0 = h[0];
-        const unsigned long long *k = h + 255 * 10;
-        auto rel = [&](unsigned long long v) { return v ? (long long)(v - k[0]) : -1ll; };
-        fprintf(stderr, "dq kernel: first CTA entry %lld, CTA0 setup %lld, act released %lld, first W issue %lld, "
-                        "CTA0 last acc ready %lld, last epilogue done %lld (segment %llu), last CTA exit %lld "
-                        "(ns from CTA0 entry)\n",
-                rel(~k[5]), rel(k[1]), rel(k[2]), rel(t0), rel(k[6]), rel(k[3]), k[7], rel(k[4]));
-        fprintf(stderr, "dq trace granules=%d gran=%d grid=%d SX=%d SA=%d NW=%d (ns from first issue)\n", p.granules,
-                p.gran, grid, SX, T::SA, NW);
-        for (int c = 0; c < 255 && h[c * 10]; ++c) {
-            const unsigned long long *r = h + c * 10;
-            auto d = [&](int i) { return r[i] ? (long long)(r[i] - t0) : -1ll; };
-            fprintf(stderr, "c%3d w %6lld x %6lld | dec: full %6lld w0 %6lld last %6lld | mma: x %6lld a %6lld done %6lld cyc %4llu\n",
-                    c, d(0), d(5), d(1), d(2), d(7), d(6), d(3), d(4), r[8]);
-        }
-    }
     return e;
 }
 
@@ -1213,10 +1108,12 @@ static cudaError_t dq_dispatch_np(int NP, int mode, bool exact, const DqMaps &M,
     return dq_dispatch_mode<CODEC, 64>(mode, exact, M, p, st);
 }
 
+static cudaError_t dq_enqueue(const MatvecArgs &a, int mode, uint32_t *tok, float *val, const DqScratch &lay,
+                              void *scr, DqMaps &M, cudaStream_t st);
+
 // mode: 0 store, 1 accumulate, 2 swiglu pair, 3 logits for the argmax head
 cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cudaStream_t st) {
-    const int B = a.batch, NP = dq_np(B);
-    const int K = (int)a.k, rows = (int)a.rows;
+    const int B = a.batch, rows = (int)a.rows;
     const bool dual = mode == 2;
     DqMaps M;
     CUtensorMap &m0 = M.m0, &m1 = M.m1;
@@ -1239,9 +1136,29 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
     }
     const size_t extra = (mode == 2) ? (size_t)2 * B * rows * 4 : (mode == 3 && !a.y) ? (size_t)B * rows * 4 : 0;
     const DqScratch lay = dq_scratch_layout(B, a.k, a.rows, extra);
-    void *scr = nullptr;
-    cudaError_t e = scratch_get(lay.total, &scr, st);
-    if (e != cudaSuccess) return e;
+    // the caller's scratch (a runtime owns one for its lifetime), else a
+    // stream-ordered allocation returned after this call's kernels
+    void *scr = a.scratch;
+    cudaError_t e = cudaSuccess;
+    if (scr) {
+        if (a.scratch_bytes < lay.total) return cudaErrorInvalidValue;
+    } else {
+        e = cudaMallocAsync(&scr, lay.total, st);
+        if (e != cudaSuccess) return e;
+        e = dq_enqueue(a, mode, tok, val, lay, scr, M, st);
+        cudaError_t f = cudaFreeAsync(scr, st);
+        return e != cudaSuccess ? e : f;
+    }
+    return dq_enqueue(a, mode, tok, val, lay, scr, M, st);
+}
+
+static cudaError_t dq_enqueue(const MatvecArgs &a, int mode, uint32_t *tok, float *val, const DqScratch &lay,
+                              void *scr, DqMaps &M, cudaStream_t st) {
+    const int B = a.batch, NP = dq_np(B);
+    const int K = (int)a.k, rows = (int)a.rows;
+    const bool dual = mode == 2;
+    CUtensorMap &m0 = M.m0;
+    cudaError_t e = cudaSuccess;
     uint8_t *base = static_cast<uint8_t *>(scr);
     __half *xh = reinterpret_cast<__half *>(base + lay.x);
     float *rowscale = reinterpret_cast<float *>(base + lay.rowscale);

@@ -66,10 +66,9 @@ void *create(const void *map, uint64_t size, const qw35_metal_tensor_desc *tenso
         set_err(err, len, "invalid runtime creation inputs");
         return nullptr;
     }
-    // q8_0 KV (kv_type 1): built, enabled by QW35_KV_Q8=1 until it has run on a GPU
-    if (kv_type > 1 || (kv_type == 1 && getenv("QW35_KV_Q8") == nullptr)) {
-        set_err(err, len, kv_type > 1 ? "invalid kv_cache_type (0 = f16, 1 = q8_0)"
-                                      : "kv_cache_type q8_0 is not enabled in this build (set QW35_KV_Q8=1; 0 = f16)");
+    // kv_cache_type (bridge.rs:31-42): 0 = f16, 1 = q8_0
+    if (kv_type > 1) {
+        set_err(err, len, "invalid kv_cache_type (0 = f16, 1 = q8_0)");
         return nullptr;
     }
     int ndev = 0;
@@ -222,7 +221,7 @@ int qw35_metal_runtime_eval_tokens(void *runtime, const uint32_t *tokens, uintpt
         if ((uint64_t)pos0 + len > rt->ctx) qw35::fail("requested position exceeds allocated context");
         const uint32_t seq = 0;
         if (rt->batched_prefill && len > 1) {
-            // one pass per run of up to rt->rows tokens (QW35_PREFILL=1): weights are
+            // one pass per run of up to rt->rows tokens: weights are
             // read once per run instead of once per token; the head only on the last
             for (uintptr_t i = 0; i < len; i += rt->rows) {
                 const uint32_t m = (uint32_t)std::min<uintptr_t>(rt->rows, len - i);
@@ -367,6 +366,12 @@ uint64_t qw35_cuda_runtime_kv_bytes(void *runtime) {
 uint64_t qw35_cuda_runtime_weight_bytes(void *runtime) {
     Runtime *rt = lookup(runtime);
     return rt ? rt->model->bytes : 0;
+}
+
+uint64_t qw35_cuda_runtime_scratch(void *runtime, uint64_t *bytes) {
+    Runtime *rt = lookup(runtime);
+    if (bytes) *bytes = rt ? rt->dq_scratch_bytes : 0;
+    return rt ? reinterpret_cast<uint64_t>(rt->dq_scratch) : 0;
 }
 
 }  // extern "C"

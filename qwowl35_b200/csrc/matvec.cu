@@ -498,11 +498,9 @@ static MvGeom mv_geometry(int rows, int K, const void *kern) {
 template <int CODEC, int B, int MODE, bool EXACT, typename XT>
 static cudaError_t mv_launch(MvParams p, cudaStream_t st, int *ctas_out) {
     auto kern = mv_kernel<CODEC, B, MODE, EXACT, XT>;
-    static bool attr_set = false;  // once per kernel instantiation
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    {
+        cudaError_t e = qw35h::smem_optin((const void *)kern, 200 * 1024);
         if (e != cudaSuccess) return e;
-        attr_set = true;
     }
     MvGeom g = mv_geometry<CODEC, B, MODE>(p.rows, p.K, (const void *)kern);
     if (g.kw > 12 || g.smem > 200 * 1024) return cudaErrorInvalidValue;

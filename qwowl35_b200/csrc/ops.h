@@ -23,6 +23,11 @@ struct MatvecArgs {
     int batch = 1;
     int mode = 0;                  // 0 store, 1 accumulate, 2 swiglu pair
     uint32_t flags = 0;
+    // tensor-core path scratch (activation tiles, row scales, two-pass
+    // outputs), owned by the caller: dq_scratch_bytes(batch, k, rows) bytes.
+    // Null: the call takes a stream-ordered allocation of its own.
+    void *scratch = nullptr;
+    size_t scratch_bytes = 0;
 };
 
 cudaError_t matvec_run(const MatvecArgs &a, cudaStream_t st);
@@ -38,7 +43,6 @@ constexpr int kDqMinBatch = 3;  // from 3 rows the CUDA-core path needs 2+ weigh
 bool dq_supported(const MatvecArgs &a);
 cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cudaStream_t st);
 size_t dq_scratch_bytes(int B, uint32_t k, uint32_t rows_out);
-cudaError_t dq_reserve(int max_batch, uint32_t max_k, uint32_t max_rows_out);
 
 cudaError_t weight_repack(uint32_t type_id, const void *src, void *dst, uint32_t rows, uint32_t k,
                           cudaStream_t st);

@@ -86,8 +86,8 @@ struct Runtime {
     uint32_t ctx = 0, vocab = 0, prefill_chunk = 1;
     uint32_t max_seqs = 1;
     uint32_t rows = 1;             // rows of the step buffers: max_seqs, or a longer prefill run
-    bool batched_prefill = false;  // eval_tokens runs a token run as one batched pass (QW35_PREFILL=1 or 2)
-    bool prefill_dn_run = false;   // ... with one DeltaNet launch per layer for the whole run (QW35_PREFILL=2)
+    bool batched_prefill = false;  // eval_tokens runs a token run as one batched pass (default; QW35_PREFILL=0 off)
+    bool prefill_dn_run = false;   // ... with one DeltaNet launch per layer for the whole run (default; QW35_PREFILL=1 off)
     int attn_window = 0, attn_sink = 0;
     cudaStream_t stream = nullptr;
     std::string deferred_error;
@@ -128,6 +128,8 @@ struct Runtime {
     size_t argmax_ws_bytes = 0;
     void *attn_ws = nullptr;
     size_t attn_ws_bytes = 0;
+    void *dq_scratch = nullptr;     // tensor-core matvec scratch, owned for the runtime's lifetime
+    size_t dq_scratch_bytes = 0;    // (its graphs hold this address; it never moves)
     float *rope_freq = nullptr;
     uint32_t proj_stride = 0;
 

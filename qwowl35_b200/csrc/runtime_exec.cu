@@ -35,6 +35,8 @@ static void mv(Runtime *rt, const DevTensor &w, const void *x, const float *norm
     a.k = w.k;
     a.batch = n;
     a.mode = mode;
+    a.scratch = rt->dq_scratch;
+    a.scratch_bytes = rt->dq_scratch_bytes;
     ck(matvec_run(a, rt->stream), "matvec");
 }
 
@@ -167,6 +169,8 @@ static void encode_step(Runtime *rt, int n, int mode, int maxlen, bool prefill =
         a.rows = ms.output.rows;
         a.k = ms.output.k;
         a.batch = hn;
+        a.scratch = rt->dq_scratch;
+        a.scratch_bytes = rt->dq_scratch_bytes;
         ck(argmax_head_run(a, rt->d_argmax_tok, rt->d_argmax_val, rt->argmax_ws, rt->argmax_ws_bytes, st),
            "argmax head");
     } else if (mode == QW35_LOGITS_FULL) {

@@ -50,7 +50,8 @@ Runtime::~Runtime() {
     if (stream) cudaStreamSynchronize(stream);
     for (auto &kv : graphs) cudaGraphExecDestroy(kv.second);
     void *dev_ptrs[] = {conv_state, ssm_state, d_chunk_table, d_in, act, proj, core, hbuf, qbuf, gbuf,
-                        logits, d_argmax_tok, d_argmax_val, argmax_ws, attn_ws, rope_freq, mixed_tmp};
+                        logits, d_argmax_tok, d_argmax_val, argmax_ws, attn_ws, rope_freq, mixed_tmp,
+                        dq_scratch};
     for (void *p : dev_ptrs)
         if (p) cudaFree(p);
     for (void *p : arenas) cudaFree(p);
@@ -112,8 +113,14 @@ Runtime *create_runtime(std::shared_ptr<ModelStore> ms, uint32_t ctx, uint32_t v
     ck(cudaMemset(rt->d_chunk_table, 0, (size_t)S * rt->table_chunks * 8), "memset");
 
     // step buffers hold max_seqs rows, or a batched prefill run (<= 64 tokens) when longer
-    rt->batched_prefill = getenv("QW35_PREFILL") != nullptr;
-    rt->prefill_dn_run = rt->batched_prefill && strcmp(getenv("QW35_PREFILL"), "2") == 0;
+    // eval_tokens runs a token run as one batched pass, its DeltaNet recurrence
+    // as one run kernel per layer; QW35_PREFILL=1 keeps the batched pass with
+    // per-token DeltaNet steps, QW35_PREFILL=0 runs consecutive decode steps
+    {
+        const char *pf = getenv("QW35_PREFILL");
+        rt->batched_prefill = !(pf && strcmp(pf, "0") == 0);
+        rt->prefill_dn_run = rt->batched_prefill && !(pf && strcmp(pf, "1") == 0);
+    }
     const uint32_t R = rt->batched_prefill ? std::max<uint32_t>(S, std::min<uint32_t>(rt->prefill_chunk, 64)) : S;
     rt->rows = R;
     rt->d_in = dmalloc<int32_t>(4ull * R);
@@ -141,10 +148,21 @@ Runtime *create_runtime(std::shared_ptr<ModelStore> ms, uint32_t ctx, uint32_t v
     rt->attn_ws_bytes = attn_workspace_bytes((int)R, (int)kMaxCtx);
     rt->attn_ws = dmalloc<uint8_t>(rt->attn_ws_bytes);
 
-    // scratch of the batched tensor-core matvec, reserved before any graph capture
-    // (a prefill run of R rows runs the head on its last row only)
-    if (R >= (uint32_t)kDqMinBatch) ck(dq_reserve((int)R, 12288, F), "reserve matvec scratch");
-    if (S >= (uint32_t)kDqMinBatch) ck(dq_reserve((int)S, 12288, std::max<uint32_t>(vocab, F)), "reserve matvec scratch");
+    // scratch of the batched tensor-core matvec, owned by this runtime: its
+    // graphs capture the address, so it is sized here for the largest matvec
+    // a step can run and freed only with the runtime (a prefill run of R rows
+    // runs the head on its last row only)
+    {
+        const uint32_t kmax = std::max<uint32_t>(H, F);
+        size_t need = 0;
+        if (R >= (uint32_t)kDqMinBatch) need = std::max(need, dq_scratch_bytes((int)std::min<uint32_t>(R, 64), kmax, std::max(F, rt->proj_stride)));
+        if (S >= (uint32_t)kDqMinBatch)
+            need = std::max(need, dq_scratch_bytes((int)std::min<uint32_t>(S, 64), kmax, std::max({vocab, F, rt->proj_stride})));
+        if (need) {
+            rt->dq_scratch = dmalloc<uint8_t>(need);
+            rt->dq_scratch_bytes = need;
+        }
+    }
 
     // RoPE ladder freq[i] = base^(-2i/n_rot) in fp32 (Qw35MetalRuntime.m:772-795)
     float freq[32];

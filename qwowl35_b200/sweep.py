@@ -1,6 +1,8 @@
 """Quantized matvec shape sweep (the reference benchmark's matvec sweep config).
 
-    python -m qwowl35_b200.sweep [--codecs gf4,q8_0,q4_k,q5_k,q6_k] [--batches 1,8,32] [--out FILE.md]
+    python -m qwowl35_b200.sweep [--codecs gf4,q8_0,q4_k,q5_k,q6_k] [--batches 1,8,32] [--shapes 12288x4096]
+                                 [--out FILE.md]
+    python -m qwowl35_b200.sweep --case matvec_gf4_b1      # one ncu workload
 
 For every codec x shape x batch: y[B][rows] = W x^T through the public ops API
 (``ops.matvec``; 1-2 rows run the CUDA-core kernels, 3-64 rows the tcgen05
@@ -79,19 +81,105 @@ def point(name: str, t: int, rows: int, k: int, batches, gen, dev, peak: float) 
     return out
 
 
+# ---- named single-kernel workloads for ncu ---------------------------------
+# ``python -m qwowl35_b200.sweep --case NAME`` runs the call the decode step makes
+# for one kernel class once per rotating weight copy (the copies exceed the
+# 126 MB L2, so a launch after the first two streams its weights from HBM);
+# e.g. capture the third launch with ``ncu -k regex:dq_kernel -s 2 -c 1``.
+
+B, H, F = 32, 4096, 12288
+
+
+_GEN = {}
+
+
+def _weight(type_id: int, rows: int, k: int, device) -> torch.Tensor:
+    """Random weight with the synthetic model's code and scale distributions."""
+    g = _GEN.setdefault(str(device), synth._Gen(7, device))
+    return ops.repack(type_id, synth.gen_tensor(g, type_id, k, rows, "weight"), rows, k)
+
+
+def gateup_gf4_b32(device) -> None:
+    """FFN gate/up pair (GF4 2 x 12288 x 4096, batch 32): one dq_kernel launch each."""
+    ws = [(_weight(ops.GF4, F, H, device), _weight(ops.GF4, F, H, device)) for _ in range(4)]
+    x = torch.randn(B, H, device=device)
+    for wg, wu in ws:
+        ops.gate_up_swiglu(ops.GF4, wg, wu, x, F, H)
+
+
+def matvec_q8_0_b32(device) -> None:
+    """DeltaNet input projection (Q8_0 12352 x 4096, batch 32)."""
+    ws = [_weight(ops.Q8_0, 12352, H, device) for _ in range(4)]
+    x = torch.randn(B, H, device=device)
+    y = torch.empty(B, 12352, device=device)
+    for w in ws:
+        ops.matvec(ops.Q8_0, w, x, 12352, H, y=y)
+
+
+def gqa_b8_ctx4096(device) -> None:
+    """GQA split-K decode (one attention layer) at batch 8, 4096 positions each,
+    over 3 rotating KV pools (3 x 134 MB): the per-CTA work of the batch-32 step
+    with a quarter of the grid (small enough for a full ncu capture)."""
+    plane = 4 * 256 * 256  # f16 elements of one K (or V) plane of a chunk
+    ctx, nch, B = 4096, 16, 8
+    pools, tables = [], []
+    for _ in range(3):
+        pool = torch.randn(B * nch * 2 * plane, device=device).to(torch.float16)
+        base = pool.data_ptr()
+        tables.append(torch.tensor([[base + (s * nch + c) * 2 * plane * 2 for c in range(nch)] for s in range(B)],
+                                   dtype=torch.int64, device=device))
+        pools.append(pool)
+    q, gate = torch.randn(B, 16, 256, device=device), torch.randn(B, 16, 256, device=device)
+    lens = torch.full((B,), ctx, dtype=torch.int32, device=device)
+    ws = ops.gqa_workspace(B, ctx, device)
+    out = torch.empty(B, 4096, device=device)
+    for t in tables:
+        ops.gqa_decode(q, gate, lens, ctx, t, 0, plane * 2, ws=ws, out=out)
+
+
+def gateup_gf4_b1(device) -> None:
+    """FFN gate/up pair (GF4 2 x 12288 x 4096, batch 1): one mv_kernel launch each."""
+    ws = [(_weight(ops.GF4, F, H, device), _weight(ops.GF4, F, H, device)) for _ in range(4)]
+    x = torch.randn(1, H, device=device)
+    for wg, wu in ws:
+        ops.gate_up_swiglu(ops.GF4, wg, wu, x, F, H)
+
+
+def matvec_gf4_b1(device) -> None:
+    """FFN up-shaped GF4 matvec 12288 x 4096 at batch 1."""
+    ws = [_weight(ops.GF4, F, H, device) for _ in range(8)]
+    x = torch.randn(1, H, device=device).to(torch.float16)
+    y = torch.empty(1, F, device=device)
+    for w in ws:
+        ops.matvec(ops.GF4, w, x, F, H, y=y)
+
+
+CASES = {"gateup_gf4_b32": gateup_gf4_b32, "gateup_gf4_b1": gateup_gf4_b1, "matvec_gf4_b1": matvec_gf4_b1,
+         "matvec_q8_0_b32": matvec_q8_0_b32, "gqa_b8_ctx4096": gqa_b8_ctx4096}
+
+
+
 def main(argv: list[str]) -> int:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default="", help="run one named ncu workload (" + ", ".join(CASES) + ") and exit")
+    ap.add_argument("--shapes", default="", help="rowsxK list, e.g. 12288x4096 (default: all five)")
     ap.add_argument("--codecs", default="gf4,q8_0,q4_k,q5_k,q6_k")
     ap.add_argument("--batches", default="1,8,32")
     ap.add_argument("--out", default="")
     a = ap.parse_args(argv)
     dev = torch.device("cuda")
+    if a.case:
+        CASES[a.case](dev)
+        torch.cuda.synchronize()
+        print("done")
+        return 0
+    shapes = [tuple(int(v) for v in sh.split("x")) for sh in a.shapes.split(",")] if a.shapes else SHAPES
     peak, kind = hbm_peak()
     gen = synth._Gen(11, dev)
     batches = [int(b) for b in a.batches.split(",")]
     rows_out = []
     for name in a.codecs.split(","):
-        for rows, k in SHAPES:
+        for rows, k in shapes:
             for r in point(name, CODECS[name], rows, k, batches, gen, dev, peak):
                 rows_out.append(r)
                 print(f"{name:5s} {k:6d}->{rows:<6d} B={r['batch']:2d}: {r['us']:9.2f} us  {r['gbs']:7.1f} GB/s  "

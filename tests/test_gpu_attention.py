@@ -112,9 +112,6 @@ def test_kv_chunk_address_math():
 
 
 # ---- q8_0 KV cache (kv_cache_type 1, qw35_attention.metal:425-793) -----------------
-# The q8_0 kernels are enabled by QW35_KV_Q8=1 until they have run on a B200.
-KVQ8 = pytest.mark.skipif(not __import__("os").environ.get("QW35_KV_Q8"),
-                          reason="q8_0 KV kernels not yet enabled (QW35_KV_Q8=1)")
 ROWQ8 = 8 * 34
 PLANEQ8 = 4 * 256 * ROWQ8  # bytes of one K (or V) q8_0 plane in a chunk
 
@@ -153,7 +150,6 @@ def gather_kv_q8(host, block_ids, L, layer, per_chunk):
     return out
 
 
-@KVQ8
 @pytest.mark.parametrize("lens,window,sink", [([1], 0, 0), ([300], 0, 0), ([1025, 7, 3000], 0, 0),
                                               ([4096, 2048], 512, 4)])
 def test_gqa_decode_q8_0_matches_oracle(lens, window, sink):
@@ -177,7 +173,6 @@ def test_gqa_decode_q8_0_matches_oracle(lens, window, sink):
         assert relerr(out[s].reshape(16, 256), ref) < TOL
 
 
-@KVQ8
 def test_preprocess_q8_0_quantises_like_the_reference():
     rng = np.random.default_rng(8)
     lens = [600, 257]

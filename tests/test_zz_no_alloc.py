@@ -78,3 +78,30 @@ def test_noalloc_rejects_sizes_beyond_its_static_scratch():
     ok = L.qw35_cuda_gqa_decode_noalloc(n, dummy.data_ptr(), None, dummy.data_ptr(), max_len, dummy.data_ptr(),
                                         1024, 0, 0, 0, 0, dummy.data_ptr(), None, err, 512)
     assert ok == 0 and b"static scratch" in err.value
+
+
+def test_noalloc_call_takes_no_device_memory():
+    """After one warm-up call, a further call leaves the device's free bytes unchanged."""
+    L = lib()
+    lens = [3000, 700]
+    pool, table = _kv(lens, 7)
+    lens_d = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    q = torch.randn(len(lens), 16, 256, device="cuda")
+    gate = torch.randn(len(lens), 16, 256, device="cuda")
+    out = torch.empty(len(lens), 4096, device="cuda")
+    err = C.create_string_buffer(512)
+    st = torch.cuda.current_stream().cuda_stream
+
+    def call():
+        assert L.qw35_cuda_gqa_decode_noalloc(len(lens), q.data_ptr(), gate.data_ptr(), lens_d.data_ptr(),
+                                              max(lens), table.data_ptr(), table.shape[1], 0, PLANE * 2, 0, 0,
+                                              out.data_ptr(), st, err, 512) == 1, err.value
+        torch.cuda.synchronize()
+
+    call()
+    free0, _ = torch.cuda.mem_get_info()
+    call()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert np.isfinite(out.cpu().numpy()).all()
+    del pool
