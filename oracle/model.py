@@ -57,6 +57,10 @@ class OracleModel:
                 self._cache[name] = Q.dequant(t, raw, r, k, gf4_exact=self.gf4_exact, tiled=self.tiled)
         return self._cache[name]
 
+    def mv(self, name: str, x: np.ndarray) -> np.ndarray:
+        """W[name] @ x for one activation row x (fp64)."""
+        return O.matvec(self.w(name), x[None])[0]
+
     def embed(self, token: int) -> np.ndarray:
         t, k, r, off, n = self.m.offsets["token_embd.weight"]
         rb = n // r
@@ -71,9 +75,9 @@ class OracleModel:
             p = f"blk.{il}."
             xn = O.rms_norm(x, self.w(p + "attn_norm.weight"), eps)
             if self._is_attn(il):
-                q_full = O.matvec(self.w(p + "attn_q.weight"), xn[None])[0]
-                kk = O.matvec(self.w(p + "attn_k.weight"), xn[None])[0]
-                vv = O.matvec(self.w(p + "attn_v.weight"), xn[None])[0]
+                q_full = self.mv(p + "attn_q.weight", xn)
+                kk = self.mv(p + "attn_k.weight", xn)
+                vv = self.mv(p + "attn_v.weight", xn)
                 if self.kv_q8:
                     q, gate, kb, vb = O.attn_preprocess_q8_0(q_full, kk, vv, self.w(p + "attn_q_norm.weight"),
                                                              self.w(p + "attn_k_norm.weight"), pos, self.freq, eps)
@@ -87,18 +91,18 @@ class OracleModel:
                 K = np.stack(self.k[il])
                 V = np.stack(self.v[il])
                 core = O.gqa_decode(q, gate, K, V, self.window, self.sink).reshape(-1)
-                x = x + O.matvec(self.w(p + "attn_output.weight"), core[None])[0]
+                x = x + self.mv(p + "attn_output.weight", core)
             else:
-                qkv = O.matvec(self.w(p + "attn_qkv.weight"), xn[None])[0]
-                z = O.matvec(self.w(p + "attn_gate.weight"), xn[None])[0]
-                beta = O.matvec(self.w(p + "ssm_beta.weight"), xn[None])[0]
-                alpha = O.matvec(self.w(p + "ssm_alpha.weight"), xn[None])[0]
+                qkv = self.mv(p + "attn_qkv.weight", xn)
+                z = self.mv(p + "attn_gate.weight", xn)
+                beta = self.mv(p + "ssm_beta.weight", xn)
+                alpha = self.mv(p + "ssm_alpha.weight", xn)
                 out, self.conv[il], self.ssm[il] = O.deltanet_step(
                     qkv, self.w(p + "ssm_conv1d.weight"), self.conv[il], beta, alpha, self.w(p + "ssm_dt.bias"),
                     self.w(p + "ssm_a"), self.ssm[il], z, self.w(p + "ssm_norm.weight"), eps)
-                x = x + O.matvec(self.w(p + "ssm_out.weight"), out[None])[0]
+                x = x + self.mv(p + "ssm_out.weight", out)
             xn = O.rms_norm(x, self.w(p + "post_attention_norm.weight"), eps)
-            h = O.gate_up_swiglu(self.w(p + "ffn_gate.weight"), self.w(p + "ffn_up.weight"), xn[None])[0]
-            x = x + O.matvec(self.w(p + "ffn_down.weight"), h[None])[0]
+            h = O.silu(self.mv(p + "ffn_gate.weight", xn)) * self.mv(p + "ffn_up.weight", xn)
+            x = x + self.mv(p + "ffn_down.weight", h)
         xn = O.rms_norm(x, self.w("output_norm.weight"), eps)
-        return O.matvec(self.w("output.weight"), xn[None])[0]
+        return self.mv("output.weight", xn)

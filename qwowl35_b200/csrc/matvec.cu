@@ -82,81 +82,40 @@ __device__ __forceinline__ void load_x32(float *dst, const XT *src) {
     }
 }
 
-// Turn the lane's 32 activations into the codec's scaled form + constants.
+// K-quants: turn the lane's 32 activations into the scaled form + constants
+// (GF4 and Q8_0 prepare theirs in prep_x_gf4 / as pairs).
 template <int CODEC, bool EXACT>
 __device__ __forceinline__ void prep_x(float *xs, float *cst) {
-    if constexpr (CODEC == QW35_GF4_TYPE) {
-#pragma unroll
-        for (int wd = 0; wd < 4; ++wd) {
-            float s = 0.0f, sx = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float x = xs[8 * wd + j];
-                s += x;
-                sx += x * gf4_xscale(j);
-            }
-            const float x4 = xs[8 * wd + 4];
-            // everything carries the -0.25 of the GF4 level spacing (exact)
-            cst[wd] = -0.25f * (sx + 4.0f * s + (EXACT ? 0.0f : 0.5f * x4));
-            cst[4 + wd] = -0.125f * x4;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) xs[8 * wd + j] *= -0.25f * gf4_xscale(j);
-        }
-    } else if constexpr (CODEC == QW35_Q8_0_TYPE) {
-        cst[0] = 0.0f;
-    } else if constexpr (CODEC == QW35_Q6_K_TYPE) {
-        // per 16-weight sub-block: low and high passes each add sum(xs); the
-        // code offset of -32 adds 32 * sum(x)
+    if constexpr (CODEC == QW35_Q6_K_TYPE) {
+        // per 16-weight sub-block: the code offset of -32 subtracts 32 * sum(x)
+        // (scaled like the products, see q4_word_den)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-            float s = 0.0f, sx = 0.0f;
+            float s = 0.0f;
 #pragma unroll
             for (int i = 16 * h; i < 16 * h + 16; ++i) {
                 s += xs[i];
-                xs[i] *= q4_xscale(i & 7);
-                sx += xs[i];
+                xs[i] *= q4_den_scale(i & 7);
             }
-            cst[h] = 17.0f * sx + 32.0f * s;
+            cst[h] = 32.0f * s * (1.0f / kKqUnscale);
         }
     } else {
-        float s = 0.0f, sx = 0.0f;
+        float s = 0.0f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
             s += xs[i];
-            xs[i] *= q4_xscale(i & 7);
-            sx += xs[i];
+            xs[i] *= q4_den_scale(i & 7);
         }
-        cst[0] = CODEC == QW35_Q5_K_TYPE ? 17.0f * sx : sx;  // Q5_K: low + 16 x high pass
-        cst[1] = s;
+        cst[0] = 0.0f;
+        cst[1] = s * (1.0f / kKqUnscale);  // the dmin * m term
     }
 }
 
-// Dot of the lane's chunk of one row (weights in shared memory) with x.
+// K-quants: dot of the lane's chunk of one row (weights in shared memory) with x.
 template <int CODEC, bool EXACT>
 __device__ __forceinline__ float chunk_fast(const uint8_t *codes, const uint8_t *scales, int c, const float *xs,
                                             const float *cst, int K) {
-    if constexpr (CODEC == QW35_GF4_TYPE) {
-        const uint4 w = *reinterpret_cast<const uint4 *>(codes + c * 16);
-        float r = gf4_word_fast<EXACT>(w.x, xs + 0, cst[0], cst[4], 0.0f);
-        r = gf4_word_fast<EXACT>(w.y, xs + 8, cst[1], cst[5], r);
-        r = gf4_word_fast<EXACT>(w.z, xs + 16, cst[2], cst[6], r);
-        r = gf4_word_fast<EXACT>(w.w, xs + 24, cst[3], cst[7], r);
-        return r;
-    } else if constexpr (CODEC == QW35_Q8_0_TYPE) {
-        const uint4 a = *reinterpret_cast<const uint4 *>(codes + c * 32);
-        const uint4 b = *reinterpret_cast<const uint4 *>(codes + c * 32 + 16);
-        const unsigned short sb = *reinterpret_cast<const unsigned short *>(scales + c * 2);
-        float acc = 0.0f;
-        acc = q8_word_fast(a.x, xs + 0, acc);
-        acc = q8_word_fast(a.y, xs + 4, acc);
-        acc = q8_word_fast(a.z, xs + 8, acc);
-        acc = q8_word_fast(a.w, xs + 12, acc);
-        acc = q8_word_fast(b.x, xs + 16, acc);
-        acc = q8_word_fast(b.y, xs + 20, acc);
-        acc = q8_word_fast(b.z, xs + 24, acc);
-        acc = q8_word_fast(b.w, xs + 28, acc);
-        return acc * __half2float(__ushort_as_half(sb));
-    } else if constexpr (CODEC == QW35_Q5_K_TYPE) {
+    if constexpr (CODEC == QW35_Q5_K_TYPE) {
         // chunk c is sub-block c & 7 of block c >> 3; the high bits of word w
         // sit at bit w of each nibble slot of one uint32
         const uint4 w = *reinterpret_cast<const uint4 *>(codes + c * 16);
@@ -165,16 +124,14 @@ __device__ __forceinline__ float chunk_fast(const uint8_t *codes, const uint8_t 
         float dl, ml;
         q4k_scale_min(h, c & 7, dl, ml);
         constexpr uint32_t M1 = 0x11111111u;
-        float acc = -cst[0], hacc = 0.0f;
-        acc = q4_word_fast(w.x, xs + 0, acc);
-        acc = q4_word_fast(w.y, xs + 8, acc);
-        acc = q4_word_fast(w.z, xs + 16, acc);
-        acc = q4_word_fast(w.w, xs + 24, acc);
-        hacc = q4_word_fast(hb & M1, xs + 0, hacc);
-        hacc = q4_word_fast((hb >> 1) & M1, xs + 8, hacc);
-        hacc = q4_word_fast((hb >> 2) & M1, xs + 16, hacc);
-        hacc = q4_word_fast((hb >> 3) & M1, xs + 24, hacc);
-        return dl * fmaf(16.0f, hacc, acc) - ml * cst[1];
+        float acc = q4_word_den(w.x, xs + 0, 0.0f), hacc = q4_word_den(hb & M1, xs + 0, 0.0f);
+        acc = q4_word_den(w.y, xs + 8, acc);
+        hacc = q4_word_den((hb >> 1) & M1, xs + 8, hacc);
+        acc = q4_word_den(w.z, xs + 16, acc);
+        hacc = q4_word_den((hb >> 2) & M1, xs + 16, hacc);
+        acc = q4_word_den(w.w, xs + 24, acc);
+        hacc = q4_word_den((hb >> 3) & M1, xs + 24, hacc);
+        return (dl * fmaf(16.0f, hacc, acc) - ml * cst[1]) * kKqUnscale;
     } else if constexpr (CODEC == QW35_Q6_K_TYPE) {
         // chunk c = sub-blocks 2c, 2c+1; high pairs of 16 weights per uint32
         const uint4 w = *reinterpret_cast<const uint4 *>(codes + c * 16);
@@ -182,35 +139,71 @@ __device__ __forceinline__ float chunk_fast(const uint8_t *codes, const uint8_t 
         const uint32_t sc2 = *reinterpret_cast<const unsigned short *>(scales + c * 2);
         const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(scales + K / 16 + (c >> 3) * 2)));
         constexpr uint32_t M2 = 0x33333333u;
-        float a0 = -cst[0], a1 = -cst[1], h0 = 0.0f, h1 = 0.0f;
-        a0 = q4_word_fast(w.x, xs + 0, a0);
-        a0 = q4_word_fast(w.y, xs + 8, a0);
-        a1 = q4_word_fast(w.z, xs + 16, a1);
-        a1 = q4_word_fast(w.w, xs + 24, a1);
-        h0 = q4_word_fast(hb.x & M2, xs + 0, h0);
-        h0 = q4_word_fast((hb.x >> 2) & M2, xs + 8, h0);
-        h1 = q4_word_fast(hb.y & M2, xs + 16, h1);
-        h1 = q4_word_fast((hb.y >> 2) & M2, xs + 24, h1);
+        float a0 = q4_word_den(w.x, xs + 0, -cst[0]), a1 = q4_word_den(w.z, xs + 16, -cst[1]);
+        float h0 = q4_word_den(hb.x & M2, xs + 0, 0.0f), h1 = q4_word_den(hb.y & M2, xs + 16, 0.0f);
+        a0 = q4_word_den(w.y, xs + 8, a0);
+        a1 = q4_word_den(w.w, xs + 24, a1);
+        h0 = q4_word_den((hb.x >> 2) & M2, xs + 8, h0);
+        h1 = q4_word_den((hb.y >> 2) & M2, xs + 24, h1);
         const float s0 = (float)(int8_t)(sc2 & 0xffu), s1 = (float)(int8_t)(sc2 >> 8);
-        return d * fmaf(s0, fmaf(16.0f, h0, a0), s1 * fmaf(16.0f, h1, a1));
+        return d * fmaf(s0, fmaf(16.0f, h0, a0), s1 * fmaf(16.0f, h1, a1)) * kKqUnscale;
     } else {
         const uint4 w = *reinterpret_cast<const uint4 *>(codes + c * 16);
         const uint4 h = *reinterpret_cast<const uint4 *>(scales + (c >> 3) * 16);
         float dl, ml;
         q4k_scale_min(h, c & 7, dl, ml);
-        float acc = -cst[0];
-        acc = q4_word_fast(w.x, xs + 0, acc);
-        acc = q4_word_fast(w.y, xs + 8, acc);
-        acc = q4_word_fast(w.z, xs + 16, acc);
-        acc = q4_word_fast(w.w, xs + 24, acc);
-        return dl * acc - ml * cst[1];
+        const float a = q4_word_den(w.y, xs + 8, q4_word_den(w.x, xs + 0, 0.0f));
+        const float c = q4_word_den(w.w, xs + 24, q4_word_den(w.z, xs + 16, 0.0f));
+        return (dl * (a + c) - ml * cst[1]) * kKqUnscale;
     }
 }
+
+// Sum each of NV per-lane values over the warp with a butterfly reduce-scatter:
+// the first log2(NV) exchange steps halve the values a lane keeps (one shuffle
+// per kept pair instead of one per value and step), the rest are plain
+// butterfly steps.  Returns the total of value mv_scatter_index<NV>(lane).
+template <int NV>
+__device__ __forceinline__ float warp_reduce_scatter(float *v, int lane) {
+#pragma unroll
+    for (int st = 0; (1 << st) < NV; ++st) {
+        const int o = 16 >> st, n = NV >> (st + 1);
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int j = 0; j < n; ++j) {
+            const float send = up ? v[j] : v[j + n];
+            const float keep = up ? v[j + n] : v[j];
+            v[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    float t = v[0];
+#pragma unroll
+    for (int o = 16 / NV; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    return t;
+}
+
+template <int NV>
+__device__ __forceinline__ int mv_scatter_index(int lane) {
+    int idx = 0;
+#pragma unroll
+    for (int st = 0; (1 << st) < NV; ++st)
+        if (lane & (16 >> st)) idx += NV >> (st + 1);
+    return idx;
+}
+
+// GF4 / Q8_0 rows per consumer warp per stage (the stage holds G = rows * RS rows)
+template <int CODEC, int MODE> constexpr int rows_per_warp() {
+    return CODEC == QW35_GF4_TYPE ? (MODE == 2 ? 2 : 4) : (MODE == 2 ? 1 : 2);
+}
+// Consumer warps per CTA: two activation rows keep twice the registers resident
+#ifndef MV_WARPS_B1
+#define MV_WARPS_B1 12
+#endif
+template <int B> constexpr int mv_max_warps() { return B == 1 ? MV_WARPS_B1 : 12; }
 
 // Shared-memory carve-up (dynamic): [NM][kStages][stage_bytes] weights |
 // [2][G][B][NM][KW] partials | 64 floats scratch | 2*kStages mbarriers | abort.
 template <int CODEC, int B, int MODE, bool EXACT, typename XT>
-__global__ void __launch_bounds__(544, 1) mv_kernel(MvParams p) {
+__global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, 1) mv_kernel(MvParams p) {
     constexpr int NM = MODE == MV_SWIGLU ? 2 : 1;
     constexpr int NC = Codec<CODEC>::NC;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -326,8 +319,20 @@ __global__ void __launch_bounds__(544, 1) mv_kernel(MvParams p) {
             }
         }
     }
+    // GF4: activations as scaled pairs for the packed exact-level decode
+    float2 xp[B][16];
+    float xa[B][4], xj[B][4];
+    if constexpr (CODEC == QW35_GF4_TYPE) {
+        prep_x_gf4<B>(xs, xp, xa, xj);
+    } else if constexpr (CODEC == QW35_Q8_0_TYPE) {
 #pragma unroll
-    for (int b = 0; b < B; ++b) prep_x<CODEC, EXACT>(xs[b], cst[b]);
+        for (int b = 0; b < B; ++b)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) xp[b][i] = make_float2(xs[b][2 * i], xs[b][2 * i + 1]);
+    } else {
+#pragma unroll
+        for (int b = 0; b < B; ++b) prep_x<CODEC, EXACT>(xs[b], cst[b]);
+    }
 
     float best_v = -INFINITY;
     uint32_t best_i = 0xffffffffu;
@@ -343,6 +348,52 @@ __global__ void __launch_bounds__(544, 1) mv_kernel(MvParams p) {
         const int row0 = r0 + g * G;
         const int nr = min(G, r1 - row0);
         float *pg = part + (g & 1) * G * B * NM * KW;
+        if constexpr (CODEC == QW35_GF4_TYPE || CODEC == QW35_Q8_0_TYPE) {
+            // this warp's rows of the stage: rs + j * RS, all in flight at once;
+            // rows past nr run on stale stage bytes and are never stored
+            constexpr int NRW = rows_per_warp<CODEC, MODE>();
+            constexpr int NV = NRW * NM * B;
+            float v[NV];
+            const int cc = active ? c : 0;
+#pragma unroll
+            for (int j = 0; j < NRW; ++j) {
+                const int i = rs + j * RS;
+#pragma unroll
+                for (int m = 0; m < NM; ++m) {
+                    const uint8_t *st = wbuf + ((size_t)m * kStages + s) * SB;
+                    if constexpr (CODEC == QW35_GF4_TYPE) {
+                        const uint4 wv = *reinterpret_cast<const uint4 *>(st + (size_t)i * p.code_row + cc * 16);
+                        float2 r2[B];
+#pragma unroll
+                        for (int b = 0; b < B; ++b) r2[b] = make_float2(0.0f, 0.0f);
+                        gf4_word_f2<EXACT, B>(wv.x, 0, xp, xa, xj, r2);
+                        gf4_word_f2<EXACT, B>(wv.y, 1, xp, xa, xj, r2);
+                        gf4_word_f2<EXACT, B>(wv.z, 2, xp, xa, xj, r2);
+                        gf4_word_f2<EXACT, B>(wv.w, 3, xp, xa, xj, r2);
+#pragma unroll
+                        for (int b = 0; b < B; ++b) v[(j * NM + m) * B + b] = active ? (r2[b].x + r2[b].y) * kGf4Unscale : 0.0f;
+                    } else {
+                        const uint8_t *codes = st + (size_t)i * p.code_row + cc * 32;
+                        const uint4 a0 = *reinterpret_cast<const uint4 *>(codes);
+                        const uint4 a1 = *reinterpret_cast<const uint4 *>(codes + 16);
+                        const unsigned short sb = *reinterpret_cast<const unsigned short *>(
+                            st + (size_t)G * p.code_row + (size_t)i * p.scale_row + cc * 2);
+                        float r[B];
+#pragma unroll
+                        for (int b = 0; b < B; ++b) r[b] = 0.0f;
+                        q8_block_f2<B>(a0, a1, __half2float(__ushort_as_half(sb)), xp, r);
+#pragma unroll
+                        for (int b = 0; b < B; ++b) v[(j * NM + m) * B + b] = active ? r[b] : 0.0f;
+                    }
+                }
+            }
+            const float tot = warp_reduce_scatter<NV>(v, lane);
+            if ((lane & (32 / NV - 1)) == 0) {
+                const int idx = mv_scatter_index<NV>(lane);
+                const int b = idx % B, m = (idx / B) % NM, j = idx / (B * NM);
+                pg[(((rs + j * RS) * B + b) * NM + m) * KW + kw] = tot;
+            }
+        } else
         for (int i = rs; i < G; i += RS) {
             float acc[NM][B];
 #pragma unroll
@@ -466,22 +517,17 @@ static MvGeom mv_geometry(int rows, int K, const void *kern) {
     g.kw = (nchunk + 31) / 32;
     codec_rows(CODEC, K, g.code_row, g.scale_row);
     const uint32_t rb = g.code_row + g.scale_row;
-    // QW35_MV_KQ_WIDE=1 gives the K-quants the same geometry (a tuning switch)
-    static const bool kq_wide = getenv("QW35_MV_KQ_WIDE") != nullptr;
-    const bool kquant = CODEC == QW35_Q4_K_TYPE || CODEC == QW35_Q5_K_TYPE || CODEC == QW35_Q6_K_TYPE;
-    if (CODEC == QW35_GF4_TYPE || (kquant && kq_wide)) {
-        // GF4 decode is latency-heavy: ~16 consumer warps keep rows in flight
-        // (measured: gate/up pair 31.5 -> 28.2 us at B = 1)
-        g.rs = g.kw >= 16 ? 1 : 16 / g.kw;
-        g.G = (int)(32 * 1024 / NM / rb);  // <= 32 KB of weights per stage over all matrices
+    if (CODEC == QW35_GF4_TYPE || CODEC == QW35_Q8_0_TYPE) {
+        // up to mv_max_warps consumer warps, each with gf4_rows_per_warp rows of a stage in flight
+        constexpr int CW = mv_max_warps<B>();
+        g.rs = g.kw >= CW ? 1 : CW / g.kw;
+        g.G = rows_per_warp<CODEC, MODE>() * g.rs;
     } else {
         g.rs = g.kw >= 8 ? 1 : 8 / g.kw;
         g.G = (int)(20 * 1024 / rb);
     }
     g.threads = (g.kw * g.rs + 1) * 32;
-    g.G = g.G < 1 ? 1 : (g.G > 16 ? 16 : g.G);
-    if ((CODEC == QW35_GF4_TYPE || (kquant && kq_wide)) && g.G >= g.rs)
-        g.G -= g.G % g.rs;  // whole rounds of the row slots
+    if (CODEC != QW35_GF4_TYPE && CODEC != QW35_Q8_0_TYPE) g.G = g.G < 1 ? 1 : (g.G > 16 ? 16 : g.G);
     g.stage_bytes = ((uint32_t)g.G * rb + 127u) & ~127u;
     g.smem = (size_t)NM * kStages * g.stage_bytes + (size_t)2 * g.G * B * NM * g.kw * 4 + 64 * 4 +
              2 * kStages * 8 + 16;

@@ -44,22 +44,10 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Default: plain polling (measured slightly faster than a suspend-time hint for
-// the matvec pipelines); QW35_SUSPEND_NS > 0 adds the hint (ns) to try_wait.
-#ifndef QW35_SUSPEND_NS
-#define QW35_SUSPEND_NS 0
-#endif
+// Plain polling (measured slightly faster than a suspend-time hint for the
+// matvec pipelines).
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
-#if QW35_SUSPEND_NS > 0
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "n"(QW35_SUSPEND_NS)
-        : "memory");
-#else
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
@@ -67,7 +55,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "=r"(ok)
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
-#endif
     return ok != 0;
 }
 

@@ -110,72 +110,156 @@ __device__ __forceinline__ float q4_word_dot(uint32_t w, const float *x) {
 }  // namespace qw35
 
 // ---------------------------------------------------------------------------
-// Fast decode for the streaming matvec.  Codes are turned into floats with one
-// LOP3/PRMT each by OR-ing them into the mantissa of 1.0f:
-//     f = 1 + q * 2^(p - 23)        (code q placed at mantissa bit p)
-// so f * xs = xs + q * x when xs = x * 2^(23 - p) (an exact power-of-two
-// scaling of the register-resident activation).  The xs terms of a word or
-// block are summed once per lane (the activation row never changes during a
-// launch) and subtracted once per word/block; p is chosen high in the
-// mantissa (>= 8) so the constant part stays within 2^15 of the code part and
-// fp32 rounding stays ~1e-6 relative.
+// Decode for the streaming matvec (batch 1-2).  Codes become exact floats
+// without conversion instructions: a code masked out of its word in place (or
+// after one shift) and read as a float is a denormal, q * 2^(p - 149), exact
+// for any bit position p < 23.  The register-resident activations carry the
+// matching power of two, so each product q * x (times a common 2^-M) is exact
+// and the dot is an fp32 sum of exact products; code offsets (GF4's -4, the
+// Q8_0 bias, K-quant minima) enter through per-lane sums of x.  FMA with
+// denormal operands runs at full rate and is exact under round-to-nearest
+// (no flush-to-zero: the library is not built with fast math).
 // ---------------------------------------------------------------------------
 namespace qw35 {
 
-// GF4: code j of the word is moved to mantissa bit 17 (j even) or 20 (j odd)
-// by one of four shifts of the word; xs_j = x_j * (j even ? 64 : 8).
-// cw = sum_j xs_j + 4 * sum_j x_j (+ x_4 / 2 in metal mode); xh = x_4 / 2.
-template <bool EXACT>
-// xs, cw and xh arrive pre-multiplied by -0.25 (the level spacing); the
-// word's e5m2 scale is applied with one FMA into the running row sum r.
-__device__ __forceinline__ float gf4_word_fast(uint32_t w, const float *xs, float cw, float xh, float r) {
-    const uint32_t s0 = w << 9, s1 = w << 3, s2 = w >> 3, s3 = w >> 9;
-    constexpr uint32_t M17 = 7u << 17, M20 = 7u << 20;
-    constexpr uint32_t X17 = 0x3F800000u | (4u << 17), X20 = 0x3F800000u | (4u << 20);
-    float acc = -cw;
-    acc = fmaf(__uint_as_float((s0 & M17) ^ X17), xs[0], acc);
-    acc = fmaf(__uint_as_float((s0 & M20) ^ X20), xs[1], acc);
-    acc = fmaf(__uint_as_float((s1 & M17) ^ X17), xs[2], acc);
-    acc = fmaf(__uint_as_float((s1 & M20) ^ X20), xs[3], acc);
-    acc = fmaf(__uint_as_float((s2 & M17) ^ X17), xs[4], acc);
-    acc = fmaf(__uint_as_float((s2 & M20) ^ X20), xs[5], acc);
-    acc = fmaf(__uint_as_float((s3 & M17) ^ X17), xs[6], acc);
-    acc = fmaf(__uint_as_float((s3 & M20) ^ X20), xs[7], acc);
-    // metal element-4 junk: bits 11..19 as 1 + junk*2^-12, times x_4/2
-    if (!EXACT) acc = fmaf(__uint_as_float((w & 0x000FF800u) | 0x3F800000u), xh, acc);
-    return fmaf(acc, e5m2_to_float(w), r);
+// Packed fp32 FMA (two lanes per instruction, sm_100): d = a * b + c.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
 }
 
-__device__ __forceinline__ float gf4_xscale(int j) { return (j & 1) ? 8.0f : 64.0f; }
-
-// Q8_0: the 1+u*2^-15 form would put the constant 2^15/|q| times above the
-// code term (~1e-4 relative error), so each byte (biased to u = q + 128) is
-// made exact instead: PRMT into the mantissa of 2^23, one FADD of -(2^23+128)
-// gives q as a float, one FMA.
-__device__ __forceinline__ float q8_word_fast(uint32_t wd, const float *x, float acc) {
-    const uint32_t wx = wd ^ 0x80808080u;
-    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u)) - 8388736.0f, x[0], acc);
-    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7541u)) - 8388736.0f, x[1], acc);
-    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7542u)) - 8388736.0f, x[2], acc);
-    acc = fmaf(__uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7543u)) - 8388736.0f, x[3], acc);
-    return acc;
+// Packed fp32 add (two lanes per instruction, sm_100): d = a + b.
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
 }
 
-// Q4_K (element-contiguous nibbles): nibble n goes to mantissa bit 15 (n even)
-// or 19 (n odd); xs_n = x_n * (n even ? 2^8 : 2^4).
-__device__ __forceinline__ float q4_word_fast(uint32_t w, const float *xs, float acc) {
-    const uint32_t s0 = w << 15, s1 = w << 7, s2 = w >> 1, s3 = w >> 9;
-    constexpr uint32_t M12 = 0xFu << 15, M16 = 0xFu << 19, E = 0x3F800000u;
-    acc = fmaf(__uint_as_float((s0 & M12) | E), xs[0], acc);
-    acc = fmaf(__uint_as_float((s0 & M16) | E), xs[1], acc);
-    acc = fmaf(__uint_as_float((s1 & M12) | E), xs[2], acc);
-    acc = fmaf(__uint_as_float((s1 & M16) | E), xs[3], acc);
-    acc = fmaf(__uint_as_float((s2 & M12) | E), xs[4], acc);
-    acc = fmaf(__uint_as_float((s2 & M16) | E), xs[5], acc);
-    acc = fmaf(__uint_as_float((s3 & M12) | E), xs[6], acc);
-    acc = fmaf(__uint_as_float((s3 & M16) | E), xs[7], acc);
-    return acc;
+// One GF4 word against B activation rows, two codes per packed FMA.
+// Codes as denormals: after one XOR that undoes the stored ^4 of every code
+// (v holds q_raw), code j masked out in place, (v & 7 << p) read as a float,
+// is exactly q_raw * 2^(p - 149).  Codes 0..4 sit at p = 8 + 3j already;
+// codes 5..7 reach p = 11, 14, 17 with one shift.  The activations carry
+// x * -0.25 * 2^(149 - p - kGf4M) (prep_x_gf4), so every product is
+// q_raw * x * -0.25 * 2^-kGf4M, exact, and the word's -4 offset enters once as
+// acc0 = sum(x) * 2^-kGf4M.  The Metal element-4 junk (bits 11..19 of w) is
+// a denormal the same way.  The decode is shared by the B rows; the word's
+// e5m2 scale multiplies the word sum; the caller scales the row by 2^kGf4M.
+// No cancelling offsets: each row of the dot is an fp32 sum of exact products.
+constexpr int kGf4M = 30;
+constexpr float kGf4Unscale = 1073741824.0f;  // 2^kGf4M
+
+template <bool EXACT, int B>
+__device__ __forceinline__ void gf4_word_f2(uint32_t w, int wd, const float2 (*xp)[16], const float (*xa)[4],
+                                            const float (*xj)[4], float2 *r2) {
+    const uint32_t v = w ^ 0x92492400u;  // bit 2 of every code
+    const uint32_t u = v >> 12;          // codes 5, 6, 7 at bits 11, 14, 17
+    const float2 g0 = make_float2(__uint_as_float(v & (7u << 8)), __uint_as_float(v & (7u << 11)));
+    const float2 g1 = make_float2(__uint_as_float(v & (7u << 14)), __uint_as_float(v & (7u << 17)));
+    const float2 g2 = make_float2(__uint_as_float(v & (7u << 20)), __uint_as_float(u & (7u << 11)));
+    const float2 g3 = make_float2(__uint_as_float(u & (7u << 14)), __uint_as_float(u & (7u << 17)));
+    const float jf = __uint_as_float(w & 0x000FF800u);  // junk * 2^(11 - 149)
+    const uint32_t hs = __byte_perm(w, 0u, 0x0404u);    // {s, s} as half2 (e5m2 = high byte of a half)
+    const float2 sc = __half22float2(*reinterpret_cast<const __half2 *>(&hs));
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+        float2 acc = make_float2(xa[b][wd], EXACT ? 0.0f : jf * xj[b][wd]);
+        acc = ffma2(g0, xp[b][4 * wd + 0], acc);
+        acc = ffma2(g1, xp[b][4 * wd + 1], acc);
+        acc = ffma2(g2, xp[b][4 * wd + 2], acc);
+        acc = ffma2(g3, xp[b][4 * wd + 3], acc);
+        r2[b] = ffma2(acc, sc, r2[b]);
+    }
 }
-__device__ __forceinline__ float q4_xscale(int n) { return (n & 1) ? 16.0f : 256.0f; }
+
+// Activations of the lane's 32 columns (4 words) for gf4_word_f2.
+template <int B>
+__device__ __forceinline__ void prep_x_gf4(const float (*xs)[32], float2 (*xp)[16], float (*xa)[4],
+                                           float (*xj)[4]) {
+    // code j of a word sits at p = 8, 11, 14, 17, 20, 11, 14, 17 (see gf4_word_f2)
+    constexpr int P[8] = {8, 11, 14, 17, 20, 11, 14, 17};
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+#pragma unroll
+        for (int wd = 0; wd < 4; ++wd) {
+            float f[8], sum = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float x = xs[b][8 * wd + j];
+                sum += x;
+                f[j] = x * -0.25f * __int_as_float((127 + 149 - P[j] - kGf4M) << 23);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xp[b][4 * wd + i] = make_float2(f[2 * i], f[2 * i + 1]);
+            xa[b][wd] = sum * (1.0f / kGf4Unscale);
+            // junk weight s * -0.25 * 2^-13 over the denormal's 2^(11 - 149)
+            xj[b][wd] = xs[b][8 * wd + 4] * -0.25f * __int_as_float((127 + 149 - 11 - 13 - kGf4M) << 23);
+        }
+    }
+}
+
+// Q8_0: 32 codes of one block (two 16-byte pieces) against B activation rows.
+// Each byte (biased to q + 128) enters the mantissa of 2^23 by one PRMT, one
+// packed add per pair leaves q exactly, two per packed FMA; the block's f16
+// scale is applied to the block sum.  xp[b][i] = {x_2i, x_2i+1}.
+template <int B>
+__device__ __forceinline__ void q8_block_f2(uint4 a, uint4 c, float d, const float2 (*xp)[16], float *r) {
+    const uint32_t wds[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+    float2 acc[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) acc[b] = make_float2(0.0f, 0.0f);
+    const float2 off = make_float2(-8388736.0f, -8388736.0f);  // 2^23 + 128
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint32_t wx = wds[i] ^ 0x80808080u;
+        const float2 q01 = fadd2(make_float2(__uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7540u)),
+                                             __uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7541u))), off);
+        const float2 q23 = fadd2(make_float2(__uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7542u)),
+                                             __uint_as_float(__byte_perm(wx, 0x4B000000u, 0x7543u))), off);
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            acc[b] = ffma2(q01, xp[b][2 * i], acc[b]);
+            acc[b] = ffma2(q23, xp[b][2 * i + 1], acc[b]);
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) r[b] = fmaf(acc[b].x + acc[b].y, d, r[b]);
+}
+
+
+
+// K-quant nibbles as denormals: nibble k of a word (element-contiguous) masked
+// in place at bit 4k (k < 6), nibbles 6 and 7 after one shift at bits 12 and
+// 16; (w & 0xF << p) read as a float is exactly n * 2^(p - 149).  xs carries
+// x * 2^(149 - p - kKqM) (q4_den_scale), so every product is n * x * 2^-kKqM,
+// exact, with no offset to cancel.  The high code bits of Q5_K / Q6_K, stored
+// in nibble slots, decode the same way.
+constexpr int kKqM = 40;
+constexpr float kKqUnscale = 1099511627776.0f;  // 2^kKqM
+__device__ __forceinline__ float q4_den_scale(int k) {
+    constexpr int P[8] = {0, 4, 8, 12, 16, 20, 12, 16};
+    return __int_as_float((127 + 149 - P[k] - kKqM) << 23);
+}
+__device__ __forceinline__ float q4_word_den(uint32_t w, const float *xs, float acc) {
+    const uint32_t u = w >> 12;
+    float a = fmaf(__uint_as_float(w & 0xFu), xs[0], acc);
+    float c = __uint_as_float(w & 0xF0u) * xs[1];
+    a = fmaf(__uint_as_float(w & 0xF00u), xs[2], a);
+    c = fmaf(__uint_as_float(w & 0xF000u), xs[3], c);
+    a = fmaf(__uint_as_float(w & 0xF0000u), xs[4], a);
+    c = fmaf(__uint_as_float(w & 0xF00000u), xs[5], c);
+    a = fmaf(__uint_as_float(u & 0xF000u), xs[6], a);
+    c = fmaf(__uint_as_float(u & 0xF0000u), xs[7], c);
+    return a + c;
+}
 
 }  // namespace qw35

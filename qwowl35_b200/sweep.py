@@ -154,7 +154,55 @@ def matvec_gf4_b1(device) -> None:
         ops.matvec(ops.GF4, w, x, F, H, y=y)
 
 
-CASES = {"gateup_gf4_b32": gateup_gf4_b32, "gateup_gf4_b1": gateup_gf4_b1, "matvec_gf4_b1": matvec_gf4_b1,
+def matvec_q8_0_b1(device) -> None:
+    """DeltaNet input projection (Q8_0 12352 x 4096) at batch 1."""
+    ws = [_weight(ops.Q8_0, 12352, H, device) for _ in range(8)]
+    x = torch.randn(1, H, device=device)
+    y = torch.empty(1, 12352, device=device)
+    for w in ws:
+        ops.matvec(ops.Q8_0, w, x, 12352, H, y=y)
+
+
+def _deltanet(device, n: int) -> None:
+    """One Gated DeltaNet decode step over n sequences, over rotating state sets
+    (> 126 MB in total) so a launch streams its 4 MiB per sequence from HBM."""
+    sets = max(3, (3 * (126 << 20)) // (n * 2 * 32 * 128 * 128 * 4) + 1)
+    conv_w = torch.randn(8192, 4, device=device) * 0.3
+    dt, a = torch.randn(32, device=device), -torch.exp(torch.randn(32, device=device) * 0.5)
+    norm_w = torch.randn(128, device=device).abs()
+    proj = torch.randn(n, 12352, device=device)
+    for _ in range(sets):
+        conv = torch.randn(n, 8192 * 3, device=device)
+        ssm = torch.randn(n, 32 * 128 * 128, device=device) * 0.01
+        ops.deltanet_step(proj, conv_w, dt, a, norm_w, conv, ssm)
+
+
+def deltanet_b1(device) -> None:
+    """Gated DeltaNet decode step for one sequence."""
+    _deltanet(device, 1)
+
+
+def deltanet_b32(device) -> None:
+    """Gated DeltaNet decode step for 32 sequences."""
+    _deltanet(device, 32)
+
+
+def attn_pre_b32(device) -> None:
+    """Attention preprocess (q/k RMS norm, NeoX RoPE, f16 K/V rows into the chunk) for 32 sequences."""
+    plane = 4 * 256 * 256
+    B = 32
+    pool = torch.zeros(B * 2 * plane, device=device, dtype=torch.float16)
+    table = torch.tensor([[pool.data_ptr() + s * 2 * plane * 2] for s in range(B)], dtype=torch.int64, device=device)
+    qkv = torch.randn(B, 16 * 512 + 2048, device=device)
+    qn, kn = torch.randn(256, device=device).abs(), torch.randn(256, device=device).abs()
+    freq = torch.pow(1.0e7, -torch.arange(0, 64, 2, device=device, dtype=torch.float32) / 64.0)
+    pos = torch.arange(B, dtype=torch.int32, device=device) * 7
+    for _ in range(3):
+        ops.attn_preprocess(qkv, qn, kn, freq, pos, table, 0, plane * 2)
+
+
+CASES = {"gateup_gf4_b32": gateup_gf4_b32, "matvec_q8_0_b1": matvec_q8_0_b1, "deltanet_b1": deltanet_b1,
+         "deltanet_b32": deltanet_b32, "attn_pre_b32": attn_pre_b32, "gateup_gf4_b1": gateup_gf4_b1, "matvec_gf4_b1": matvec_gf4_b1,
          "matvec_q8_0_b32": matvec_q8_0_b32, "gqa_b8_ctx4096": gqa_b8_ctx4096}
 
 

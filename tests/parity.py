@@ -1,0 +1,33 @@
+"""Error measures shared by the GPU parity tests.
+
+``relerr`` is the bar every CUDA-vs-oracle comparison is held to (fp32
+accumulation, tolerance 1e-3 in the tests): the larger of
+  * the norm-wise error  max|y - ref| / max|ref|, and
+  * the per-element relative error  max |y_i - ref_i| / |ref_i| over the
+    elements with |ref_i| > 1e-3 * max|ref|
+so a row-local error on a small output cannot hide under the largest one.
+``normerr`` is the norm-wise part alone, for the few checks that compare two
+fp32 renderings of the same exact quantity at a much tighter bound.
+"""
+import numpy as np
+
+SIGNIFICANT = 1e-3  # elements below this fraction of max|ref| only count norm-wise
+
+
+def normerr(y, ref) -> float:
+    y = np.asarray(y, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    return float(np.max(np.abs(y - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def elemerr(y, ref) -> float:
+    y = np.asarray(y, dtype=np.float64).reshape(-1)
+    ref = np.asarray(ref, dtype=np.float64).reshape(-1)
+    m = np.abs(ref) > SIGNIFICANT * max(np.max(np.abs(ref)), 1e-30)
+    if not m.any():
+        return 0.0
+    return float(np.max(np.abs(y[m] - ref[m]) / np.abs(ref[m])))
+
+
+def relerr(y, ref) -> float:
+    return max(normerr(y, ref), elemerr(y, ref))

@@ -2,6 +2,7 @@
 oracle (qw35_attention.metal:29-414).  KV-chunk indexing must be exact;
 outputs within max relative error 1e-3."""
 import numpy as np
+from parity import normerr, relerr
 import pytest
 import torch
 
@@ -12,8 +13,6 @@ TOL = 1e-3
 PLANE = 4 * 256 * 256  # f16 elements of one K (or V) plane in a chunk
 
 
-def relerr(y, ref):
-    return float(np.max(np.abs(np.asarray(y, np.float64) - ref)) / max(np.max(np.abs(ref)), 1e-30))
 
 
 def make_pool(rng, lens, layers=1):
@@ -94,7 +93,7 @@ def test_preprocess_writes_kv_rows_and_rope():
     blocks = ((table.astype(np.int64) - base) // (per_chunk * 2))
     for s in range(n):
         rq, rg, rk, rv = O.attn_preprocess(qkv[s, :8192], qkv[s, 8192:9216], qkv[s, 9216:], qn, kn, int(pos[s]), freq)
-        assert relerr(q[s].cpu().numpy(), rq) < 1e-5
+        assert normerr(q[s].cpu().numpy(), rq) < 1e-5
         np.testing.assert_array_equal(gate[s].cpu().numpy(), rg.astype(np.float32))
         K, V = gather_kv(pool, perm, blocks[s], int(pos[s]) + 1, 0, per_chunk)
         np.testing.assert_array_equal(V[pos[s]], rv)                      # V: exact f16 RNE
@@ -195,7 +194,7 @@ def test_preprocess_q8_0_quantises_like_the_reference():
     for s in range(n):
         rq, rg, (rkd, rkq), (rvd, rvq) = O.attn_preprocess_q8_0(qkv[s, :8192], qkv[s, 8192:9216], qkv[s, 9216:],
                                                                 qn, kn, int(pos[s]), freq)
-        assert relerr(q[s].cpu().numpy(), rq) < 1e-5
+        assert normerr(q[s].cpu().numpy(), rq) < 1e-5
         (kd, kq), (vd, vq) = gather_kv_q8(host, blocks[s], int(pos[s]) + 1, 0, per_chunk)
         t = int(pos[s])
         np.testing.assert_array_equal(vq[t], rvq)                       # V: the same fp32 input, exact

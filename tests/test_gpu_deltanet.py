@@ -1,6 +1,7 @@
 """Gated DeltaNet decode step: CUDA (thread-block cluster kernel) vs the fp64
 oracle restating qw35_ssm.metal:260-451.  Tolerance: max relative error 1e-3."""
 import numpy as np
+from parity import normerr, relerr
 import pytest
 import torch
 
@@ -10,8 +11,6 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-3
 
 
-def relerr(y, ref):
-    return float(np.max(np.abs(np.asarray(y, np.float64) - ref)) / max(np.max(np.abs(ref)), 1e-30))
 
 
 def layer_params(rng):

@@ -5,6 +5,7 @@ argmax token ids.  Matvec family: max relative error 1e-3 (north-star
 tolerance) measured as max|y - y_ref| / max|y_ref|, fp64 reference.
 """
 import numpy as np
+from parity import normerr, relerr
 import pytest
 import torch
 
@@ -17,9 +18,6 @@ TOL = 1e-3
 CODECS = [Q.GF4_TYPE, Q.Q8_0_TYPE, Q.Q4_K_TYPE, Q.Q5_K_TYPE, Q.Q6_K_TYPE]
 
 
-def relerr(y, ref):
-    y = np.asarray(y, dtype=np.float64)
-    return float(np.max(np.abs(y - ref)) / max(np.max(np.abs(ref)), 1e-30))
 
 
 def make(t, rows, k, seed=0):
@@ -210,7 +208,7 @@ def test_batched_and_single_paths_agree():
     x = torch.from_numpy(np.random.default_rng(26).standard_normal((32, k)).astype(np.float32)).cuda()
     yb = ops.matvec(Q.Q8_0_TYPE, w, x, rows, k).cpu().numpy()
     ys = np.concatenate([ops.matvec(Q.Q8_0_TYPE, w, x[i:i + 1], rows, k).cpu().numpy() for i in range(32)])
-    assert relerr(yb, ys.astype(np.float64)) < 1e-5
+    assert normerr(yb, ys.astype(np.float64)) < 1e-5
     from qwowl35_b200 import lib
     torch.cuda.synchronize()
     assert lib().qw35_cuda_device_error() == 0

@@ -1,6 +1,7 @@
 """End-to-end decode through the drop-in C ABI (qw35_metal_* and the batched
 extensions) on a small synthetic model, against the fp64 oracle model."""
 import numpy as np
+from parity import normerr, relerr
 import pytest
 
 from oracle.model import OracleModel
@@ -12,8 +13,6 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-3
 
 
-def relerr(y, ref):
-    return float(np.max(np.abs(np.asarray(y, np.float64) - ref)) / max(np.max(np.abs(ref)), 1e-30))
 
 
 @pytest.fixture(scope="module")

@@ -101,3 +101,17 @@ def test_attn_preprocess_q8_0_matches_f16_twin_up_to_quantisation():
     kdq = O.q8_0_kv_dequant(kd, kq)
     assert np.max(np.abs(kdq - k16.astype(np.float64))) <= np.max(np.abs(k16.astype(np.float64))) / 127 + 1e-2
     np.testing.assert_array_equal(O.q8_0_kv_quantize(v.astype(np.float32))[1], vq)
+
+
+def test_parity_measure_catches_small_row_errors():
+    """The GPU tests' relerr adds a per-element bound above 1e-3 of the largest
+    output, so a 1% error on a small element fails although it is far below the
+    norm-wise 1e-3 of the largest one."""
+    from parity import elemerr, normerr, relerr
+    ref = np.array([1000.0, 2.0, -3.0, 1e-4])
+    y = ref.copy()
+    y[1] *= 1.01
+    assert normerr(y, ref) < 1e-3 and relerr(y, ref) > 1e-3
+    y = ref.copy()
+    y[3] *= 2.0  # below the significance floor: norm-wise only
+    assert elemerr(y, ref) == 0.0 and relerr(y, ref) < 1e-6
