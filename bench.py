@@ -15,7 +15,8 @@ Printed JSON line (rank 0):
   e2e       the same metric through the public C ABI in a greedy loop:
             token ids host->device, argmax ids device->host every step;
   roofline  the step's dominant kernel, timed alone with CUDA events;
-  cpu_baseline  the CPU oracle port on a bounded sample (rank 0, N=1).
+  cpu_baseline  the CPU oracle port on a bounded sample of the same batch
+            (rank 0, N=1; RefSample).
 --impl reference runs the reference's CPU rendering of the path (the oracle
 port: the reference's own GPU code is Metal-only) on the host cores.
 """
@@ -48,58 +49,6 @@ def peaks():
 # CPU leg: the oracle port on a bounded sample (test infrastructure; the
 # product path never touches it)
 # ---------------------------------------------------------------------------
-def cpu_token_seconds(ctx: int = 4096, head_frac: int = 64):
-    """Seconds for one decoded token of the CPU port (b=1), extrapolated from a
-    sample: one GF4 FFN (gate/up/down), one DeltaNet layer (Q8_0 projections +
-    step + out), one attention layer at `ctx` context and 1/head_frac of the
-    Q8_0 lm_head, each timed once and scaled by its per-token count."""
-    import numpy as np
-
-    from oracle import ops as O
-    from oracle import quants as Q
-    rng = np.random.default_rng(0)
-    H, F = 4096, 12288
-    gf4 = [Q.gen_weight(rng, Q.GF4_TYPE, r, k) for r, k in ((F, H), (F, H), (H, F))]
-    proj_d = Q.gen_weight(rng, Q.Q8_0_TYPE, 12352, H, 127.0)
-    proj_a = Q.gen_weight(rng, Q.Q8_0_TYPE, 10240, H, 127.0)
-    outw = Q.gen_weight(rng, Q.Q8_0_TYPE, H, 4096, 127.0)
-    headw = Q.gen_weight(rng, Q.Q8_0_TYPE, 248320 // head_frac, H, 127.0)
-    x = rng.standard_normal((1, H))
-    K = rng.standard_normal((ctx, 4, 256)).astype(np.float16)
-    V = rng.standard_normal((ctx, 4, 256)).astype(np.float16)
-    S = rng.normal(0, 0.01, (32, 128, 128))
-    conv_w, cs = rng.normal(0, 0.3, (8192, 4)), np.zeros((8192, 3))
-
-    t0 = time.perf_counter()
-    g = O.matvec(Q.dequant(Q.GF4_TYPE, gf4[0], F, H), x)
-    u = O.matvec(Q.dequant(Q.GF4_TYPE, gf4[1], F, H), x)
-    O.matvec(Q.dequant(Q.GF4_TYPE, gf4[2], H, F), O.silu(g) * u)
-    t_ffn = time.perf_counter() - t0
-
-    t0 = time.perf_counter()
-    p = O.matvec(Q.dequant(Q.Q8_0_TYPE, proj_d, 12352, H), x)[0]
-    out, _, _ = O.deltanet_step(p[:8192], conv_w, cs, p[12288:12320], p[12320:], np.zeros(32), -np.ones(32), S,
-                                p[8192:12288], np.ones(128))
-    O.matvec(Q.dequant(Q.Q8_0_TYPE, outw, H, 4096), out[None])
-    t_delta = time.perf_counter() - t0
-
-    t0 = time.perf_counter()
-    p = O.matvec(Q.dequant(Q.Q8_0_TYPE, proj_a, 10240, H), x)[0]
-    q, gate, _, _ = O.attn_preprocess(p[:8192], p[8192:9216], p[9216:], np.ones(256), np.ones(256), ctx - 1,
-                                      O.rope_freqs())
-    core = O.gqa_decode(q, gate, K, V).reshape(1, -1)
-    O.matvec(Q.dequant(Q.Q8_0_TYPE, outw, H, 4096), core)
-    t_attn = time.perf_counter() - t0
-
-    t0 = time.perf_counter()
-    O.matvec(Q.dequant(Q.Q8_0_TYPE, headw, 248320 // head_frac, H), x)
-    t_head = (time.perf_counter() - t0) * head_frac
-    total = 32 * t_ffn + 24 * t_delta + 8 * t_attn + t_head
-    sample = (f"1 GF4 FFN + 1 DeltaNet layer + 1 attention layer (ctx {ctx}) + 1/{head_frac} of the Q8_0 "
-              f"head, each timed once (fp64 numpy oracle, b=1), extrapolated to a 32-layer token")
-    return total, sample
-
-
 def cpu_cores() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -310,24 +259,110 @@ def max_over_ranks(v: float, world: int, device) -> float:
     return float(t.item())
 
 
+class RefSample:
+    """The reference arm's unit of work: one slice of one layer of the decode
+    step for the whole batch (the same config as the GPU arm), rendered by
+    the CPU oracle port (numpy, the host's BLAS threads).  A slice is 1/SLICES
+    of the layer's matrix rows (dequantised, then multiplied by all B
+    activation rows at once, as a batched engine reads weights once per step)
+    plus the per-sequence mixer (DeltaNet step or attention at ctx positions)
+    of B/SLICES sequences.  Step i takes layer i % 32 (attention when
+    (i + 1) % 4 == 0), so a run of K steps covers the model's layer mix; the
+    lm_head's slice is timed once.  The estimated decode step is
+    SLICES * (24 mean DeltaNet slices + 8 mean attention slices + 1 head slice)."""
+
+    SLICES = 16
+
+    def __init__(self, B: int, ctx: int):
+        import numpy as np
+
+        from oracle import quants as Q
+        self.np, self.Q = np, Q
+        self.B, self.ctx = B, ctx
+        rng = np.random.default_rng(0)
+        H, F, S = 4096, 12288, self.SLICES
+        self.rng = rng
+        # the slice's rows of every matrix of a layer (GGUF bytes; dequantised per use)
+        self.gate = Q.gen_weight(rng, Q.GF4_TYPE, F // S, H)
+        self.up = Q.gen_weight(rng, Q.GF4_TYPE, F // S, H)
+        self.down = Q.gen_weight(rng, Q.GF4_TYPE, H // S, F)
+        self.proj_d = Q.gen_weight(rng, Q.Q8_0_TYPE, 12352 // S, H, 127.0)
+        self.proj_a = Q.gen_weight(rng, Q.Q8_0_TYPE, 10240 // S, H, 127.0)
+        self.outw = Q.gen_weight(rng, Q.Q8_0_TYPE, H // S, 4096, 127.0)
+        self.head = Q.gen_weight(rng, Q.Q8_0_TYPE, 248320 // S, H, 127.0)
+        self.x = rng.standard_normal((B, H))
+        self.h = rng.standard_normal((B, F))
+        nseq = max(1, B // S)
+        self.nseq = nseq
+        self.K = rng.standard_normal((ctx, 4, 256)).astype(np.float16)
+        self.V = rng.standard_normal((ctx, 4, 256)).astype(np.float16)
+        self.S = [rng.normal(0, 0.01, (32, 128, 128)) for _ in range(nseq)]
+
+    def _mm(self, t, raw, rows, k, x):
+        return x @ self.Q.dequant(t, raw, rows, k).T.astype(self.np.float64)
+
+    def layer(self, attn: bool) -> float:
+        from oracle import ops as O
+        np, Q, H, F, S = self.np, self.Q, 4096, 12288, self.SLICES
+        t0 = time.perf_counter()
+        if attn:
+            self._mm(Q.Q8_0_TYPE, self.proj_a, 10240 // S, H, self.x)
+            for _ in range(self.nseq):
+                p = self.rng.standard_normal(10240)
+                q, gate, _, _ = O.attn_preprocess(p[:8192], p[8192:9216], p[9216:], np.ones(256), np.ones(256),
+                                                  self.ctx - 1, O.rope_freqs())
+                O.gqa_decode(q, gate, self.K, self.V)
+        else:
+            self._mm(Q.Q8_0_TYPE, self.proj_d, 12352 // S, H, self.x)
+            for i in range(self.nseq):
+                p = self.rng.standard_normal(12352)
+                O.deltanet_step(p[:8192], np.ones((8192, 4)) * 0.3, np.zeros((8192, 3)), p[12288:12320],
+                                p[12320:], np.zeros(32), -np.ones(32), self.S[i], p[8192:12288], np.ones(128))
+        self._mm(Q.Q8_0_TYPE, self.outw, H // S, 4096, self.x)
+        self._mm(Q.GF4_TYPE, self.gate, F // S, H, self.x)
+        self._mm(Q.GF4_TYPE, self.up, F // S, H, self.x)
+        self._mm(Q.GF4_TYPE, self.down, H // S, F, self.h)
+        return time.perf_counter() - t0
+
+    def head_slice(self) -> float:
+        t0 = time.perf_counter()
+        self._mm(self.Q.Q8_0_TYPE, self.head, 248320 // self.SLICES, 4096, self.x)
+        return time.perf_counter() - t0
+
+    def describe(self) -> str:
+        return (f"per step: 1/{self.SLICES} of one layer (rows of every matrix dequantised and multiplied by "
+                f"all {self.B} activation rows, plus the DeltaNet step / attention at ctx {self.ctx} for "
+                f"{self.nseq} sequence(s)), layers rotating through the 24 DeltaNet + 8 attention mix, fp64 "
+                f"numpy oracle port; decode step = {self.SLICES} x (24 DeltaNet + 8 attention + head) slices")
+
+
 def run_reference(args, world):
     rank, _, _ = dist_env()
     if rank != 0:
         return
     cores = cpu_cores()
-    times = []
-    sample = ""
+    ref = RefSample(args.batch, args.ctx_fill)
+    head = ref.head_slice()
+    t_delta, t_attn, times = [], [], []
     for i in range(args.warmup + args.steps):
-        t, sample = cpu_token_seconds(ctx=args.ctx_fill, head_frac=256)
+        attn = (i + 1) % 4 == 0
+        t = ref.layer(attn)
         if i >= args.warmup:
+            (t_attn if attn else t_delta).append(t)
             times.append(t)
-    tps = 1.0 / (sum(times) / len(times))
+    if not t_attn:  # fewer than 4 timed steps: time one attention slice as well
+        t_attn.append(ref.layer(True))
+    if not t_delta:
+        t_delta.append(ref.layer(False))
+    step_s = RefSample.SLICES * (24 * sum(t_delta) / len(t_delta) + 8 * sum(t_attn) / len(t_attn) + head)
+    tps = args.batch / step_s
     line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / tps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": workload_config(args, world),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
+            "step_unit": f"one 1/{RefSample.SLICES}-layer slice of the batch (see cpu_baseline.sample)",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic", "config": workload_config(args, 1),
             "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": "port",
-                             "sample": "per step: " + sample + "; the reference's own decode path is Metal-only "
+                             "sample": ref.describe() + "; the reference's own decode path is Metal-only "
                                        "(unavailable on this box), so its kernels run as the numpy oracle port"},
             "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -344,6 +379,54 @@ def workload_config(args, world):
             "l2": "inputs larger than L2: every step streams 5.7 GB of weights plus state/KV"}
 
 
+def run_ragged(args, rank, world, device, model, cfg):
+    """BASELINE config 4's ragged batch through the full decode step: 32 sequences
+    per GPU (global batch 32 * world) with context lengths log-uniform in
+    512..131072, assigned to ranks by the step-bytes partitioner
+    (qwowl35_b200.partition); each rank decodes only its own sequences, every
+    sequence at its own position.  KV caches are synthetic (no prefill).
+    Returns (tokens, device seconds of the slowest rank, detail dict)."""
+    import numpy as np
+    import torch
+
+    from qwowl35_b200.partition import imbalance, log_uniform_lengths, partition
+    from qwowl35_b200.runtime import LogitsMode, Runtime
+
+    lens = log_uniform_lengths(32 * world, seed=4)
+    parts = partition(lens, world)
+    mine = [lens[i] for i in parts[rank]]
+    n = len(mine)
+    steps = args.ragged_steps
+    rt = Runtime(model, ctx=max(mine) + steps + args.warmup + 8, max_seqs=max(n, 1))
+    ids = [0] + [rt.seq_alloc() for _ in range(n - 1)]
+    for k, (s_, L) in enumerate(zip(ids, mine)):
+        rt.seq_fill_synthetic(s_, L, seed=1000 + parts[rank][k])
+    pos = list(mine)
+    tok = [int((7919 * (i + 1)) % cfg.vocab) for i in range(n)]
+    for _ in range(args.warmup):
+        rt.eval_batch(ids, tok, pos, LogitsMode.ARGMAX)
+        pos = [p_ + 1 for p_ in pos]
+    rt.sync()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ext = torch.cuda.ExternalStream(rt.stream(), device=device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(steps):
+        rt.eval_batch(ids, tok, pos, LogitsMode.ARGMAX)
+        pos = [p_ + 1 for p_ in pos]
+    e1.record(ext)
+    e1.synchronize()
+    t = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, device)
+    rt.close()
+    detail = {"sequences": 32 * world, "lengths": "log-uniform 512..131072, seed 4",
+              "partition": "greedy by per-step bytes (weights + state + KV)",
+              "bytes_imbalance": round(imbalance(lens, parts), 4), "steps": steps,
+              "kv_positions_total": int(np.sum(lens))}
+    return 32 * world * steps, t, detail
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -355,6 +438,8 @@ def main():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel roofline table")
+    ap.add_argument("--ragged-steps", type=int, default=5,
+                    help="steps of the ragged config-4 batch (32 sequences/GPU, 512..131072 positions); 0 skips it")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_env()
@@ -386,14 +471,12 @@ def main():
     ids = [0] + [rt.seq_alloc() for _ in range(B - 1)]
     tok = (np.arange(B, dtype=np.uint32) * 7919) % cfg.vocab
 
-    # context fill (untimed): sequence 0 decodes ctx_fill positions, then every
-    # other sequence is forked from it (recurrent state + KV chunks copied)
+    # context (untimed): every sequence gets ctx_fill positions of synthetic KV
+    # (deterministic pseudo-random rows, no prefill); the recurrent state starts
+    # at zero.  A decode step reads the same bytes either way.
     t0 = time.time()
-    for p in range(args.ctx_fill):
-        rt.eval_batch([0], [int((p * 7919) % cfg.vocab)], [p], LogitsMode.NONE)
-    rt.sync()
-    for s_ in ids[1:]:
-        rt.seq_fork(0, s_)
+    for k, s_ in enumerate(ids):
+        rt.seq_fill_synthetic(s_, args.ctx_fill, seed=k)
     t_fill = time.time() - t0
     pos = args.ctx_fill
 
@@ -457,6 +540,10 @@ def main():
     e1.synchronize()
     b1_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, device)
     rt.close()
+    ragged = None
+    if args.ragged_steps > 0:
+        r_tok, r_s, r_detail = run_ragged(args, rank, world, device, model, cfg)
+        ragged = dict(value=r_tok / r_s, unit="tok/s", ms_per_step=r_s / args.ragged_steps * 1e3, **r_detail)
     del model
 
     line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -467,6 +554,7 @@ def main():
                     "d2h_bytes_per_step": 8 * B},
             "gpu_launches": kernels * args.steps,
             "b1": {"value": world * n1 / b1_s, "unit": "tok/s", "ms_per_token": b1_s / n1 * 1e3},
+            "ragged": ragged,
             "setup_s": {"generate": round(t_gen, 1), "upload": round(t_load, 1), "ctx_fill": round(t_fill, 1)}}
 
     if rank == 0 and not args.no_kernels:
@@ -496,9 +584,13 @@ def main():
         except Exception as exc:  # the GEMV table never blocks the bench line
             line["gemv"] = {"error": str(exc)[:200]}
     if rank == 0 and world == 1 and not args.no_cpu:
-        t, sample = cpu_token_seconds(ctx=args.ctx_fill, head_frac=64)
-        line["cpu_baseline"] = {"value": 1.0 / t, "unit": "tok/s", "cores": cpu_cores(), "kind": "port",
-                                "sample": sample}
+        ref = RefSample(B, args.ctx_fill)
+        head = ref.head_slice()
+        td = [ref.layer(False) for _ in range(3)]
+        ta = [ref.layer(True)]
+        step_s = RefSample.SLICES * (24 * sum(td) / len(td) + 8 * sum(ta) / len(ta) + head)
+        line["cpu_baseline"] = {"value": B / step_s, "unit": "tok/s", "cores": cpu_cores(), "kind": "port",
+                                "sample": ref.describe() + " (3 DeltaNet + 1 attention slice timed)"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -166,6 +166,14 @@ uint32_t qw35_cuda_runtime_max_seqs(void *runtime);
 // Copy sequence src (recurrent state and KV chunks) into allocated sequence
 // dst; both then continue from the same prefix.  Waits for the device.
 int qw35_cuda_runtime_seq_fork(void *runtime, uint32_t src, uint32_t dst, char *err, uintptr_t err_len);
+// Benchmark helper (no counterpart in the reference): gives sequence seq_id a
+// KV cache of `positions` rows in every attention layer, filled with
+// deterministic pseudo-random values from `seed` (f16 planes: uniform in
+// [-2, 2); q8_0 planes: d = 2/127, codes uniform in [-127, 127]), so a long
+// context can be decoded without prefilling it.  The recurrent state is left
+// as it is.  Waits for the device.
+int qw35_cuda_runtime_seq_fill_synthetic(void *runtime, uint32_t seq_id, uint32_t positions, uint64_t seed,
+                                         char *err, uintptr_t err_len);
 // One decode step for n sequences (token ids and positions are host arrays).
 int qw35_cuda_runtime_eval_batch(void *runtime, uint32_t n, const uint32_t *seq_ids, const uint32_t *tokens,
                                  const uint32_t *pos, int logits_mode, char *err, uintptr_t err_len);

@@ -147,9 +147,29 @@ def gf4_dequant_metal_half(words: np.ndarray) -> np.ndarray:
     return gf4_dequant_metal(words).astype(np.float16).astype(np.float32)
 
 
-def gf4_dequant(words: np.ndarray, exact: bool = False, half: bool = False) -> np.ndarray:
+def gf4_dequant_batched(words: np.ndarray) -> np.ndarray:
+    """Metal-mode weights as the batched (tensor-core, 3+ rows) path of this
+    build uses them: the reference decode values exactly (levels and the
+    element-4 junk), except in a 16-byte piece (4 words) holding a scale with
+    |s| > 252 (e5m2 byte & 0x7f > 0x5B), where element 4 takes the tiled
+    path's half rounding (``gf4_dequant_metal_half``)."""
+    w = np.asarray(words, dtype=np.uint32)
+    exact = gf4_dequant_metal(w)
+    rows = w.shape[0]
+    big = ((w & np.uint32(0x7F)) > np.uint32(0x5B)).reshape(rows, -1, 4).any(axis=-1)  # [rows, quads]
+    if not big.any():
+        return exact
+    half = gf4_dequant_metal_half(w).reshape(rows, -1, 32)
+    out = exact.reshape(rows, -1, 32).copy()
+    out[big] = half[big]
+    return out.reshape(exact.shape)
+
+
+def gf4_dequant(words: np.ndarray, exact: bool = False, half: bool = False, batched: bool = False) -> np.ndarray:
     if exact:
         return gf4_dequant_exact(words)
+    if batched:
+        return gf4_dequant_batched(words)
     return gf4_dequant_metal_half(words) if half else gf4_dequant_metal(words)
 
 
@@ -255,16 +275,18 @@ def dequant(type_id: int, raw: np.ndarray, rows: int, k: int, gf4_exact: bool = 
             gf4_half: bool = False, tiled: bool = False) -> np.ndarray:
     """Dequantised weights [rows, k] float32.
 
-    ``tiled=True`` gives the weights of the reference's multi-row (tiled)
-    path, which dequantises into half tiles (``qw35_tiled_mm.metal:197-255``):
-    GF4 element 4 rounded to half (``gf4_half``, unless ``gf4_exact``) and the
-    K-quants' fp32 values rounded to half (Q4_K ``dl*q - ml``,
+    ``tiled=True`` gives the weights of this build's batched (tensor-core)
+    path: GF4 exactly the decode values (``gf4_dequant_batched``; element 4
+    rounded to half only in pieces with a scale past 252, as the reference's
+    tiled path ``qw35_tiled_mm.metal:197-255`` rounds it everywhere), and the
+    K-quants' fp32 values rounded to half as the reference's tiled path
+    computes them (Q4_K ``dl*q - ml``,
     ``qw35_matvec.metal:20-38``; Q5_K the same with the fifth bit, :40-64;
     Q6_K ``d*sc*(q - 32)``, exact in fp32, :66-98).
     """
     if type_id == GF4_TYPE:
         return gf4_dequant(np.asarray(raw).view(np.uint32).reshape(rows, k // 8), exact=gf4_exact,
-                           half=gf4_half or (tiled and not gf4_exact))
+                           half=gf4_half, batched=tiled and not gf4_exact)
     if type_id == Q8_0_TYPE:
         return q8_0_dequant(raw, rows, k)
     if type_id == Q4_K_TYPE:

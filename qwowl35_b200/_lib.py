@@ -103,6 +103,7 @@ _SIGS = {
     "qw35_cuda_runtime_seq_reset": (C.c_int, [vp, C.c_uint32, cp, up]),
     "qw35_cuda_runtime_max_seqs": (C.c_uint32, [vp]),
     "qw35_cuda_runtime_seq_fork": (C.c_int, [vp, C.c_uint32, C.c_uint32, cp, up]),
+    "qw35_cuda_runtime_seq_fill_synthetic": (C.c_int, [vp, C.c_uint32, C.c_uint32, C.c_uint64, cp, up]),
     "qw35_cuda_runtime_eval_batch": (C.c_int, [vp, C.c_uint32, u32p, u32p, u32p, C.c_int, cp, up]),
     "qw35_cuda_runtime_argmax_batch": (C.c_int, [vp, C.c_uint32, u32p, f32p, cp, up]),
     "qw35_cuda_runtime_copy_logits_batch": (C.c_int, [vp, C.c_uint32, vp, up, cp, up]),

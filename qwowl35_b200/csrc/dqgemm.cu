@@ -91,16 +91,28 @@ struct DqParams {
     int red_tma;            // split tiles add into y by TMA bulk reduction (else per-element atomics)
 };
 
-// activation stage: the chunk's 2*NP rows (hi | lo) x KC columns of f16
-template <int CODEC, int NP>
-__host__ __device__ constexpr uint32_t dq_xstage() { return 2u * NP * DqGeo<CODEC>::KC * 2; }
+// Metal-mode GF4 carries each word's element-4 junk (the reference decode
+// kernel's unmasked bits, qw35_gf4.metal:8-20) exactly: the main f16 tile holds
+// the levels (q - 4) * s * -0.25 (exact), and a compact junk tile holds per
+// word the two parts of junk * s * -0.25 * 2^-13, times 2^10 (exact halves:
+// 5 + 3 and 4 + 3 significant bits), against an extra activation k-atom of
+// x_4 * 2^-10 per word.  K-steps per chunk: 16 main + 4 junk.
+template <int CODEC, bool EXACT>
+__host__ __device__ constexpr bool dq_junk() { return CODEC == QW35_GF4_TYPE && !EXACT; }
+
+// activation stage: the chunk's 2*NP rows (hi | lo) x KC columns of f16 (+ the
+// 64-column junk atom)
+template <int CODEC, int NP, bool JK>
+__host__ __device__ constexpr uint32_t dq_xstage() { return 2u * NP * (DqGeo<CODEC>::KC + (JK ? 64 : 0)) * 2; }
 
 // TMEM plan (512 columns): two segment accumulators of 2*NP columns
-// [hi-activation products | lo-activation products], then SA decoded A tiles.
-template <int CODEC, int NP> struct DqTmem {
+// [hi-activation products | lo-activation products], then SA decoded A tiles
+// (each ACOLS main columns, then 32 junk columns when JK).
+template <int CODEC, int NP, bool JK> struct DqTmem {
     static constexpr int RC = 2 * NP;  // columns of one accumulator
-    static constexpr int SA = NP == 64 ? 2 : 3;
-    static constexpr int A0 = 512 - SA * DqGeo<CODEC>::ACOLS;  // first A column
+    static constexpr int AC = DqGeo<CODEC>::ACOLS + (JK ? 32 : 0);  // columns of one A tile
+    static constexpr int SA = JK ? 2 : 3;
+    static constexpr int A0 = 512 - SA * AC;  // first A column
     static_assert(2 * RC <= A0, "TMEM plan");
 };
 
@@ -221,6 +233,46 @@ __device__ __forceinline__ void gf4_quad_to_halves(const uint4 w4, uint4 &o0, ui
     }
 }
 
+// The junk of a word as the two halves of the junk tile (see dq_junk):
+// {(junk & 31) * s * -2^-5, (junk >> 5) * 32 * s * -2^-5}, i.e. the word's
+// element-4 junk s * -0.25 * 2^-13 * junk times 2^10, split so both parts are
+// exact halves.  One PRMT puts bytes 1 and 2 of w (junk bits 3..7 of byte 1,
+// bits 0..3 of byte 2) under the exponent of 1024, one AND keeps those bits.
+// Exact for |s| >= 2^-14; callers use it only for |s| <= 252.
+__device__ __forceinline__ uint32_t gf4_junk_halves(uint32_t w) {
+    const uint32_t v = __byte_perm(w, 0x64646464u, 0x4241u) & 0xFF0FFFF8u;  // {1024 + 8 jl, 1024 + jh}
+    const __half2 q = __hsub2(*reinterpret_cast<const __half2 *>(&v),
+                              __half2half2(__ushort_as_half((unsigned short)0x6400)));  // {8 jl, jh}
+    const uint32_t hs = __byte_perm(w, 0u, 0x0404u);                                      // {s, s}
+    const __half2 m = __hmul2(*reinterpret_cast<const __half2 *>(&hs),
+                              __halves2half2(__ushort_as_half((unsigned short)0x9C00),     // -2^-8
+                                             __ushort_as_half((unsigned short)0xBC00)));   // -1
+    const __half2 j = __hmul2(q, m);
+    return *reinterpret_cast<const uint32_t *>(&j);
+}
+
+// Four words for the metal-mode tiles with the junk apart: exact levels into
+// o0..o3 and the junk halves into j[0..3]; words of a quad with a scale past
+// 252 keep the tiled-path rounding of element 4 instead (junk halves zero).
+__device__ __forceinline__ void gf4_quad_levels_junk(const uint4 w4, uint4 &o0, uint4 &o1, uint4 &o2, uint4 &o3,
+                                                     uint32_t *j) {
+    const uint32_t sb = __byte_perm(__byte_perm(w4.x, w4.y, 0x0040u), __byte_perm(w4.z, w4.w, 0x0040u), 0x5410u);
+    if ((((sb & 0x7f7f7f7fu) + 0x24242424u) & 0x80808080u) == 0u) {
+        o0 = gf4_word_fast<true>(w4.x);
+        o1 = gf4_word_fast<true>(w4.y);
+        o2 = gf4_word_fast<true>(w4.z);
+        o3 = gf4_word_fast<true>(w4.w);
+        j[0] = gf4_junk_halves(w4.x);
+        j[1] = gf4_junk_halves(w4.y);
+        j[2] = gf4_junk_halves(w4.z);
+        j[3] = gf4_junk_halves(w4.w);
+    } else {
+        gf4_pair_to_halves<false>(w4.x, w4.y, o0, o1);
+        gf4_pair_to_halves<false>(w4.z, w4.w, o2, o3);
+        j[0] = j[1] = j[2] = j[3] = 0u;
+    }
+}
+
 // Q8_0: 8 int8 codes -> 8 exact halves (1024 + (q + 128) - 1152).
 __device__ __forceinline__ uint4 q8_codes_to_halves(uint32_t a, uint32_t b) {
     const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6480));  // 1152
@@ -284,15 +336,19 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
           const __grid_constant__ CUtensorMap hmap0, const __grid_constant__ CUtensorMap hmap1, DqParams p, int SX,
           int NW) {
     using G = DqGeo<CODEC>;
-    using T = DqTmem<CODEC, NP>;
+    constexpr bool JK = dq_junk<CODEC, EXACT>();
+    using T = DqTmem<CODEC, NP, JK>;
     constexpr bool Q8 = G::Q8;
     constexpr int KC = G::KC;
     constexpr int RC = T::RC, SA = T::SA;
-    constexpr uint32_t XS = dq_xstage<CODEC, NP>();
+    constexpr uint32_t XS = dq_xstage<CODEC, NP, JK>();
     constexpr uint32_t WS = G::WS;
     constexpr uint32_t IDESC = idesc_f16_f32(TM, 2 * NP);  // B = [x_hi rows ; x_lo rows]
     constexpr uint32_t IDESC_HI = idesc_f16_f32(TM, NP);   // B = x_hi rows only (Q8_0 lo weights)
     constexpr int DEC = G::DEC, EPI = G::EPI;
+    // chunks per tensor-core accumulation (see the MMA issuer); the epilogue
+    // keeps NP fp32 sums per row, so batches of 64 use whole segments
+    constexpr int SUB = 2;
     extern __shared__ __align__(1024) uint8_t smem[];
 
     // 1024-byte aligned base (128B-swizzle atoms need it)
@@ -405,25 +461,28 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
         int c = 0, ul = 0;
         Ring rx, ra;
         DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
-            if (!*abort_flag) {
+            for (int u0 = c0; u0 < c1 && !*abort_flag; u0 += SUB) {
+                // one accumulation of at most SUB chunks (a sub-segment): short
+                // tensor-core accumulation chains, summed in fp32 by the epilogue
+                const int u1 = min(c1, u0 + SUB);
                 const int ab = ul & 1;
                 if (ul >= 2) {
                     dq_wait(&acc_empty[ab], ((ul >> 1) - 1) & 1, abort_flag, 16u);
                     tc_fence_after();
                 }
-                for (int kc = c0; kc < c1; ++kc, ++c) {
+                for (int kc = u0; kc < u1; ++kc, ++c) {
                     const int sx = rx.s, sa = ra.s;
                     dq_wait(&full_x[sx], rx.ph, abort_flag, 16u);
                     dq_wait(&full_a[sa], ra.ph, abort_flag, 16u);
                     if (*abort_flag) break;
                     tc_fence_after();
-                    const uint32_t a0 = tmem + T::A0 + sa * G::ACOLS;
+                    const uint32_t a0 = tmem + T::A0 + sa * T::AC;
                     // descriptor of k-step 0; later k-steps add a compile-time offset
                     // (start address field, 16-byte units; smem addresses stay < 2^18)
                     const uint64_t bd0 = smem_desc_sw128(smem_u32(xst + (size_t)sx * XS));
                     const uint32_t d0 = tmem + ab * RC;
                     if (elect_one()) {
-                        tc_mma_f16_ts(d0, a0, bd0, IDESC, kc > c0 ? 1u : 0u);
+                        tc_mma_f16_ts(d0, a0, bd0, IDESC, kc > u0 ? 1u : 0u);
                         if constexpr (Q8) tc_mma_f16_ts_acc(d0, a0 + 64, bd0, IDESC_HI);
 #pragma unroll
                         for (int j = 1; j < KC / 16; ++j) {
@@ -433,9 +492,17 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                             tc_mma_f16_ts_acc(d0, a0 + j * 8, bd, IDESC);
                             if constexpr (Q8) tc_mma_f16_ts_acc(d0, a0 + 64 + j * 8, bd, IDESC_HI);
                         }
+                        if constexpr (JK) {
+                            // junk tile (TMEM columns ACOLS..ACOLS+31) x the junk atom (the fifth)
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const uint64_t bd = bd0 + (uint64_t)((4 * (2 * NP * 128) + j * 32) >> 4);
+                                tc_mma_f16_ts_acc(d0, a0 + G::ACOLS + j * 8, bd, IDESC);
+                            }
+                        }
                         tc_commit(&free_a[sa]);
                         tc_commit(&free_x[sx]);
-                        if (kc + 1 == c1) tc_commit(&acc_full[ab]);
+                        if (kc + 1 == u1) tc_commit(&acc_full[ab]);
                     }
                     __syncwarp();
                     rx.next(SX);
@@ -471,7 +538,7 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                 if (*abort_flag) break;
                 tc_fence_after();
                 const uint8_t *row = wst + (size_t)sw * WS + r * 128;
-                const uint32_t tcol = tmem + lane_addr + T::A0 + sa * G::ACOLS + grp * 32;
+                const uint32_t tcol = tmem + lane_addr + T::A0 + sa * T::AC + grp * 32;
                 if constexpr (G::K4 || G::K5 || G::K6) {
                     // K-quants: 64 columns = pieces 2g, 2g+1 of the row (32 weights each).
                     // Low nibbles plus, for Q5_K / Q6_K, the high bits (stored in nibble
@@ -535,8 +602,16 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                     const uint4 wa = *reinterpret_cast<const uint4 *>(row + (((2 * grp) ^ (r & 7)) << 4));
                     const uint4 wb = *reinterpret_cast<const uint4 *>(row + (((2 * grp + 1) ^ (r & 7)) << 4));
                     uint4 h[8];
-                    gf4_quad_to_halves<EXACT>(wa, h[0], h[1], h[2], h[3]);
-                    gf4_quad_to_halves<EXACT>(wb, h[4], h[5], h[6], h[7]);
+                    if constexpr (JK) {
+                        uint32_t jk[8];
+                        gf4_quad_levels_junk(wa, h[0], h[1], h[2], h[3], jk);
+                        gf4_quad_levels_junk(wb, h[4], h[5], h[6], h[7], jk + 4);
+                        // junk tile columns ACOLS + 8 * grp .. (word 8 * grp + i at column i)
+                        tmem_st8(tmem + lane_addr + T::A0 + sa * T::AC + G::ACOLS + grp * 8, jk);
+                    } else {
+                        gf4_quad_to_halves<EXACT>(wa, h[0], h[1], h[2], h[3]);
+                        gf4_quad_to_halves<EXACT>(wb, h[4], h[5], h[6], h[7]);
+                    }
                     uint32_t o[32];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
@@ -597,9 +672,6 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
         DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
             if (!*abort_flag) {
                 const int row = tile * TM + row_in_tile;
-                const int ab = ul & 1;
-                dq_wait(&acc_full[ab], (ul >> 1) & 1, abort_flag, 64u);
-                tc_fence_after();
                 float es = 1.0f;  // Q8_0: 2^-e of the row
                 if constexpr (Q8) {
                     const int e = row < p.rows ? (int)p.rexp[m][row] : 0;
@@ -612,22 +684,13 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                 // Whole-tile schedules (gran == nch) store.
                 const bool split = MODE == DQ_ACCUM || p.gran < nch;
                 const CUtensorMap *ymap = (MODE == DQ_DUAL && m) ? &ymap1 : &ymap0;
-#pragma unroll
-                for (int n0 = 0; n0 < NP; n0 += 16) {
-                    uint32_t th[16], tl[16];
-                    tmem_ld16_async(tmem + lane_addr + ab * RC + n0, th);
-                    tmem_ld16_async(tmem + lane_addr + ab * RC + NP + n0, tl);
-                    tmem_ld_wait();
-                    if (n0 + 16 >= NP) {  // accumulator read out: the MMA may reuse it
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&acc_empty[ab]);
-                    }
+                // 16 columns of the row's result (hi + lo products), scaled and written
+                auto emit16 = [&](int n0, const float *sum) {
                     float v[16];
 #pragma unroll
                     for (int n = 0; n < 16; ++n) {
                         const float rs = __shfl_sync(0xffffffffu, n0 + n < 32 ? rs0 : rs1, (n0 + n) & 31);
-                        v[n] = (__uint_as_float(th[n]) + __uint_as_float(tl[n])) * es * rs;
+                        v[n] = sum[n] * es * rs;
                     }
                     if (split && p.red_tma) {
                         float *buf = stg + (sg & 1) * (16 * TM);
@@ -654,8 +717,57 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                             }
                         }
                     }
+                };
+                if constexpr (NP <= 32) {
+                    // the segment's sub-segment accumulators, summed in fp32
+                    float acc[NP];
+#pragma unroll
+                    for (int n = 0; n < NP; ++n) acc[n] = 0.0f;
+                    for (int u0 = c0; u0 < c1 && !*abort_flag; u0 += SUB) {
+                        const int ab = ul & 1;
+                        dq_wait(&acc_full[ab], (ul >> 1) & 1, abort_flag, 64u);
+                        tc_fence_after();
+#pragma unroll
+                        for (int n0 = 0; n0 < NP; n0 += 16) {
+                            uint32_t th[16], tl[16];
+                            tmem_ld16_async(tmem + lane_addr + ab * RC + n0, th);
+                            tmem_ld16_async(tmem + lane_addr + ab * RC + NP + n0, tl);
+                            tmem_ld_wait();
+#pragma unroll
+                            for (int n = 0; n < 16; ++n)
+                                acc[n0 + n] += __uint_as_float(th[n]) + __uint_as_float(tl[n]);
+                        }
+                        // accumulator read out: the MMA may reuse it
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&acc_empty[ab]);
+                        ++ul;
+                    }
+#pragma unroll
+                    for (int n0 = 0; n0 < NP; n0 += 16) emit16(n0, acc + n0);
+                } else {
+                    // one accumulation per segment, streamed out 16 columns at a time
+                    const int ab = ul & 1;
+                    dq_wait(&acc_full[ab], (ul >> 1) & 1, abort_flag, 64u);
+                    tc_fence_after();
+#pragma unroll
+                    for (int n0 = 0; n0 < NP; n0 += 16) {
+                        uint32_t th[16], tl[16];
+                        tmem_ld16_async(tmem + lane_addr + ab * RC + n0, th);
+                        tmem_ld16_async(tmem + lane_addr + ab * RC + NP + n0, tl);
+                        tmem_ld_wait();
+                        if (n0 + 16 >= NP) {  // accumulator read out: the MMA may reuse it
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&acc_empty[ab]);
+                        }
+                        float sum[16];
+#pragma unroll
+                        for (int n = 0; n < 16; ++n) sum[n] = __uint_as_float(th[n]) + __uint_as_float(tl[n]);
+                        emit16(n0, sum);
+                    }
+                    ++ul;
                 }
-                ++ul;
             }
         })
         if (ew == 0 && lane == 0) bulk_wait_all();  // our reductions are complete before exit
@@ -712,7 +824,7 @@ __device__ __forceinline__ void load8(const XT *p, float *v) {
 // running matvec CTA.
 template <typename XT>
 __global__ void __launch_bounds__(128) dq_prep_kernel(const XT *x, const float *norm_w, float eps, int K, int B, int NP,
-                                                      int gf4_perm, __half *xh, float *rowscale, float *zero0,
+                                                      int gf4_perm, int junk, __half *xh, float *rowscale, float *zero0,
                                                       float *zero1, int zero_rows) {
     __shared__ float red_s[4], red_m[4];
     pdl_trigger();  // the matvec may start streaming its weights now
@@ -795,13 +907,23 @@ __global__ void __launch_bounds__(128) dq_prep_kernel(const XT *x, const float *
             hw[i] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
             lw[i] = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
         }
-        // per 128-column chunk: [k-atom of 64][2*NP rows: hi rows, then lo rows][128 B swizzled]
-        const int k = g * 8, kl = k & 127;
-        uint8_t *base = reinterpret_cast<uint8_t *>(xh) + (size_t)(k >> 7) * (2 * NP) * 256 +
-                        (size_t)(kl >> 6) * (2 * NP) * 128;
-        const uint32_t c = (uint32_t)((kl & 63) >> 3);
+        // k-atoms of 64 columns [2*NP rows: hi rows, then lo rows][128 B swizzled],
+        // per 256 columns the four atoms of the chunk, then (junk) the junk atom
+        const int k = g * 8;
+        const size_t atom = (size_t)(k >> 8) * (junk ? 5 : 4) + ((k & 255) >> 6);
+        uint8_t *base = reinterpret_cast<uint8_t *>(xh) + atom * (2 * NP) * 128;
+        const uint32_t c = (uint32_t)((k & 63) >> 3);
         *reinterpret_cast<uint4 *>(base + sw128_off((uint32_t)n, c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
         *reinterpret_cast<uint4 *>(base + sw128_off((uint32_t)(NP + n), c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        if (junk) {
+            // word w of the chunk: junk-atom columns 2w, 2w+1 both hold x_4 * 2^-10 (hi | lo rows)
+            const float a = v[4] * 0.0009765625f;
+            const __half ha = __float2half_rn(a), la = __float2half_rn(a - __half2float(ha));
+            const uint32_t w = (uint32_t)((k & 255) >> 3);
+            uint8_t *jb = reinterpret_cast<uint8_t *>(xh) + ((size_t)(k >> 8) * 5 + 4) * (2 * NP) * 128 + (w & 3) * 4;
+            *reinterpret_cast<uint32_t *>(jb + sw128_off((uint32_t)n, w >> 2)) = (uint32_t)__half_as_ushort(ha) * 0x10001u;
+            *reinterpret_cast<uint32_t *>(jb + sw128_off((uint32_t)(NP + n), w >> 2)) = (uint32_t)__half_as_ushort(la) * 0x10001u;
+        }
     }
     if (n < B && (zero0 || zero1)) {
         __syncthreads();  // every read of x row n is done (y may alias x)
@@ -1013,7 +1135,7 @@ bool out_map(const void *y, uint32_t rows, uint32_t B, CUtensorMap *out) {
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int dq_np(int B) { return B <= 16 ? 16 : (B <= 32 ? 32 : 64); }
+int dq_np(int B) { return B <= 16 ? 16 : 32; }
 
 }  // namespace
 
@@ -1040,7 +1162,7 @@ static DqScratch dq_scratch_layout(int B, uint32_t k, uint32_t rows_out, size_t 
     auto up = [](size_t v) { return (v + 255) & ~(size_t)255; };
     DqScratch l{};
     l.x = 0;
-    l.rowscale = up((size_t)2 * NP * k * 2);
+    l.rowscale = up((size_t)2 * NP * k * 2 * 5 / 4);  // (GF4 metal mode: + a junk atom per 256 columns)
     l.ext = l.rowscale + 256;
     l.total = up(l.ext + ext_bytes);
     return l;
@@ -1061,11 +1183,12 @@ static cudaError_t dq_launch(const DqMaps &M, DqParams p, cudaStream_t st) {
     // stages <= 176 KB (+ 16 KB epilogue staging), so a 128-thread activation
     // prep CTA fits beside it on the SM
     constexpr uint32_t budget = 176u * 1024u;
-    constexpr uint32_t xs = dq_xstage<CODEC, NP>(), ws = DqGeo<CODEC>::WS;
+    constexpr bool JK = dq_junk<CODEC, EXACT>();
+    constexpr uint32_t xs = dq_xstage<CODEC, NP, JK>(), ws = DqGeo<CODEC>::WS;
     int SX = xs >= 65536u ? 2 : 3;
     // (at least two weight stages: Q6_K's 28 KB stages then pass the budget)
     int NW = std::max(2, std::min(4, (int)((budget - SX * xs) / ws)));
-    using T = DqTmem<CODEC, NP>;
+    using T = DqTmem<CODEC, NP, JK>;
     const size_t smem = 1024 + (size_t)SX * xs + (size_t)NW * ws + 2 * 16 * TM * 4 +
                         (2 * NW + 2 * SX + 2 * T::SA + 4 + 1) * 8 + 16;
     {
@@ -1104,8 +1227,7 @@ static cudaError_t dq_dispatch_mode(int mode, bool exact, const DqMaps &M, const
 template <int CODEC>
 static cudaError_t dq_dispatch_np(int NP, int mode, bool exact, const DqMaps &M, const DqParams &p, cudaStream_t st) {
     if (NP == 16) return dq_dispatch_mode<CODEC, 16>(mode, exact, M, p, st);
-    if (NP == 32) return dq_dispatch_mode<CODEC, 32>(mode, exact, M, p, st);
-    return dq_dispatch_mode<CODEC, 64>(mode, exact, M, p, st);
+    return dq_dispatch_mode<CODEC, 32>(mode, exact, M, p, st);
 }
 
 static cudaError_t dq_enqueue(const MatvecArgs &a, int mode, uint32_t *tok, float *val, const DqScratch &lay,
@@ -1113,6 +1235,20 @@ static cudaError_t dq_enqueue(const MatvecArgs &a, int mode, uint32_t *tok, floa
 
 // mode: 0 store, 1 accumulate, 2 swiglu pair, 3 logits for the argmax head
 cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cudaStream_t st) {
+    if (a.batch > 32) {
+        // two launches of at most 32 rows: the epilogue sums each row's short
+        // tensor-core accumulations in registers, 32 batch columns at most
+        MatvecArgs h = a;
+        h.batch = 32;
+        cudaError_t e = dq_run(h, mode, tok, val, st);
+        if (e != cudaSuccess) return e;
+        const size_t xes = a.x_dtype == QW35_F16_TYPE ? 2 : 4;
+        h = a;
+        h.batch = a.batch - 32;
+        h.x = static_cast<const uint8_t *>(a.x) + (size_t)32 * a.k * xes;
+        if (a.y) h.y = a.y + (size_t)32 * a.rows;
+        return dq_run(h, mode, tok ? tok + 32 : nullptr, val ? val + 32 : nullptr, st);
+    }
     const int B = a.batch, rows = (int)a.rows;
     const bool dual = mode == 2;
     DqMaps M;
@@ -1199,6 +1335,7 @@ static cudaError_t dq_enqueue(const MatvecArgs &a, int mode, uint32_t *tok, floa
                 out_map(y0, rows, B, &y0m) && (!dual || out_map(y1, rows, B, &y1m));
     if (!dual) y1m = y0m;
     const bool gperm = a.type_id == QW35_GF4_TYPE;
+    const int junk = (a.type_id == QW35_GF4_TYPE && !(a.flags & QW35_MV_GF4_EXACT)) ? 1 : 0;
     {
         cudaLaunchConfig_t cfg{};
         cfg.gridDim = dim3(NP);
@@ -1211,10 +1348,10 @@ static cudaError_t dq_enqueue(const MatvecArgs &a, int mode, uint32_t *tok, floa
         cfg.numAttrs = getenv("QW35_NO_PDL") ? 0 : 1;
         if (a.x_dtype == QW35_F16_TYPE)
             e = cudaLaunchKernelEx(&cfg, dq_prep_kernel<__half>, static_cast<const __half *>(a.x), a.norm_w, a.eps, K,
-                                   B, NP, (int)gperm, xh, rowscale, zero ? y0 : nullptr, zero ? y1 : nullptr, rows);
+                                   B, NP, (int)gperm, junk, xh, rowscale, zero ? y0 : nullptr, zero ? y1 : nullptr, rows);
         else
             e = cudaLaunchKernelEx(&cfg, dq_prep_kernel<float>, static_cast<const float *>(a.x), a.norm_w, a.eps, K, B,
-                                   NP, (int)gperm, xh, rowscale, zero ? y0 : nullptr, zero ? y1 : nullptr, rows);
+                                   NP, (int)gperm, junk, xh, rowscale, zero ? y0 : nullptr, zero ? y1 : nullptr, rows);
         if (e != cudaSuccess) return e;
     }
     e = cudaGetLastError();

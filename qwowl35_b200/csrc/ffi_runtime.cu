@@ -298,6 +298,15 @@ int qw35_cuda_runtime_seq_fork(void *runtime, uint32_t src, uint32_t dst, char *
     });
 }
 
+int qw35_cuda_runtime_seq_fill_synthetic(void *runtime, uint32_t seq_id, uint32_t positions, uint64_t seed,
+                                         char *err, uintptr_t err_len) {
+    return guarded(runtime, err, err_len, [&](Runtime *rt) {
+        if (seq_id >= rt->max_seqs || !rt->slot_used[seq_id]) qw35::fail("sequence %u is not allocated", seq_id);
+        if (positions > rt->ctx) qw35::fail("%u positions exceed the context of %u", positions, rt->ctx);
+        qw35::rt_fill_synthetic(rt, seq_id, positions, seed);
+    });
+}
+
 uint32_t qw35_cuda_runtime_max_seqs(void *runtime) {
     Runtime *rt = lookup(runtime);
     return rt ? rt->max_seqs : 0;

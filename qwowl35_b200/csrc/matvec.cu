@@ -22,6 +22,7 @@
 // warp kw owns the 32 columns of chunk kw*32+l), and decode every code with
 // one logic op + one FMA (quant.cuh "fast decode").  Per-row partials reduce
 // with warp shuffles, then across the KW warps through shared memory.
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 
@@ -199,11 +200,17 @@ template <int CODEC, int MODE> constexpr int rows_per_warp() {
 #define MV_WARPS_B1 12
 #endif
 template <int B> constexpr int mv_max_warps() { return B == 1 ? MV_WARPS_B1 : 12; }
+// 32-column chunks each consumer lane owns (its activations stay in registers):
+// two for batch-1 GF4, which halves the per-row reduction work per weight
+template <int CODEC, int B> constexpr int mv_lane_chunks() { return 1; }
 
 // Shared-memory carve-up (dynamic): [NM][kStages][stage_bytes] weights |
-// [2][G][B][NM][KW] partials | 64 floats scratch | 2*kStages mbarriers | abort.
+// [row of the CTA][B][NM][KW] partials | 64 floats scratch | 2*kStages
+// mbarriers | abort.  Each consumer warp writes its own partial slot of every
+// row it handles (no stage-wide barrier); the rows are summed in a fixed order
+// and written once, after the last stage.
 template <int CODEC, int B, int MODE, bool EXACT, typename XT>
-__global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, 1) mv_kernel(MvParams p) {
+__global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, mv_max_warps<B>() <= 8 ? 2 : 1) mv_kernel(MvParams p) {
     constexpr int NM = MODE == MV_SWIGLU ? 2 : 1;
     constexpr int NC = Codec<CODEC>::NC;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -215,13 +222,14 @@ __global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, 1) mv_kernel(MvP
     const uint32_t SB = p.stage_bytes;
     uint8_t *wbuf = smem;
     float *part = reinterpret_cast<float *>(smem + (size_t)NM * kStages * SB);
-    float *red = part + 2 * G * B * NM * KW;
+    // contiguous, balanced split of the row groups over the grid
+    const int groups_total = (p.rows + G - 1) / G;
+    const int max_rows = (groups_total + gridDim.x - 1) / gridDim.x * G;
+    float *red = part + (size_t)max_rows * B * NM * KW;
     uint64_t *full = reinterpret_cast<uint64_t *>(red + 64);
     uint64_t *empty = full + kStages;
     volatile int *abort_flag = reinterpret_cast<volatile int *>(empty + kStages);
 
-    // contiguous, balanced split of the row groups over the grid
-    const int groups_total = (p.rows + G - 1) / G;
     const int g0 = (int)(((long long)blockIdx.x * groups_total) / gridDim.x);
     const int g1 = (int)(((long long)(blockIdx.x + 1) * groups_total) / gridDim.x);
     const int r0 = g0 * G;
@@ -275,22 +283,26 @@ __global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, 1) mv_kernel(MvP
     }
 
     // -------------------------------- consumers ------------------------------
+    constexpr int LC = mv_lane_chunks<CODEC, B>();
     const int kw = wid % KW, rs = wid / KW;
-    const int nchunk = p.K >> 5;
-    const int c = kw * 32 + lane;
+    const int nchunk = p.K / (32 * LC);
+    const int c = kw * 32 + lane;  // the lane's columns: [c * 32 * LC, (c + 1) * 32 * LC)
     const bool active = c < nchunk;
     pdl_wait();  // the activation row is written by the previous kernel
 
-    float xs[B][32];
+    float xs[B][32 * LC];
     float cst[B][NC];
     const XT *xg = reinterpret_cast<const XT *>(p.x);
 #pragma unroll
     for (int b = 0; b < B; ++b) {
-        if (active) {
-            load_x32<XT>(xs[b], xg + (size_t)b * p.K + (size_t)c * 32);
-        } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) xs[b][i] = 0.0f;
+        for (int q = 0; q < LC; ++q) {
+            if (active) {
+                load_x32<XT>(xs[b] + 32 * q, xg + (size_t)b * p.K + ((size_t)c * LC + q) * 32);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) xs[b][32 * q + i] = 0.0f;
+            }
         }
     }
     if (p.norm_w != nullptr) {
@@ -298,7 +310,7 @@ __global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, 1) mv_kernel(MvP
         for (int b = 0; b < B; ++b) {
             float ss = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 32; ++i) ss = fmaf(xs[b][i], xs[b][i], ss);
+            for (int i = 0; i < 32 * LC; ++i) ss = fmaf(xs[b][i], xs[b][i], ss);
             ss = warp_sum(ss);
             if (lane == 0 && rs == 0) red[kw] = ss;
             named_sync(1, ncons);
@@ -307,9 +319,9 @@ __global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, 1) mv_kernel(MvP
             named_sync(1, ncons);
             const float inv = rsqrtf(tot / (float)p.K + p.eps);
             if (active) {
-                const float4 *nw = reinterpret_cast<const float4 *>(p.norm_w + (size_t)c * 32);
+                const float4 *nw = reinterpret_cast<const float4 *>(p.norm_w + (size_t)c * 32 * LC);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
+                for (int i = 0; i < 8 * LC; ++i) {
                     const float4 w4 = __ldg(nw + i);
                     xs[b][4 * i] = xs[b][4 * i] * inv * w4.x;
                     xs[b][4 * i + 1] = xs[b][4 * i + 1] * inv * w4.y;
@@ -320,10 +332,10 @@ __global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, 1) mv_kernel(MvP
         }
     }
     // GF4: activations as scaled pairs for the packed exact-level decode
-    float2 xp[B][16];
-    float xa[B][4], xj[B][4];
+    float2 xp[B][16 * LC];
+    float xa[B][4 * LC], xj[B][4 * LC];
     if constexpr (CODEC == QW35_GF4_TYPE) {
-        prep_x_gf4<B>(xs, xp, xa, xj);
+        prep_x_gf4<B, 4 * LC>(xs, xp, xa, xj);
     } else if constexpr (CODEC == QW35_Q8_0_TYPE) {
 #pragma unroll
         for (int b = 0; b < B; ++b)
@@ -334,20 +346,14 @@ __global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, 1) mv_kernel(MvP
         for (int b = 0; b < B; ++b) prep_x<CODEC, EXACT>(xs[b], cst[b]);
     }
 
-    float best_v = -INFINITY;
-    uint32_t best_i = 0xffffffffu;
-    const int fin_slots = G * B;
-    const int ft = threadIdx.x;
-    const int f_i = ft / B, f_b = ft % B;
 
     for (int g = 0; g < ngroups; ++g) {
         const int s = g % kStages;
         if (!*abort_flag) {
             if (!mbar_wait(&full[s], (g / kStages) & 1, 2u)) *abort_flag = 1;
         }
-        const int row0 = r0 + g * G;
-        const int nr = min(G, r1 - row0);
-        float *pg = part + (g & 1) * G * B * NM * KW;
+        const int nr = min(G, r1 - (r0 + g * G));
+        float *pg = part + (size_t)g * G * B * NM * KW;  // this stage's rows
         if constexpr (CODEC == QW35_GF4_TYPE || CODEC == QW35_Q8_0_TYPE) {
             // this warp's rows of the stage: rs + j * RS, all in flight at once;
             // rows past nr run on stale stage bytes and are never stored
@@ -362,14 +368,17 @@ __global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, 1) mv_kernel(MvP
                 for (int m = 0; m < NM; ++m) {
                     const uint8_t *st = wbuf + ((size_t)m * kStages + s) * SB;
                     if constexpr (CODEC == QW35_GF4_TYPE) {
-                        const uint4 wv = *reinterpret_cast<const uint4 *>(st + (size_t)i * p.code_row + cc * 16);
                         float2 r2[B];
 #pragma unroll
                         for (int b = 0; b < B; ++b) r2[b] = make_float2(0.0f, 0.0f);
-                        gf4_word_f2<EXACT, B>(wv.x, 0, xp, xa, xj, r2);
-                        gf4_word_f2<EXACT, B>(wv.y, 1, xp, xa, xj, r2);
-                        gf4_word_f2<EXACT, B>(wv.z, 2, xp, xa, xj, r2);
-                        gf4_word_f2<EXACT, B>(wv.w, 3, xp, xa, xj, r2);
+#pragma unroll
+                        for (int q = 0; q < LC; ++q) {
+                            const uint4 wv = *reinterpret_cast<const uint4 *>(st + (size_t)i * p.code_row + (cc * LC + q) * 16);
+                            gf4_word_f2<EXACT, B, 16 * LC, 4 * LC>(wv.x, 4 * q + 0, xp, xa, xj, r2);
+                            gf4_word_f2<EXACT, B, 16 * LC, 4 * LC>(wv.y, 4 * q + 1, xp, xa, xj, r2);
+                            gf4_word_f2<EXACT, B, 16 * LC, 4 * LC>(wv.z, 4 * q + 2, xp, xa, xj, r2);
+                            gf4_word_f2<EXACT, B, 16 * LC, 4 * LC>(wv.w, 4 * q + 3, xp, xa, xj, r2);
+                        }
 #pragma unroll
                         for (int b = 0; b < B; ++b) v[(j * NM + m) * B + b] = active ? (r2[b].x + r2[b].y) * kGf4Unscale : 0.0f;
                     } else {
@@ -415,45 +424,66 @@ __global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, 1) mv_kernel(MvP
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with the stage
-        named_sync(1, ncons);
-        if (ft < fin_slots && f_i < nr) {
-            const int row = row0 + f_i;
-            const float *pp = pg + (f_i * B + f_b) * NM * KW;
-            float s0 = 0.0f;
-            for (int k = 0; k < KW; ++k) s0 += pp[k];
-            float *yo = p.y + (size_t)f_b * p.rows + row;
-            if constexpr (MODE == MV_STORE) {
-                *yo = s0;
-            } else if constexpr (MODE == MV_ACCUM) {
-                *yo += s0;
-            } else if constexpr (MODE == MV_SWIGLU) {
-                float s1 = 0.0f;
-                for (int k = 0; k < KW; ++k) s1 += pp[KW + k];
-                *yo = silu_f(s0) * s1;
-            } else {
-                if (p.y != nullptr) *yo = s0;
-                if (s0 > best_v) { best_v = s0; best_i = (uint32_t)row; }  // rows ascend: keeps lowest id
-            }
+    }
+
+    // ---- the CTA's rows: partials summed in a fixed order, written once ----
+    named_sync(1, ncons);
+    const int nrows = r1 - r0;
+    float best_v[B];
+    uint32_t best_i[B];
+#pragma unroll
+    for (int b = 0; b < B; ++b) { best_v[b] = -INFINITY; best_i[b] = 0xffffffffu; }
+    for (int t = threadIdx.x; t < nrows * B; t += ncons) {
+        const int b = t / nrows, rr = t - b * nrows;  // consecutive threads: consecutive rows
+        const float *pp = part + ((size_t)rr * B + b) * NM * KW;
+        float s0 = 0.0f;
+        for (int k = 0; k < KW; ++k) s0 += pp[k];
+        float *yo = p.y + (size_t)b * p.rows + r0 + rr;
+        if constexpr (MODE == MV_STORE) {
+            *yo = s0;
+        } else if constexpr (MODE == MV_ACCUM) {
+            *yo += s0;
+        } else if constexpr (MODE == MV_SWIGLU) {
+            float s1 = 0.0f;
+            for (int k = 0; k < KW; ++k) s1 += pp[KW + k];
+            *yo = silu_f(s0) * s1;
+        } else {
+            if (p.y != nullptr) *yo = s0;
+            // a thread's rows ascend within each batch row: keeps the lowest id on ties
+#pragma unroll
+            for (int bb = 0; bb < B; ++bb)
+                if (bb == b && s0 > best_v[bb]) { best_v[bb] = s0; best_i[bb] = (uint32_t)(r0 + rr); }
         }
-        // partials are double-buffered by group parity: one barrier per group
     }
 
     if constexpr (MODE == MV_ARGMAX) {
-        named_sync(1, ncons);
-        float *bv = red;  // fin_slots = G * B <= 32
+        // per batch row: (max, lowest id) over the warp by shuffles, then over the
+        // consumer warps through shared memory (ncw * B <= 32 slots)
+        float *bv = red;
         uint32_t *bi = reinterpret_cast<uint32_t *>(red + 32);
-        if (ft < fin_slots) { bv[ft] = best_v; bi[ft] = best_i; }
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            float v = best_v[b];
+            uint32_t id = best_i[b];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+                const uint32_t oi = __shfl_xor_sync(0xffffffffu, id, o);
+                if (ov > v || (ov == v && oi < id)) { v = ov; id = oi; }
+            }
+            if (lane == 0) { bv[wid * B + b] = v; bi[wid * B + b] = id; }
+        }
         named_sync(1, ncons);
-        if (ft < B) {
+        if ((int)threadIdx.x < B) {
             float v = -INFINITY;
             uint32_t id = 0xffffffffu;
-            for (int t = ft; t < fin_slots; t += B) {
-                const float tv = bv[t];
-                const uint32_t ti = bi[t];
+            for (int w = 0; w < ncw; ++w) {
+                const float tv = bv[w * B + threadIdx.x];
+                const uint32_t ti = bi[w * B + threadIdx.x];
                 if (tv > v || (tv == v && ti < id)) { v = tv; id = ti; }
             }
-            p.part_val[(size_t)blockIdx.x * B + ft] = v;
-            p.part_idx[(size_t)blockIdx.x * B + ft] = id;
+            p.part_val[(size_t)blockIdx.x * B + threadIdx.x] = v;
+            p.part_idx[(size_t)blockIdx.x * B + threadIdx.x] = id;
         }
     }
 }
@@ -513,7 +543,7 @@ template <int CODEC, int B, int MODE>
 static MvGeom mv_geometry(int rows, int K, const void *kern) {
     constexpr int NM = MODE == MV_SWIGLU ? 2 : 1;
     MvGeom g;
-    const int nchunk = K / 32;
+    const int nchunk = K / (32 * mv_lane_chunks<CODEC, B>());
     g.kw = (nchunk + 31) / 32;
     codec_rows(CODEC, K, g.code_row, g.scale_row);
     const uint32_t rb = g.code_row + g.scale_row;
@@ -529,14 +559,25 @@ static MvGeom mv_geometry(int rows, int K, const void *kern) {
     g.threads = (g.kw * g.rs + 1) * 32;
     if (CODEC != QW35_GF4_TYPE && CODEC != QW35_Q8_0_TYPE) g.G = g.G < 1 ? 1 : (g.G > 16 ? 16 : g.G);
     g.stage_bytes = ((uint32_t)g.G * rb + 127u) & ~127u;
-    g.smem = (size_t)NM * kStages * g.stage_bytes + (size_t)2 * g.G * B * NM * g.kw * 4 + 64 * 4 +
-             2 * kStages * 8 + 16;
-    int occ = 1;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, g.threads, g.smem);
-    if (occ < 1) occ = 1;
-    const int max_ctas = qw35h::sm_count() * occ;
+    // stages + 64 floats + mbarriers, then the CTA's row partials, which depend
+    // on the grid (rows per CTA): sized for the grid the occupancy allows
+    const size_t base = (size_t)NM * kStages * g.stage_bytes + 64 * 4 + 2 * kStages * 8 + 16;
     const int groups = (rows + g.G - 1) / g.G;
-    g.ctas = groups < max_ctas ? groups : max_ctas;
+    auto part_bytes = [&](int ctas) {
+        return (size_t)((groups + ctas - 1) / ctas) * g.G * B * NM * g.kw * 4;
+    };
+    int occ = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, g.threads, base);
+    if (occ < 1) occ = 1;
+    g.ctas = std::min(groups, qw35h::sm_count() * occ);
+    g.smem = base + part_bytes(g.ctas);
+    int occ2 = 1;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ2, kern, g.threads, g.smem);
+    if (occ2 < 1) occ2 = 1;
+    if (occ2 < occ) {
+        g.ctas = std::min(groups, qw35h::sm_count() * occ2);
+        g.smem = base + part_bytes(g.ctas);
+    }
     g.rows_per_cta = 0;  // the kernel splits the groups evenly over the grid
     return g;
 }
@@ -550,7 +591,7 @@ static cudaError_t mv_launch(MvParams p, cudaStream_t st, int *ctas_out) {
     }
     MvGeom g = mv_geometry<CODEC, B, MODE>(p.rows, p.K, (const void *)kern);
     if (g.kw > 12 || g.smem > 200 * 1024) return cudaErrorInvalidValue;
-    if (MODE == MV_ARGMAX && (p.part_val == nullptr || g.G * B > 32)) return cudaErrorInvalidValue;
+    if (MODE == MV_ARGMAX && (p.part_val == nullptr || g.kw * g.rs * B > 32)) return cudaErrorInvalidValue;
     p.kw = g.kw;
     p.rs = g.rs;
     p.G = g.G;

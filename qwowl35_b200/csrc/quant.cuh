@@ -158,9 +158,9 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
 constexpr int kGf4M = 30;
 constexpr float kGf4Unscale = 1073741824.0f;  // 2^kGf4M
 
-template <bool EXACT, int B>
-__device__ __forceinline__ void gf4_word_f2(uint32_t w, int wd, const float2 (*xp)[16], const float (*xa)[4],
-                                            const float (*xj)[4], float2 *r2) {
+template <bool EXACT, int B, int NP = 16, int NWD = 4>
+__device__ __forceinline__ void gf4_word_f2(uint32_t w, int wd, const float2 (*xp)[NP], const float (*xa)[NWD],
+                                            const float (*xj)[NWD], float2 *r2) {
     const uint32_t v = w ^ 0x92492400u;  // bit 2 of every code
     const uint32_t u = v >> 12;          // codes 5, 6, 7 at bits 11, 14, 17
     const float2 g0 = make_float2(__uint_as_float(v & (7u << 8)), __uint_as_float(v & (7u << 11)));
@@ -181,16 +181,16 @@ __device__ __forceinline__ void gf4_word_f2(uint32_t w, int wd, const float2 (*x
     }
 }
 
-// Activations of the lane's 32 columns (4 words) for gf4_word_f2.
-template <int B>
-__device__ __forceinline__ void prep_x_gf4(const float (*xs)[32], float2 (*xp)[16], float (*xa)[4],
-                                           float (*xj)[4]) {
+// Activations of the lane's NWD words (8 * NWD columns) for gf4_word_f2.
+template <int B, int NWD>
+__device__ __forceinline__ void prep_x_gf4(const float (*xs)[8 * NWD], float2 (*xp)[4 * NWD], float (*xa)[NWD],
+                                           float (*xj)[NWD]) {
     // code j of a word sits at p = 8, 11, 14, 17, 20, 11, 14, 17 (see gf4_word_f2)
     constexpr int P[8] = {8, 11, 14, 17, 20, 11, 14, 17};
 #pragma unroll
     for (int b = 0; b < B; ++b) {
 #pragma unroll
-        for (int wd = 0; wd < 4; ++wd) {
+        for (int wd = 0; wd < NWD; ++wd) {
             float f[8], sum = 0.0f;
 #pragma unroll
             for (int j = 0; j < 8; ++j) {

@@ -180,6 +180,9 @@ void rt_ensure_kv(Runtime *rt, uint32_t slot, uint64_t positions);
 void rt_reset_slot(Runtime *rt, uint32_t slot);
 void rt_set_ctx(Runtime *rt, uint32_t ctx);
 void rt_fork(Runtime *rt, uint32_t src, uint32_t dst);
+// KV rows [0, positions) of every attention layer of `slot` filled with
+// deterministic pseudo-random values (benchmark contexts without a prefill)
+void rt_fill_synthetic(Runtime *rt, uint32_t slot, uint32_t positions, uint64_t seed);
 uint64_t rt_state_size(const Runtime *rt);
 void rt_state_export(Runtime *rt, uint32_t slot, uint8_t *buf, uint64_t len);
 void rt_state_import(Runtime *rt, uint32_t slot, const uint8_t *buf, uint64_t len);

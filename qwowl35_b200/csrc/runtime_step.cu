@@ -254,6 +254,54 @@ void rt_fork(Runtime *rt, uint32_t src, uint32_t dst) {
     rt_wait(rt);
 }
 
+// Pseudo-random KV contents: f16 planes get values uniform in [-2, 2) from a
+// hash of (seed, chunk, element); q8_0 planes get blocks {d = 2/127 as f16,
+// codes uniform in [-127, 127]}.  One CTA per (chunk, slice of the chunk).
+__device__ __forceinline__ uint32_t fill_hash(uint64_t a) {
+    a ^= a >> 33;
+    a *= 0xff51afd7ed558ccdull;
+    a ^= a >> 33;
+    a *= 0xc4ceb9fe1a85ec53ull;
+    a ^= a >> 33;
+    return (uint32_t)a;
+}
+
+__global__ void kv_fill_kernel(const uint64_t *chunks, size_t chunk_bytes, int kv_q8, uint64_t seed) {
+    uint8_t *base = reinterpret_cast<uint8_t *>(chunks[blockIdx.y]);
+    const uint64_t key = seed * 0x9E3779B97F4A7C15ull + blockIdx.y;
+    if (!kv_q8) {
+        const size_t n = chunk_bytes / 4;  // half2 words
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+            const uint32_t h = fill_hash(key * 0x100000001B3ull + i);
+            const float a = (float)(h & 0xffffu) * (4.0f / 65536.0f) - 2.0f;
+            const float b = (float)(h >> 16) * (4.0f / 65536.0f) - 2.0f;
+            reinterpret_cast<__half2 *>(base)[i] = __floats2half2_rn(a, b);
+        }
+    } else {
+        const size_t n = chunk_bytes / 34;  // q8_0 blocks {f16 d; int8 qs[32]}
+        const __half d = __float2half_rn(2.0f / 127.0f);
+        for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+            uint8_t *blk = base + i * 34;
+            *reinterpret_cast<__half *>(blk) = d;
+            for (int j = 0; j < 32; j += 4) {
+                const uint32_t h = fill_hash(key * 0x100000001B3ull + i * 8 + (j >> 2));
+#pragma unroll
+                for (int t = 0; t < 4; ++t) blk[2 + j + t] = (uint8_t)(int8_t)((int)((h >> (8 * t)) % 255u) - 127);
+            }
+        }
+    }
+}
+
+void rt_fill_synthetic(Runtime *rt, uint32_t slot, uint32_t positions, uint64_t seed) {
+    if (rt->model->n_attn == 0 || positions == 0) return;
+    rt_ensure_kv(rt, slot, positions);
+    const uint32_t nch = (positions + kChunk - 1) / kChunk;
+    kv_fill_kernel<<<dim3(64, nch), 256, 0, rt->stream>>>(rt->d_chunk_table + (size_t)slot * rt->table_chunks,
+                                                          rt->chunk_bytes, rt->kv_q8, seed);
+    ck(cudaGetLastError(), "kv fill");
+    rt_wait(rt);
+}
+
 void rt_set_ctx(Runtime *rt, uint32_t ctx) {
     if (ctx <= rt->ctx) return;
     if (ctx > kMaxCtx) fail("ctx %u exceeds the maximum %u tokens the KV cache can address", ctx, kMaxCtx);

@@ -124,6 +124,10 @@ class Runtime:
     def seq_fork(self, src: int, dst: int):
         self._call("qw35_cuda_runtime_seq_fork", src, dst)
 
+    def seq_fill_synthetic(self, seq: int, positions: int, seed: int = 0):
+        """Benchmark contexts: `positions` pseudo-random KV rows without a prefill."""
+        self._call("qw35_cuda_runtime_seq_fill_synthetic", seq, positions, seed)
+
     def seq_reset(self, seq: int):
         self._call("qw35_cuda_runtime_seq_reset", seq)
 

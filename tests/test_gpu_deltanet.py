@@ -89,3 +89,45 @@ def test_deltanet_core_config3(n):
                                  1.0 / np.sqrt(128))
         assert relerr(y[i], yr) < TOL
         assert relerr(Sn[i], Sr) < TOL
+
+
+def test_deltanet_core_known_answer():
+    """Hand-derived values pin the order of the delta rule (qw35_ssm.metal:393-428):
+    k_dot and q_dot read the OLD state, delta = (v - gate * k_dot) * beta, the
+    state becomes S * gate + delta (x) k, y = (gate * q_dot + delta * (k . q)) * scale.
+    Head 0 (qk group 0): S = [[1, 0], [0, 2]], k = e0, q = e1, v = (3, 4), beta 1/2,
+    gate 1 (g = 0): k_dot = (1, 0), q_dot = (0, 2), k.q = 0, delta = (1, 2),
+    S' = [[2, 0], [2, 2]], y = (0, 2) * scale.  Head 1 (group 1): S = [[1, 0], [0, 2]],
+    q = k = e0, v = (3, 4), beta 1, gate 1: k_dot = q_dot = (1, 0), k.q = 1,
+    delta = (2, 4), S' = [[3, 0], [4, 2]], y = (1 + 2, 0 + 4) * scale = (3, 4) * scale.
+    Every other entry is zero.  All values are exact in fp32: the match is exact."""
+    q = np.zeros((1, 16, 128), np.float16)
+    k = np.zeros((1, 16, 128), np.float16)
+    v = np.zeros((1, 32, 128), np.float16)
+    S = np.zeros((1, 32, 128, 128), np.float32)
+    beta = np.zeros((1, 32), np.float32)
+    g = np.zeros((1, 32), np.float32)
+    k[0, 0, 0], q[0, 0, 1] = 1, 1
+    k[0, 1, 0], q[0, 1, 0] = 1, 1
+    for h in (0, 1):
+        S[0, h, 0, 0], S[0, h, 1, 1] = 1, 2
+        v[0, h, 0], v[0, h, 1] = 3, 4
+    beta[0, 0], beta[0, 1] = 0.5, 1.0
+    from qwowl35_b200 import ops
+    Sd = torch.from_numpy(S.copy()).cuda()
+    y = ops.deltanet_core(*(torch.from_numpy(a).cuda() for a in (q, k, v, beta, g)), Sd).cpu().numpy()
+    Sn = Sd.cpu().numpy()
+    scale = np.float32(1.0 / np.sqrt(128.0))
+    ey = np.zeros((32, 128), np.float32)
+    ey[0, 1] = np.float32(2) * scale
+    ey[1, 0], ey[1, 1] = np.float32(3) * scale, np.float32(4) * scale
+    eS = np.zeros((32, 128, 128), np.float32)
+    eS[0, :2, :2] = [[2, 0], [2, 2]]
+    eS[1, :2, :2] = [[3, 0], [4, 2]]
+    np.testing.assert_array_equal(y[0], ey)
+    np.testing.assert_array_equal(Sn[0], eS)
+    # the oracle restatement gives the same numbers
+    yr, Sr = O.deltanet_core(S[0], q[0].astype(np.float64), k[0].astype(np.float64), v[0], beta[0], g[0],
+                             float(scale))
+    np.testing.assert_allclose(yr, ey, rtol=0, atol=1e-7)
+    np.testing.assert_array_equal(Sr, eS.astype(np.float64))

@@ -13,8 +13,9 @@
   log-uniform in 512..131072 (the seeded list below), K/V in shuffled
   256-position chunks, against the oracle per sequence.
 
-Tolerance: ``parity.relerr`` < 1e-3 (norm-wise and per element above 1e-3 of
-the largest); argmax ids bit-exact against the argmax of the returned logits
+Tolerance: logits ``parity.modelerr`` < 1e-3 (norm-wise, and per element above
+1e-2 of the largest logit); GQA ``parity.relerr`` < 1e-3 (per element above
+1e-3 of the largest output); argmax ids bit-exact against the argmax of the returned logits
 and equal to the oracle's wherever its top-2 gap exceeds the tolerance.
 """
 from concurrent.futures import ThreadPoolExecutor
@@ -26,7 +27,7 @@ import torch
 from oracle import ops as O
 from oracle import quants as Q
 from oracle.model import OracleModel
-from parity import elemerr, normerr, relerr
+from parity import MODEL_FLOOR, elemerr, modelerr, normerr, relerr
 from qwowl35_b200 import ops, synth
 from qwowl35_b200.runtime import LogitsMode, Runtime
 
@@ -70,8 +71,8 @@ def full():
 
 
 def _check_logits(got, ref, where):
-    e = relerr(got, ref)
-    assert e < TOL, (where, "norm-wise", normerr(got, ref), "per element", elemerr(got, ref))
+    e = modelerr(got, ref)
+    assert e < TOL, (where, "norm-wise", normerr(got, ref), "per element", elemerr(got, ref, MODEL_FLOOR))
     top = np.argsort(ref)[-2:]
     if ref[top[1]] - ref[top[0]] > TOL * np.max(np.abs(ref)):
         assert int(np.argmax(got)) == int(top[1]), where

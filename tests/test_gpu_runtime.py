@@ -1,7 +1,7 @@
 """End-to-end decode through the drop-in C ABI (qw35_metal_* and the batched
 extensions) on a small synthetic model, against the fp64 oracle model."""
 import numpy as np
-from parity import normerr, relerr
+from parity import modelerr as relerr  # decode-step logits (see parity.py)
 import pytest
 
 from oracle.model import OracleModel

@@ -115,3 +115,18 @@ def test_parity_measure_catches_small_row_errors():
     y = ref.copy()
     y[3] *= 2.0  # below the significance floor: norm-wise only
     assert elemerr(y, ref) == 0.0 and relerr(y, ref) < 1e-6
+
+
+def test_deltanet_core_known_answer_two_by_two():
+    """The delta rule on a 2-dimensional head, derived by hand from
+    qw35_ssm.metal:393-428 (k_dot / q_dot from the OLD state; gate 1/2):
+    S = [[1, 0], [0, 2]], k = e0, q = e1, v = (3, 4), beta = 1/2, gate = 1/2:
+    k_dot = (1, 0), q_dot = (0, 2), k.q = 0, delta = (3 - 1/2, 4) / 2 = (1.25, 2),
+    S' = S / 2 + delta (x) k = [[1.75, 0], [2, 1]], y = (gate * q_dot) * scale = (0, 1)."""
+    S = np.array([[[1.0, 0.0], [0.0, 2.0]]])
+    k = np.array([[1.0, 0.0]])
+    q = np.array([[0.0, 1.0]])
+    v = np.array([[3.0, 4.0]])
+    y, Sn = O.deltanet_core(S, q, k, v, np.array([0.5]), np.array([np.log(0.5)]), 1.0)
+    np.testing.assert_allclose(Sn[0], [[1.75, 0.0], [2.0, 1.0]], rtol=0, atol=1e-15)
+    np.testing.assert_allclose(y[0], [0.0, 1.0], rtol=0, atol=1e-15)
