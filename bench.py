@@ -238,6 +238,116 @@ def kernel_table(B: int, ctx: int, device):
 
 
 # ---------------------------------------------------------------------------
+# BASELINE configs 1, 3 and 4 as kernel-level lines (each with its roofline
+# fraction and a CPU-port baseline on a bounded sample)
+# ---------------------------------------------------------------------------
+CONFIG4_LENS = [131072, 512, 114894, 801, 14856, 4129, 43695, 1347, 64324, 10452, 76211, 7217, 5571, 40667,
+                120045, 3977, 110329, 88427, 1371, 14980, 25512, 95448, 20527, 1072, 8095, 7907, 8202, 104175,
+                3564, 1770, 9259, 17921]  # np.random.default_rng(4) log-uniform 512..131072, ends pinned
+
+
+def config_lines(device, peak: float, kind: str):
+    """Config 1: the GF4 12288 x 4096 up-projection at batch 1 (x fp16).
+    Config 3: the DeltaNet recurrent core (prepared q/k/v, beta, log-decay) for
+    1 and 64 sequences.  Config 4: one attention layer's GQA decode over 32
+    sequences of 512..131072 positions in shuffled 256-position chunks.
+    GPU: CUDA events over graph replays of rotating inputs larger than L2.
+    CPU: the numpy oracle port on a sample (rows / sequences), scaled up."""
+    import numpy as np
+    import torch
+
+    from oracle import ops as O
+    from oracle import quants as Q
+    from qwowl35_b200 import ops, synth, sweep
+
+    out = {}
+    cores = cpu_cores()
+    # ---- config 1 -------------------------------------------------------------
+    g = synth._Gen(0, device)
+    pt = sweep.point("gf4", ops.GF4, 12288, 4096, [1], g, device, peak)[0]
+    rng = np.random.default_rng(0)
+    rows_s = 768  # 1/16 of the rows
+    raw = Q.gen_weight(rng, Q.GF4_TYPE, rows_s, 4096)
+    x = rng.standard_normal((1, 4096)).astype(np.float16).astype(np.float32)
+    t0 = time.perf_counter()
+    O.matvec(Q.dequant(Q.GF4_TYPE, raw, rows_s, 4096), x)
+    cpu_s = (time.perf_counter() - t0) * (12288 / rows_s)
+    b1 = 25165824 + 8192 + 49152
+    out["config1"] = {"workload": "GF4 matvec 12288x4096, batch 1, x fp16", "unit": "GB/s",
+                      "value": pt["gbs"], "us": pt["us"], "bytes": b1,
+                      "roofline": {"bound": "hbm", "achieved": pt["gbs"], "peak": peak, "peak_kind": kind,
+                                   "frac": pt["gbs"] / peak},
+                      "cpu_baseline": {"value": b1 / cpu_s / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+                                       "sample": f"{rows_s} of 12288 rows dequantised (metal semantics) and "
+                                                 "multiplied in fp64 numpy, scaled to the whole matrix"}}
+    # ---- config 3 -------------------------------------------------------------
+    per = 4227072  # state R+W + q, k, v + out per sequence-layer
+    rows3 = []
+    for n in (1, 64):
+        q = torch.randn(n, 16, 128, device=device)
+        q = (q / q.norm(dim=-1, keepdim=True)).half()
+        k = torch.randn(n, 16, 128, device=device)
+        k = (k / k.norm(dim=-1, keepdim=True)).half()
+        v = torch.randn(n, 32, 128, device=device).half()
+        beta = torch.sigmoid(torch.randn(n, 32, device=device))
+        gl = -torch.nn.functional.softplus(torch.randn(n, 32, device=device))
+        nst = max(2, (400 << 20) // (n * 32 * 128 * 128 * 4) + 1)
+        states = [torch.randn(n, 32, 128, 128, device=device) * 0.01 for _ in range(min(nst, 64))]
+        fns = [(lambda S=S: ops.deltanet_core(q, k, v, beta, gl, S)) for S in states]
+        us = sweep.graph_us(fns * max(1, 8 // len(fns)))
+        gbs = n * per / us / 1e3
+        rows3.append({"sequences": n, "us": round(us, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 3)})
+        del states
+    rng = np.random.default_rng(3)
+    S = rng.normal(0, 0.01, (32, 128, 128))
+    qq = rng.standard_normal((16, 128))
+    qq /= np.linalg.norm(qq, axis=-1, keepdims=True)
+    t0 = time.perf_counter()
+    O.deltanet_core(S, qq, qq, rng.standard_normal((32, 128)), np.full(32, 0.5), np.full(32, -0.5), 0.0884)
+    cpu3 = time.perf_counter() - t0
+    out["config3"] = {"workload": "Gated DeltaNet recurrent core, one layer, ragged 1..64 sequences",
+                      "unit": "GB/s", "value": rows3[-1]["gbs"], "rows": rows3,
+                      "roofline": {"bound": "hbm", "achieved": rows3[-1]["gbs"], "peak": peak, "peak_kind": kind,
+                                   "frac": rows3[-1]["gbs"] / peak},
+                      "cpu_baseline": {"value": per / cpu3 / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+                                       "sample": "one sequence-layer of the fp64 numpy oracle"}}
+    # ---- config 4 -------------------------------------------------------------
+    lens = CONFIG4_LENS
+    plane = 4 * 256 * 256
+    nch = [(L + 255) // 256 for L in lens]
+    total = sum(nch)
+    pool = torch.randn(total * 2 * plane, device=device).half()
+    perm = np.random.default_rng(44).permutation(total)
+    table = np.zeros((len(lens), max(nch)), dtype=np.int64)
+    i = 0
+    for s_, c in enumerate(nch):
+        for j in range(c):
+            table[s_, j] = pool.data_ptr() + int(perm[i]) * 2 * plane * 2
+            i += 1
+    tab = torch.from_numpy(table).to(device)
+    qd, gd = torch.randn(len(lens), 16, 256, device=device), torch.randn(len(lens), 16, 256, device=device)
+    lens_d = torch.tensor(lens, dtype=torch.int32, device=device)
+    ws = ops.gqa_workspace(len(lens), max(lens), device)
+    o4 = torch.empty(len(lens), 4096, device=device)
+    us4 = sweep.graph_us([lambda: ops.gqa_decode(qd, gd, lens_d, max(lens), tab, 0, plane * 2, ws=ws, out=o4)] * 4)
+    b4 = 4096 * sum(lens) + len(lens) * 16 * 256 * 12
+    del pool
+    Ls = 8192  # CPU sample: one sequence of 8192 positions, scaled by the positions
+    Kc = rng.standard_normal((Ls, 4, 256)).astype(np.float16)
+    t0 = time.perf_counter()
+    O.gqa_decode(rng.standard_normal((16, 256)), rng.standard_normal((16, 256)), Kc, Kc)
+    cpu4 = (time.perf_counter() - t0) * sum(lens) / Ls
+    out["config4"] = {"workload": "GQA decode, one layer, 32 sequences of 512..131072 positions (seed 4)",
+                      "unit": "GB/s", "value": b4 / us4 / 1e3, "us": us4, "bytes": b4,
+                      "roofline": {"bound": "hbm", "achieved": b4 / us4 / 1e3, "peak": peak, "peak_kind": kind,
+                                   "frac": b4 / us4 / 1e3 / peak},
+                      "cpu_baseline": {"value": b4 / cpu4 / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+                                       "sample": f"one sequence of {Ls} positions in fp64 numpy, scaled by positions"}}
+    torch.cuda.empty_cache()
+    return out
+
+
+# ---------------------------------------------------------------------------
 # main
 # ---------------------------------------------------------------------------
 def dist_env():
@@ -533,9 +643,11 @@ def main():
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(ext)
     n1 = min(args.steps, 8)
+    torch.cuda.nvtx.range_push("timed_b1")
     for _ in range(n1):
         rt.eval_batch([0], [1], [pos], LogitsMode.ARGMAX)
         pos += 1
+    torch.cuda.nvtx.range_pop()
     e1.record(ext)
     e1.synchronize()
     b1_s = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, device)
@@ -583,6 +695,10 @@ def main():
                                       "frac_of_8tbs": round(r["gbs"] / 8000.0, 3)} for r in pts]}
         except Exception as exc:  # the GEMV table never blocks the bench line
             line["gemv"] = {"error": str(exc)[:200]}
+        try:
+            line["configs"] = config_lines(device, peak, kind)
+        except Exception as exc:
+            line["configs"] = {"error": str(exc)[:200]}
     if rank == 0 and world == 1 and not args.no_cpu:
         ref = RefSample(B, args.ctx_fill)
         head = ref.head_slice()

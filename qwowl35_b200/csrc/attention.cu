@@ -38,7 +38,8 @@ constexpr int ASTG = 3;     // cp.async stages per warp in the split kernel (8 p
 constexpr size_t ASMEM = (size_t)4 * ASTG * 2 * 8 * 32 * 16;  // 48 KiB of K/V staging per CTA
 // q8_0 planes: per warp a ring of raw q8_0 rows plus one dequantised f16 stage
 constexpr size_t ARAWQ8 = (size_t)ASTG * 2 * 8 * kKvQ8Row;             // 13,056 B
-constexpr size_t ASMEM_Q8 = (size_t)4 * (ARAWQ8 + 2 * 8 * 32 * 16);    // 84,992 B
+constexpr size_t AQ8D = 16 * 8 * 4;                                     // block scales [16 rows][8 blocks] f32
+constexpr size_t ASMEM_Q8 = (size_t)4 * (ARAWQ8 + 2 * 8 * 32 * 16 + AQ8D);  // 87,040 B
 
 // One q8_0 block of 32 values held 8 per lane by 4 consecutive lanes (lane % 4
 // = the lane's quarter): qw35_q8_0_quantize_block (qw35_attention.metal:429-440).
@@ -212,11 +213,13 @@ __device__ __forceinline__ void split_h2(float a, float b, uint32_t &hi, uint32_
 // g for heads 2t, 2t+1 and O^T rows (dims) 16 j + g, + 8 for the same heads;
 // lanes with t >= 2 carry the padding.
 // Q8: the planes hold q8_0 rows (272 B per head-row); each warp stages the raw
-// rows with cp.async and, per step, turns them into the same swizzled f16
-// tile (half(d * q): the exact product rounded once), so the MMA core is
-// unchanged.  The reference computes these products in fp32
-// (qw35_attention.metal:665-682); the half rounding stays far inside the
-// 1e-3 bar.
+// rows with cp.async and, per step, turns the codes into the same swizzled f16
+// tile (the int8 codes, exact in half) and the block scales d into a small
+// f32 table.  The scale goes in after the MMA, in fp32, as the reference
+// computes d * q (qw35_attention.metal:665-682): scores accumulate per 32-dim
+// block (two k-steps) and add d_K * block sum; for the values, each 32-dim
+// block b multiplies P by d_V[position][b] before it is split into the f16
+// hi / lo operand.
 template <bool Q8>
 __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_max) {
     const int split = blockIdx.x, kvh = blockIdx.y, seq = blockIdx.z;
@@ -262,9 +265,10 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_
     // distinct bank groups (cp.async, zero-filled past i1).
     extern __shared__ __align__(16) uint4 ring[];  // [4 warps][ASTG][2][8 rows][32 pieces]
     // (Q8: [4 warps] x {raw [ASTG][2][8 rows][272 B], f16 tile [2][8 rows][32 pieces]})
-    uint4 *wring = Q8 ? ring + (size_t)wid * ((ARAWQ8 + 2 * 8 * 32 * 16) / 16) : ring + (size_t)wid * ASTG * 2 * 8 * 32;
+    uint4 *wring = Q8 ? ring + (size_t)wid * ((ARAWQ8 + 2 * 8 * 32 * 16 + AQ8D) / 16) : ring + (size_t)wid * ASTG * 2 * 8 * 32;
     uint8_t *wraw = reinterpret_cast<uint8_t *>(wring);
     uint4 *wtile = wring + ARAWQ8 / 16;
+    float *wdsc = reinterpret_cast<float *>(wtile + 2 * 8 * 32);  // [16 rows: K 0-7, V 8-15][8 blocks]
     auto issue = [&](int ib, int stage) {
         if constexpr (Q8) {
             // 2 x 8 rows of 17 16-byte pieces; pieces past i1 are zero-filled
@@ -315,22 +319,24 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_
         __syncwarp();
         const uint4 *ks = wring + (size_t)stage * 2 * 8 * 32;
         if constexpr (Q8) {
-            // raw rows -> f16 tile: lane = 16-byte piece (dims 8 lane .. +7) = quarter
-            // lane % 4 of block lane / 4; q + 1152 - 1152 in half is exact, times
-            // the block's half d in one HMUL2 (the exact product rounded once)
+            // raw rows -> f16 code tile: lane = 16-byte piece (dims 8 lane .. +7) =
+            // quarter lane % 4 of block lane / 4; q + 1152 - 1152 in half is exact;
+            // the block's d goes to the f32 table
             const uint8_t *rs = wraw + (size_t)stage * 2 * 8 * kKvQ8Row + 34 * (lane >> 2);
             const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6480));  // 1152
 #pragma unroll
             for (int kr = 0; kr < 16; ++kr) {  // K rows 0-7, then V rows 0-7
                 const uint8_t *blk = rs + kr * kKvQ8Row;
-                const __half2 d2 = __half2half2(__ushort_as_half(*reinterpret_cast<const unsigned short *>(blk)));
+                if ((lane & 3) == 0)
+                    wdsc[kr * 8 + (lane >> 2)] =
+                        __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(blk)));
                 const unsigned short *qd = reinterpret_cast<const unsigned short *>(blk + 2 + 8 * (lane & 3));
                 uint32_t hw[4];
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
                     const uint32_t two = (uint32_t)qd[u] ^ 0x8080u;  // biased codes q + 128
                     const uint32_t v = __byte_perm(two, 0x64646464u, 0x4140u);  // halves 1024 + (q + 128)
-                    const __half2 h = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&v), off), d2);
+                    const __half2 h = __hsub2(*reinterpret_cast<const __half2 *>(&v), off);
                     hw[u] = *reinterpret_cast<const uint32_t *>(&h);
                 }
                 const int r = kr & 7;
@@ -344,18 +350,38 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_
         // S^T (16 x 8) = K (16 x 256) Q^T (256 x 8): A rows = positions (rows 8-15 repeat 0-7)
         // four independent accumulators (q hi / lo x even / odd k-step) keep four
         // MMA chains in flight instead of one 32-long dependent chain
-        float acc4[4][4] = {};
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            uint32_t a[4];
-            const int c = 2 * j + ((lane >> 4) & 1);  // matrices 2, 3: dims + 8
-            ldsm_x4(a, ks + lr * 32 + (c ^ lr));
-            mma16816(acc4[j & 1], a, qh[j][0], qh[j][1]);
-            mma16816(acc4[2 + (j & 1)], a, ql[j][0], ql[j][1]);
-        }
         float sc[4];
+        if constexpr (Q8) {
+            // per 32-dim block: codes x q over two k-steps, then + d_K[row g][block] * sum
+            sc[0] = sc[1] = sc[2] = sc[3] = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) sc[i] = (acc4[0][i] + acc4[1][i]) + (acc4[2][i] + acc4[3][i]);
+            for (int b = 0; b < 8; ++b) {
+                float ah[4] = {}, al[4] = {};
+#pragma unroll
+                for (int j = 2 * b; j < 2 * b + 2; ++j) {
+                    uint32_t a[4];
+                    const int c = 2 * j + ((lane >> 4) & 1);
+                    ldsm_x4(a, ks + lr * 32 + (c ^ lr));
+                    mma16816(ah, a, qh[j][0], qh[j][1]);
+                    mma16816(al, a, ql[j][0], ql[j][1]);
+                }
+                const float d = wdsc[g * 8 + b];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sc[i] = fmaf(d, ah[i] + al[i], sc[i]);
+            }
+        } else {
+            float acc4[4][4] = {};
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                uint32_t a[4];
+                const int c = 2 * j + ((lane >> 4) & 1);  // matrices 2, 3: dims + 8
+                ldsm_x4(a, ks + lr * 32 + (c ^ lr));
+                mma16816(acc4[j & 1], a, qh[j][0], qh[j][1]);
+                mma16816(acc4[2 + (j & 1)], a, ql[j][0], ql[j][1]);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sc[i] = (acc4[0][i] + acc4[1][i]) + (acc4[2][i] + acc4[3][i]);
+        }
         // online softmax of heads 2t, 2t+1 over this step's 8 positions (lane rows g)
         const bool valid = ib + g < i1;
         const float sa = valid ? sc[0] : -INFINITY, sb = valid ? sc[1] : -INFINITY;
@@ -393,16 +419,36 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_
         const float x1a = __shfl_sync(0xffffffffu, pa, src1), x1b = __shfl_sync(0xffffffffu, pb, src1);
         const float p0 = g < AGRP ? ((g & 1) ? x0b : x0a) : 0.0f;
         const float p1 = g < AGRP ? ((g & 1) ? x1b : x1a) : 0.0f;
-        uint32_t ph, pl;
-        split_h2(p0, p1, ph, pl);
         // O^T (256 x 8) += V^T (256 x 16) P^T (16 x 8): positions 8-15 have p = 0
+        if constexpr (Q8) {
+            // dims block b = j / 2: P rows (positions 2t, 2t+1) times d_V[position][b],
+            // times 2^8 so small products keep their bits in the f16 hi / lo halves
+            // (the partials are scaled back below)
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            uint32_t a[4];
-            const int c = 2 * j + ((lane >> 3) & 1);  // matrices 1, 3: dims + 8
-            ldsm_x4_t(a, vs + lr * 32 + (c ^ lr));
-            mma16816(o[j], a, ph, 0u);
-            mma16816(o[j], a, pl, 0u);
+            for (int b = 0; b < 8; ++b) {
+                uint32_t ph, pl;
+                split_h2(p0 * (wdsc[(8 + 2 * t4) * 8 + b] * 256.0f), p1 * (wdsc[(9 + 2 * t4) * 8 + b] * 256.0f), ph,
+                         pl);
+#pragma unroll
+                for (int j = 2 * b; j < 2 * b + 2; ++j) {
+                    uint32_t a[4];
+                    const int c = 2 * j + ((lane >> 3) & 1);
+                    ldsm_x4_t(a, vs + lr * 32 + (c ^ lr));
+                    mma16816(o[j], a, ph, 0u);
+                    mma16816(o[j], a, pl, 0u);
+                }
+            }
+        } else {
+            uint32_t ph, pl;
+            split_h2(p0, p1, ph, pl);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                uint32_t a[4];
+                const int c = 2 * j + ((lane >> 3) & 1);  // matrices 1, 3: dims + 8
+                ldsm_x4_t(a, vs + lr * 32 + (c ^ lr));
+                mma16816(o[j], a, ph, 0u);
+                mma16816(o[j], a, pl, 0u);
+            }
         }
         __syncwarp();  // the stage may be refilled by the next iteration's issue
         if (++stage == ASTG) stage = 0;
@@ -414,12 +460,13 @@ __global__ void __launch_bounds__(128) attn_split_kernel(AttnArgs p, int nsplit_
         wl[wid][2 * t4] = la; wl[wid][2 * t4 + 1] = lb;
     }
     if (t4 < 2) {
+        constexpr float osc = Q8 ? 1.0f / 256.0f : 1.0f;  // Q8: undo the 2^8 of the value operand
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-            wacc[wid][2 * t4][16 * j + g] = o[j][0];
-            wacc[wid][2 * t4 + 1][16 * j + g] = o[j][1];
-            wacc[wid][2 * t4][16 * j + g + 8] = o[j][2];
-            wacc[wid][2 * t4 + 1][16 * j + g + 8] = o[j][3];
+            wacc[wid][2 * t4][16 * j + g] = o[j][0] * osc;
+            wacc[wid][2 * t4 + 1][16 * j + g] = o[j][1] * osc;
+            wacc[wid][2 * t4][16 * j + g + 8] = o[j][2] * osc;
+            wacc[wid][2 * t4 + 1][16 * j + g + 8] = o[j][3] * osc;
         }
     }
     __syncthreads();

@@ -12,6 +12,7 @@
 // retires the conv-state shift only after a cluster barrier.  Every state
 // byte is on a coalesced 512-byte row walk, issued at kernel entry.
 #include <cooperative_groups.h>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "ops.h"
@@ -151,6 +152,99 @@ deltanet_step_kernel(DeltaNetArgs p) {
         const float z = proj[ZOFF + h * DS + tid];
         p.out[(size_t)seq * p.out_stride + h * DS + tid] = y_s[tid] * inv * p.norm_w[tid] * silu_f(z);
     }
+}
+
+// ---- small batches: a value head split over four CTAs ---------------------------
+// With few sequences the one-CTA-per-head layout leaves most SMs idle (32 CTAs
+// for one sequence).  Here a cluster of 8 CTAs covers the two heads of a qk
+// group x four quarters of their 128 state rows (128 threads, 32 rows each):
+// every CTA recomputes the group's q / k conv and norms (256 channels), the
+// quarter's v rows and their window shift are its own, rank 0 retires the q / k
+// window shift after a cluster barrier, and the per-head RMS of y is summed
+// over the four quarters through distributed shared memory in a fixed order.
+__global__ void __cluster_dims__(8, 1, 1) __launch_bounds__(128)
+deltanet_step_quarter_kernel(DeltaNetArgs p) {
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int)cluster.block_rank();  // head half (rank / 4), row quarter (rank % 4)
+    const int g = blockIdx.y;
+    const int seq = blockIdx.z;
+    const int h = g + NQK * (rank >> 2);
+    const int qr = rank & 3;
+    const int tid = threadIdx.x;
+    const long long slot = p.slots ? (long long)p.slots[seq] : (long long)seq;
+
+    __shared__ __align__(16) float qn_s[DS];
+    __shared__ __align__(16) float kn_s[DS];
+    __shared__ float v_s[ROWS];
+    __shared__ float y_s[ROWS];
+    __shared__ float red[32];
+    __shared__ float ysq;
+
+    const float *proj = p.proj + (size_t)seq * p.proj_stride;
+    float *cs = p.conv_state + slot * p.conv_stride;
+    float *S = p.ssm_state + slot * p.ssm_stride + (size_t)h * DS * DS + (size_t)qr * ROWS * DS;
+
+    float4 sv[8];
+    load_rows(S, sv);  // 4 warps x 8 rows of this quarter
+
+    // (1) conv + SiLU: thread d computes q and k channel d of the group; threads
+    // 0..31 the quarter's value channels (their window shifts right away)
+    const int qc = g * DS + tid, kc = NQK * DS + g * DS + tid;
+    const float qw0 = cs[qc * 3 + 0], qw1 = cs[qc * 3 + 1], qw2 = cs[qc * 3 + 2], qx = proj[qc];
+    const float kw0 = cs[kc * 3 + 0], kw1 = cs[kc * 3 + 1], kw2 = cs[kc * 3 + 2], kx = proj[kc];
+    const float4 wq = reinterpret_cast<const float4 *>(p.conv_w)[qc];
+    const float4 wk = reinterpret_cast<const float4 *>(p.conv_w)[kc];
+    const float q = silu_f(qw0 * wq.x + qw1 * wq.y + qw2 * wq.z + qx * wq.w);
+    const float k = silu_f(kw0 * wk.x + kw1 * wk.y + kw2 * wk.z + kx * wk.w);
+    if (tid < ROWS) {
+        const int vc = 2 * NQK * DS + h * DS + qr * ROWS + tid;
+        const float v0 = cs[vc * 3 + 0], v1 = cs[vc * 3 + 1], v2 = cs[vc * 3 + 2], vx = proj[vc];
+        const float4 wv = reinterpret_cast<const float4 *>(p.conv_w)[vc];
+        v_s[tid] = silu_f(v0 * wv.x + v1 * wv.y + v2 * wv.z + vx * wv.w);
+        cs[vc * 3 + 0] = v1;
+        cs[vc * 3 + 1] = v2;
+        cs[vc * 3 + 2] = vx;
+    }
+
+    // (2) L2 norms with max(norm, eps) and the normalised k.q dot
+    const float q_ss = block_sum(q * q, red);
+    const float k_ss = block_sum(k * k, red);
+    qn_s[tid] = q * (1.0f / fmaxf(sqrtf(q_ss), p.eps));
+    kn_s[tid] = k * (1.0f / fmaxf(sqrtf(k_ss), p.eps));
+    __syncthreads();
+    const float kq = block_sum(qn_s[tid] * kn_s[tid], red);
+
+    // every CTA of the cluster has read the old q/k window: rank 0 retires the shift
+    cluster.sync();
+    if (rank == 0) {
+        cs[qc * 3 + 0] = qw1; cs[qc * 3 + 1] = qw2; cs[qc * 3 + 2] = qx;
+        cs[kc * 3 + 0] = kw1; cs[kc * 3 + 1] = kw2; cs[kc * 3 + 2] = kx;
+    }
+
+    // (3) gates and the delta-rule update of the quarter's 32 rows
+    const float beta = sigmoid_f(proj[BOFF + h]);
+    const float gate = expf(softplus_f(proj[AOFF + h] + p.dt[h]) * p.a[h]);
+    const int lane = tid & 31;
+    const float4 kc4 = reinterpret_cast<const float4 *>(kn_s)[lane];
+    const float4 qc4 = reinterpret_cast<const float4 *>(qn_s)[lane];
+    delta_rows(S, sv, kc4, qc4, v_s, gate, beta, kq, 0.08838834764831845f, y_s);
+    __syncthreads();
+
+    // (4) the head's RMS of y: the four quarters' sums of squares, in rank order
+    const float y2 = block_sum(tid < ROWS ? y_s[tid] * y_s[tid] : 0.0f, red);
+    if (tid == 0) ysq = y2;
+    cluster.sync();
+    float tot = 0.0f;
+    const int r0 = rank & 4;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) tot += *cluster.map_shared_rank(&ysq, r0 + i);
+    const float inv = rsqrtf(tot / (float)DS + p.eps);
+    if (tid < ROWS) {
+        const int d = qr * ROWS + tid;
+        const float z = proj[ZOFF + h * DS + d];
+        p.out[(size_t)seq * p.out_stride + h * DS + d] = y_s[tid] * inv * p.norm_w[d] * silu_f(z);
+    }
+    cluster.sync();  // the other CTAs' reads of ysq are done before this CTA exits
 }
 
 // ---- a run of T tokens of one sequence (prefill) ------------------------------
@@ -297,6 +391,11 @@ __global__ void __launch_bounds__(128) deltanet_core_kernel(DeltaCoreArgs p) {
 cudaError_t deltanet_step_run(const DeltaNetArgs &a, cudaStream_t st) {
     if (a.n_seq <= 0) return cudaSuccess;
     if (a.n_seq > 65535) return cudaErrorInvalidValue;
+    if (a.n_seq <= 4) {
+        // few sequences: four CTAs per head fill the SMs (cluster of 8 per qk group)
+        deltanet_step_quarter_kernel<<<dim3(8, NQK, a.n_seq), 128, 0, st>>>(a);
+        return cudaGetLastError();
+    }
     dim3 grid(2, NQK, a.n_seq);
     deltanet_step_kernel<<<grid, 512, 0, st>>>(a);
     return cudaGetLastError();

@@ -79,7 +79,7 @@ void *create(const void *map, uint64_t size, const qw35_metal_tensor_desc *tenso
     }
     try {
         auto ms = qw35::shared_model(map, size, tensors, count, *hp, vocab);
-        Runtime *rt = qw35::create_runtime(ms, ctx, vocab, prefill_chunk, max_seqs, kv_type);
+        Runtime *rt = qw35::create_runtime(ms, *hp, ctx, vocab, prefill_chunk, max_seqs, kv_type);
         std::lock_guard<std::mutex> g(g_mu);
         g_live.insert(rt);
         return rt;

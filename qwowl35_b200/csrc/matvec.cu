@@ -195,11 +195,8 @@ __device__ __forceinline__ int mv_scatter_index(int lane) {
 template <int CODEC, int MODE> constexpr int rows_per_warp() {
     return CODEC == QW35_GF4_TYPE ? (MODE == 2 ? 2 : 4) : (MODE == 2 ? 1 : 2);
 }
-// Consumer warps per CTA: two activation rows keep twice the registers resident
-#ifndef MV_WARPS_B1
-#define MV_WARPS_B1 12
-#endif
-template <int B> constexpr int mv_max_warps() { return B == 1 ? MV_WARPS_B1 : 12; }
+// Consumer warps per CTA (at most; Q8_0 takes 8 where it can, see mv_geometry)
+template <int B> constexpr int mv_max_warps() { return 12; }
 // 32-column chunks each consumer lane owns (its activations stay in registers):
 // two for batch-1 GF4, which halves the per-row reduction work per weight
 template <int CODEC, int B> constexpr int mv_lane_chunks() { return 1; }
@@ -210,7 +207,7 @@ template <int CODEC, int B> constexpr int mv_lane_chunks() { return 1; }
 // row it handles (no stage-wide barrier); the rows are summed in a fixed order
 // and written once, after the last stage.
 template <int CODEC, int B, int MODE, bool EXACT, typename XT>
-__global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, mv_max_warps<B>() <= 8 ? 2 : 1) mv_kernel(MvParams p) {
+__global__ void __launch_bounds__((mv_max_warps<B>() + 1) * 32, 1) mv_kernel(MvParams p) {
     constexpr int NM = MODE == MV_SWIGLU ? 2 : 1;
     constexpr int NC = Codec<CODEC>::NC;
     extern __shared__ __align__(128) uint8_t smem[];
@@ -548,8 +545,10 @@ static MvGeom mv_geometry(int rows, int K, const void *kern) {
     codec_rows(CODEC, K, g.code_row, g.scale_row);
     const uint32_t rb = g.code_row + g.scale_row;
     if (CODEC == QW35_GF4_TYPE || CODEC == QW35_Q8_0_TYPE) {
-        // up to mv_max_warps consumer warps, each with gf4_rows_per_warp rows of a stage in flight
-        constexpr int CW = mv_max_warps<B>();
+        // up to mv_max_warps consumer warps, each with rows_per_warp rows of a stage
+        // in flight; Q8_0 (80 registers) takes 8 where its K allows, so two CTAs
+        // share an SM (measured: 12352 x 4096 11.8 -> 10.9 us, head 174 -> 159 us)
+        const int CW = (CODEC == QW35_Q8_0_TYPE && g.kw <= 8) ? 8 : mv_max_warps<B>();
         g.rs = g.kw >= CW ? 1 : CW / g.kw;
         g.G = rows_per_warp<CODEC, MODE>() * g.rs;
     } else {

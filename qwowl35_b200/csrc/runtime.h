@@ -167,8 +167,8 @@ std::shared_ptr<ModelStore> load_model(const void *map, uint64_t map_size, const
                                        uintptr_t n, const qw35_metal_hparams &hp, uint32_t vocab);
 std::shared_ptr<ModelStore> shared_model(const void *map, uint64_t map_size, const qw35_metal_tensor_desc *descs,
                                          uintptr_t n, const qw35_metal_hparams &hp, uint32_t vocab);
-Runtime *create_runtime(std::shared_ptr<ModelStore> ms, uint32_t ctx, uint32_t vocab, uint32_t prefill_chunk,
-                        uint32_t max_seqs, uint32_t kv_type = 0);
+Runtime *create_runtime(std::shared_ptr<ModelStore> ms, const qw35_metal_hparams &hp, uint32_t ctx, uint32_t vocab,
+                        uint32_t prefill_chunk, uint32_t max_seqs, uint32_t kv_type = 0);
 void rt_enqueue_step(Runtime *rt, uint32_t n, const uint32_t *seq_ids, const uint32_t *tokens,
                      const uint32_t *pos, int mode);
 // tokens[0..len) of one sequence at positions pos0.. as one pass (len <= rt->rows);

