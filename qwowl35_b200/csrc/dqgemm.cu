@@ -116,13 +116,14 @@ template <int CODEC, int NP, bool JK> struct DqTmem {
     static_assert(2 * RC <= A0, "TMEM plan");
 };
 
-// ---- decode of one 16-byte chunk of a weight row into 8 halves --------------------
-// GF4: one word -> 8 halves in k order [0,4,1,5,2,6,3,7] (the activation prep
-// applies the same permutation inside every 8-column group, so the dot is
-// unchanged).  Values: (q_raw - 4) * (-0.25 * s), exact in f16; in metal mode
-// element 4 is half(float(q4 * 8192 + junk) * s * -0.25 * 2^-13), the
-// reference's tiled-path rounding.
-// Halves of one word, without the Metal element-4 junk (that is added by
+// ---- GF4 decode into halves ---------------------------------------------------------
+// Values: (q_raw - 4) * (-0.25 * s), exact in f16.  The main path decodes two
+// words at a time (gf4_pair_levels) with the element-4 junk in its own tile;
+// words with a scale past 252 take the per-word decode below, where metal mode
+// rounds element 4 as half(float(q4 * 8192 + junk) * s * -0.25 * 2^-13), the
+// reference's tiled-path rounding.  The activation prep applies the matching
+// column order to every 16 columns, so the dot is unchanged.
+// Halves of one word in k order [0,4,1,5,2,6,3,7], without the Metal element-4 junk (that is added by
 // gf4_pair_to_halves below, two words at a time).  No conversion-unit (XU)
 // instructions: the range check is an integer compare on the half bits.
 __device__ __forceinline__ uint4 gf4_word_levels(uint32_t w, uint32_t &scbits) {
@@ -179,60 +180,6 @@ __device__ __forceinline__ void gf4_pair_to_halves(uint32_t w0, uint32_t w1, uin
     }
 }
 
-// Fast path for one word whose |s| <= 252.  The codes of pair i sit (in
-// `packed`, two halves) at bits 4+3i; shifted down to bits 4-6 they are OR-ed
-// into the mantissa of 1024 with one LOP3: h = 1024 + 16 q_raw.  Then
-// (q_raw - 4) * (-0.25 s) = h * (-s/64) + 17 s in one HFMA2: exact, since
-// -s/64 and 17 s are exact in half for every such s (subnormal s included)
-// and the exact result is representable.  In Metal mode element 4 (high half
-// of pair 0) then gains junk * s * -0.25 * 2^-13 = (junk * 2^-9) * (-s/64)
-// through one more HFMA2 whose low lane adds 0: the exact value rounded once,
-// the reference's half(float(int16 * s')).
-template <bool EXACT>
-__device__ __forceinline__ uint4 gf4_word_fast(uint32_t w) {
-    const uint32_t packed = (w & 0xfff00000u) | ((w >> 4) & 0x0000fff0u);  // codes i | i+4 16 bits apart
-    const uint32_t hs = __byte_perm(w, 0u, 0x0404u);  // {s, s} as half2
-    const __half2 s2 = *reinterpret_cast<const __half2 *>(&hs);
-    const __half2 m16 = __hmul2(s2, __half2half2(__ushort_as_half((unsigned short)0xA400)));  // -s/64
-    const __half2 a16 = __hmul2(s2, __half2half2(__ushort_as_half((unsigned short)0x4C40)));  // 17 s
-    const uint32_t v0 = (packed & 0x00700070u) ^ 0x64406440u;  // 1024 + 16 q_raw
-    const uint32_t v1 = ((packed >> 3) & 0x00700070u) ^ 0x64406440u;
-    const uint32_t v2 = ((packed >> 6) & 0x00700070u) ^ 0x64406440u;
-    const uint32_t v3 = ((packed >> 9) & 0x00700070u) ^ 0x64406440u;
-    __half2 h0 = __hfma2(*reinterpret_cast<const __half2 *>(&v0), m16, a16);
-    const __half2 h1 = __hfma2(*reinterpret_cast<const __half2 *>(&v1), m16, a16);
-    const __half2 h2 = __hfma2(*reinterpret_cast<const __half2 *>(&v2), m16, a16);
-    const __half2 h3 = __hfma2(*reinterpret_cast<const __half2 *>(&v3), m16, a16);
-    if (!EXACT) {
-        // {+0, 2 + junk * 2^-9} - {0, 2}: the junk (w bits 11-19) in the high lane
-        const uint32_t jb = ((w << 5) & 0x01ff0000u) | 0x40000000u;
-        const __half2 j = __hsub2(*reinterpret_cast<const __half2 *>(&jb),
-                                  __halves2half2(__ushort_as_half((unsigned short)0x0000),
-                                                 __ushort_as_half((unsigned short)0x4000)));
-        h0 = __hfma2(j, m16, h0);
-    }
-    return make_uint4(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1),
-                      *reinterpret_cast<const uint32_t *>(&h2), *reinterpret_cast<const uint32_t *>(&h3));
-}
-
-// Four words (one 16-byte piece of a weight row) -> four 8-half outputs.  The
-// fast path is taken when all four scales have |s| <= 252 (e5m2 byte & 0x7f
-// <= 0x5B), checked at once: adding 0x24 to each byte sets its top bit
-// exactly when the byte exceeds 0x5B.  Realistic scales never leave it.
-template <bool EXACT>
-__device__ __forceinline__ void gf4_quad_to_halves(const uint4 w4, uint4 &o0, uint4 &o1, uint4 &o2, uint4 &o3) {
-    const uint32_t sb = __byte_perm(__byte_perm(w4.x, w4.y, 0x0040u), __byte_perm(w4.z, w4.w, 0x0040u), 0x5410u);
-    if ((((sb & 0x7f7f7f7fu) + 0x24242424u) & 0x80808080u) == 0u) {
-        o0 = gf4_word_fast<EXACT>(w4.x);
-        o1 = gf4_word_fast<EXACT>(w4.y);
-        o2 = gf4_word_fast<EXACT>(w4.z);
-        o3 = gf4_word_fast<EXACT>(w4.w);
-    } else {
-        gf4_pair_to_halves<EXACT>(w4.x, w4.y, o0, o1);
-        gf4_pair_to_halves<EXACT>(w4.z, w4.w, o2, o3);
-    }
-}
-
 // The junk of a word as the two halves of the junk tile (see dq_junk):
 // {(junk & 31) * s * -2^-5, (junk >> 5) * 32 * s * -2^-5}, i.e. the word's
 // element-4 junk s * -0.25 * 2^-13 * junk times 2^10, split so both parts are
@@ -251,26 +198,71 @@ __device__ __forceinline__ uint32_t gf4_junk_halves(uint32_t w) {
     return *reinterpret_cast<const uint32_t *>(&j);
 }
 
-// Four words for the metal-mode tiles with the junk apart: exact levels into
-// o0..o3 and the junk halves into j[0..3]; words of a quad with a scale past
-// 252 keep the tiled-path rounding of element 4 instead (junk halves zero).
-__device__ __forceinline__ void gf4_quad_levels_junk(const uint4 w4, uint4 &o0, uint4 &o1, uint4 &o2, uint4 &o3,
-                                                     uint32_t *j) {
-    const uint32_t sb = __byte_perm(__byte_perm(w4.x, w4.y, 0x0040u), __byte_perm(w4.z, w4.w, 0x0040u), 0x5410u);
-    if ((((sb & 0x7f7f7f7fu) + 0x24242424u) & 0x80808080u) == 0u) {
-        o0 = gf4_word_fast<true>(w4.x);
-        o1 = gf4_word_fast<true>(w4.y);
-        o2 = gf4_word_fast<true>(w4.z);
-        o3 = gf4_word_fast<true>(w4.w);
-        j[0] = gf4_junk_halves(w4.x);
-        j[1] = gf4_junk_halves(w4.y);
-        j[2] = gf4_junk_halves(w4.z);
-        j[3] = gf4_junk_halves(w4.w);
-    } else {
-        gf4_pair_to_halves<false>(w4.x, w4.y, o0, o1);
-        gf4_pair_to_halves<false>(w4.z, w4.w, o2, o3);
-        j[0] = j[1] = j[2] = j[3] = 0u;
+// Two words of a row (16 columns, A then B) -> 8 exact level half2s in the
+// K order [A0,A5, A1,A6, A2,A7, B0,B5, B1,B6, B2,B7, A3,B3, A4,B4] (the
+// activation prep applies the same order to every 16 columns).  Fewer logic
+// ops than one word at a time: codes 0-2 and 5-7 of a word sit in the low
+// and high half mantissas of w >> 7 at bits p = (1,0), (4,3), (7,6); codes 3
+// and 4 of both words sit at bits 1 and 4 of one PRMT of the words' high
+// halves.  Each lane's exponent is set to E = 10 - p, so one LOP3 (mask, flip
+// of code bit 2, exponent) leaves h = 2^E + q' (q' = q_raw ^ 4) exactly, and
+// (q' - 4) * (-s/4) = h * (-s/4) + s * (1 + 2^(E-2)) in one HFMA2: exact, as
+// -s/4, s * (1 + 2^(E-2)) (<= 11 significant bits, <= 257 * 252) and the
+// result are halves.  Requires |s| <= 252 for both words.
+#define QW35_GF4_KL(E, p) ((uint32_t)(((E) + 15) << 10) | (4u << (p)))
+#define QW35_GF4_K2(El, pl, Eh, ph) (QW35_GF4_KL(El, pl) | (QW35_GF4_KL(Eh, ph) << 16))
+#define QW35_GF4_M2(pl, ph) ((7u << (pl)) | (7u << (16 + (ph))))
+__device__ __forceinline__ void gf4_pair_levels(uint32_t wA, uint32_t wB, uint32_t *o) {
+    auto hu = [](__half2 h) { return *reinterpret_cast<uint32_t *>(&h); };
+    auto uh = [](uint32_t u) { return *reinterpret_cast<__half2 *>(&u); };
+    auto hc = [](unsigned short lo, unsigned short hi) {
+        return __halves2half2(__ushort_as_half(lo), __ushort_as_half(hi));
+    };
+    const uint32_t hsA = __byte_perm(wA, 0u, 0x0404u), hsB = __byte_perm(wB, 0u, 0x0404u);  // {s, s}
+    const __half2 q4 = __half2half2(__ushort_as_half((unsigned short)0xB400));              // -0.25
+    const uint32_t ws[2] = {wA, wB}, hs[2] = {hsA, hsB};
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const uint32_t t = ws[i] >> 7;
+        const __half2 s2 = uh(hs[i]);
+        const __half2 m = __hmul2(s2, q4);
+        const uint32_t v0 = (t & QW35_GF4_M2(1, 0)) ^ QW35_GF4_K2(9, 1, 10, 0);
+        const uint32_t v1 = (t & QW35_GF4_M2(4, 3)) ^ QW35_GF4_K2(6, 4, 7, 3);
+        const uint32_t v2 = (t & QW35_GF4_M2(7, 6)) ^ QW35_GF4_K2(3, 7, 4, 6);
+        o[3 * i + 0] = hu(__hfma2(uh(v0), m, __hmul2(s2, hc(0x5808, 0x5C04))));  // 129, 257
+        o[3 * i + 1] = hu(__hfma2(uh(v1), m, __hmul2(s2, hc(0x4C40, 0x5020))));  // 17, 33
+        o[3 * i + 2] = hu(__hfma2(uh(v2), m, __hmul2(s2, hc(0x4200, 0x4500))));  // 3, 5
     }
+    const uint32_t x = __byte_perm(wA, wB, 0x7632u);  // bits 16-31 of A | of B
+    const __half2 sAB = uh(__byte_perm(hsA, hsB, 0x5410u));
+    const __half2 mAB = __hmul2(sAB, q4);
+    const uint32_t v3 = (x & QW35_GF4_M2(1, 1)) ^ QW35_GF4_K2(9, 1, 9, 1);
+    const uint32_t v4 = (x & QW35_GF4_M2(4, 4)) ^ QW35_GF4_K2(6, 4, 6, 4);
+    o[6] = hu(__hfma2(uh(v3), mAB, __hmul2(sAB, hc(0x5808, 0x5808))));  // 129
+    o[7] = hu(__hfma2(uh(v4), mAB, __hmul2(sAB, hc(0x4C40, 0x4C40))));  // 17
+}
+
+// The same 16 columns from the per-word decode (any scale; [0,4,1,5,2,6,3,7]
+// order per word), rearranged into the order of gf4_pair_levels.
+template <bool EXACT>
+__device__ __forceinline__ void gf4_pair_any(uint32_t wA, uint32_t wB, uint32_t *o) {
+    uint4 a, b;
+    gf4_pair_to_halves<EXACT>(wA, wB, a, b);
+    o[0] = __byte_perm(a.x, a.y, 0x7610u);  // A0, A5
+    o[1] = __byte_perm(a.y, a.z, 0x7610u);  // A1, A6
+    o[2] = __byte_perm(a.z, a.w, 0x7610u);  // A2, A7
+    o[3] = __byte_perm(b.x, b.y, 0x7610u);
+    o[4] = __byte_perm(b.y, b.z, 0x7610u);
+    o[5] = __byte_perm(b.z, b.w, 0x7610u);
+    o[6] = __byte_perm(a.w, b.w, 0x5410u);  // A3, B3
+    o[7] = __byte_perm(a.x, b.x, 0x7632u);  // A4, B4
+}
+
+// true when every scale of a 16-byte piece has |s| <= 252 (e5m2 & 0x7f <=
+// 0x5B): adding 0x24 to each masked byte sets its top bit exactly past 0x5B
+__device__ __forceinline__ bool gf4_scales_small(const uint4 a) {
+    const uint32_t sb = __byte_perm(__byte_perm(a.x, a.y, 0x0040u), __byte_perm(a.z, a.w, 0x0040u), 0x5410u);
+    return (((sb & 0x7f7f7f7fu) + 0x24242424u) & 0x80808080u) == 0u;
 }
 
 // Q8_0: 8 int8 codes -> 8 exact halves (1024 + (q + 128) - 1152).
@@ -601,21 +593,24 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                     // 64 columns = 8 words = pieces 2g, 2g+1 of the row
                     const uint4 wa = *reinterpret_cast<const uint4 *>(row + (((2 * grp) ^ (r & 7)) << 4));
                     const uint4 wb = *reinterpret_cast<const uint4 *>(row + (((2 * grp + 1) ^ (r & 7)) << 4));
-                    uint4 h[8];
+                    // word pairs (16 columns each) in the gf4_pair_levels order; a
+                    // 16-byte piece holding a scale past 252 (rare) takes the per-word
+                    // decode (Metal mode: element 4 rounded with its junk, the tiled-path
+                    // semantics, junk halves zero)
+                    uint32_t o[32];
+                    const uint32_t wd[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+                    const bool small[2] = {gf4_scales_small(wa), gf4_scales_small(wb)};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        if (small[i >> 1]) gf4_pair_levels(wd[2 * i], wd[2 * i + 1], o + 8 * i);
+                        else gf4_pair_any<EXACT>(wd[2 * i], wd[2 * i + 1], o + 8 * i);
+                    }
                     if constexpr (JK) {
                         uint32_t jk[8];
-                        gf4_quad_levels_junk(wa, h[0], h[1], h[2], h[3], jk);
-                        gf4_quad_levels_junk(wb, h[4], h[5], h[6], h[7], jk + 4);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) jk[i] = small[i >> 2] ? gf4_junk_halves(wd[i]) : 0u;
                         // junk tile columns ACOLS + 8 * grp .. (word 8 * grp + i at column i)
                         tmem_st8(tmem + lane_addr + T::A0 + sa * T::AC + G::ACOLS + grp * 8, jk);
-                    } else {
-                        gf4_quad_to_halves<EXACT>(wa, h[0], h[1], h[2], h[3]);
-                        gf4_quad_to_halves<EXACT>(wb, h[4], h[5], h[6], h[7]);
-                    }
-                    uint32_t o[32];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        o[4 * i] = h[i].x; o[4 * i + 1] = h[i].y; o[4 * i + 2] = h[i].z; o[4 * i + 3] = h[i].w;
                     }
                     tmem_st32(tcol, o);
                 } else {
@@ -879,29 +874,35 @@ __global__ void __launch_bounds__(128) dq_prep_kernel(const XT *x, const float *
         rowscale[n] = 1.0f;
     }
     const float rs = 1.0f / e2;  // exact power of two
-    for (int g = threadIdx.x; g < G; g += 128) {
-        float v[8];
+    // GF4 tiles hold each 16 columns (two words A, B) in the order
+    // [A0,A5,A1,A6,A2,A7,B0,B5,B1,B6,B2,B7,A3,B3,A4,B4] (gf4_pair_levels)
+    constexpr int kPerm16[16] = {0, 5, 1, 6, 2, 7, 8, 13, 9, 14, 10, 15, 3, 11, 4, 12};
+    for (int g = threadIdx.x; g < (G >> 1); g += 128) {
+        float v[16];
         if (n < B) {
-            load8(xr + g * 8, v);
+            load8(xr + g * 16, v);
+            load8(xr + g * 16 + 8, v + 8);
             if (norm_w) {
-                const float4 w0 = *reinterpret_cast<const float4 *>(norm_w + g * 8);
-                const float4 w1 = *reinterpret_cast<const float4 *>(norm_w + g * 8 + 4);
-                const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = (v[i] * inv * w[i]) * rs;
+                for (int h = 0; h < 2; ++h) {
+                    const float4 w0 = *reinterpret_cast<const float4 *>(norm_w + g * 16 + 8 * h);
+                    const float4 w1 = *reinterpret_cast<const float4 *>(norm_w + g * 16 + 8 * h + 4);
+                    const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[8 * h + i] = (v[8 * h + i] * inv * w[i]) * rs;
+                }
             } else {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = v[i] * rs;
+                for (int i = 0; i < 16; ++i) v[i] = v[i] * rs;
             }
         } else {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+            for (int i = 0; i < 16; ++i) v[i] = 0.0f;
         }
-        // GF4 tiles hold a word's k in the order [0,4,1,5,2,6,3,7]
-        uint32_t hw[4], lw[4];
+        uint32_t hw[8], lw[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float a = gf4_perm ? v[i] : v[2 * i], b = gf4_perm ? v[i + 4] : v[2 * i + 1];
+        for (int i = 0; i < 8; ++i) {
+            const float a = gf4_perm ? v[kPerm16[2 * i]] : v[2 * i], b = gf4_perm ? v[kPerm16[2 * i + 1]] : v[2 * i + 1];
             const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
             const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
             hw[i] = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
@@ -909,20 +910,28 @@ __global__ void __launch_bounds__(128) dq_prep_kernel(const XT *x, const float *
         }
         // k-atoms of 64 columns [2*NP rows: hi rows, then lo rows][128 B swizzled],
         // per 256 columns the four atoms of the chunk, then (junk) the junk atom
-        const int k = g * 8;
+        const int k = g * 16;
         const size_t atom = (size_t)(k >> 8) * (junk ? 5 : 4) + ((k & 255) >> 6);
         uint8_t *base = reinterpret_cast<uint8_t *>(xh) + atom * (2 * NP) * 128;
         const uint32_t c = (uint32_t)((k & 63) >> 3);
-        *reinterpret_cast<uint4 *>(base + sw128_off((uint32_t)n, c)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4 *>(base + sw128_off((uint32_t)(NP + n), c)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            *reinterpret_cast<uint4 *>(base + sw128_off((uint32_t)n, c + h)) =
+                make_uint4(hw[4 * h], hw[4 * h + 1], hw[4 * h + 2], hw[4 * h + 3]);
+            *reinterpret_cast<uint4 *>(base + sw128_off((uint32_t)(NP + n), c + h)) =
+                make_uint4(lw[4 * h], lw[4 * h + 1], lw[4 * h + 2], lw[4 * h + 3]);
+        }
         if (junk) {
-            // word w of the chunk: junk-atom columns 2w, 2w+1 both hold x_4 * 2^-10 (hi | lo rows)
-            const float a = v[4] * 0.0009765625f;
-            const __half ha = __float2half_rn(a), la = __float2half_rn(a - __half2float(ha));
-            const uint32_t w = (uint32_t)((k & 255) >> 3);
-            uint8_t *jb = reinterpret_cast<uint8_t *>(xh) + ((size_t)(k >> 8) * 5 + 4) * (2 * NP) * 128 + (w & 3) * 4;
-            *reinterpret_cast<uint32_t *>(jb + sw128_off((uint32_t)n, w >> 2)) = (uint32_t)__half_as_ushort(ha) * 0x10001u;
-            *reinterpret_cast<uint32_t *>(jb + sw128_off((uint32_t)(NP + n), w >> 2)) = (uint32_t)__half_as_ushort(la) * 0x10001u;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                // word w of the chunk: junk-atom columns 2w, 2w+1 both hold x_4 * 2^-10 (hi | lo rows)
+                const float a = v[8 * h + 4] * 0.0009765625f;
+                const __half ha = __float2half_rn(a), la = __float2half_rn(a - __half2float(ha));
+                const uint32_t w = (uint32_t)(((k + 8 * h) & 255) >> 3);
+                uint8_t *jb = reinterpret_cast<uint8_t *>(xh) + ((size_t)(k >> 8) * 5 + 4) * (2 * NP) * 128 + (w & 3) * 4;
+                *reinterpret_cast<uint32_t *>(jb + sw128_off((uint32_t)n, w >> 2)) = (uint32_t)__half_as_ushort(ha) * 0x10001u;
+                *reinterpret_cast<uint32_t *>(jb + sw128_off((uint32_t)(NP + n), w >> 2)) = (uint32_t)__half_as_ushort(la) * 0x10001u;
+            }
         }
     }
     if (n < B && (zero0 || zero1)) {
