@@ -116,10 +116,10 @@ class ClockSampler:
 # the step's kernels timed alone (roofline of the dominant one)
 # ---------------------------------------------------------------------------
 # DRAM bytes (read + write) per launch measured by ncu for a kernel class of the
-# table, from the capture summarised in profiles/ (see the file named per entry).
+# table: one `--set full` capture of `python -m qwowl35_b200.sweep --case
+# gateup_gf4_b32` (third launch, weights not in L2).
 NCU_TRAFFIC = {
-    # profiles/dq_kernel_gf4_gateup_b32.md: DRAM read + write of one launch
-    "gate_up_swiglu GF4 12288x4096": 54618368,
+    "gate_up_swiglu GF4 12288x4096": 55032064,
 }
 
 
