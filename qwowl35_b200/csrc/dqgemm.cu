@@ -89,7 +89,59 @@ struct DqParams {
     int rows, K, B, tiles;
     int gran, granules;     // schedule: granules of `gran` k-chunks spread over the grid
     int red_tma;            // split tiles add into y by TMA bulk reduction (else per-element atomics)
+    float *amax_val;        // fused argmax head (whole tiles, no logits stored): per-CTA
+    uint32_t *amax_idx;     //   (max, lowest id) of each batch column, [grid][B]
 };
+
+// The fused argmax epilogue is compiled for the head's codecs (Q8_0, Q6_K)
+// in store mode only; elsewhere its registers would crowd the decode warps.
+template <int CODEC, int MODE>
+__host__ __device__ constexpr bool dq_amax() {
+    return MODE == DQ_STORE && (CODEC == QW35_Q8_0_TYPE || CODEC == QW35_Q6_K_TYPE);
+}
+
+// (value, id) a beats b: larger value, ties to the lower id
+__device__ __forceinline__ bool amax_better(float va, uint32_t ia, float vb, uint32_t ib) {
+    return va > vb || (va == vb && ia < ib);
+}
+
+// Column-wise (max, lowest id) over the warp's 32 rows of NV columns (v[n],
+// id[n] of this lane's row): a butterfly reduce-scatter leaves lane l with
+// column amax_column<NV>(l) (lanes that share a column hold the same result).
+template <int NV>
+__device__ __forceinline__ void warp_amax_scatter(float *v, uint32_t *id, int lane, float &bv, uint32_t &bi) {
+#pragma unroll
+    for (int st = 0; (1 << st) < NV; ++st) {
+        const int o = 16 >> st, n = NV >> (st + 1);
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int j = 0; j < n; ++j) {
+            const float sv = up ? v[j] : v[j + n], kv = up ? v[j + n] : v[j];
+            const uint32_t si = up ? id[j] : id[j + n], ki = up ? id[j + n] : id[j];
+            const float ov = __shfl_xor_sync(0xffffffffu, sv, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, si, o);
+            const bool take = amax_better(ov, oi, kv, ki);
+            v[j] = take ? ov : kv;
+            id[j] = take ? oi : ki;
+        }
+    }
+    bv = v[0];
+    bi = id[0];
+#pragma unroll
+    for (int o = 16 / NV; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (amax_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+}
+template <int NV>
+__device__ __forceinline__ int amax_column(int lane) {
+    int idx = 0;
+#pragma unroll
+    for (int st = 0; (1 << st) < NV; ++st)
+        if (lane & (16 >> st)) idx += NV >> (st + 1);
+    return idx;
+}
 
 // Metal-mode GF4 carries each word's element-4 junk (the reference decode
 // kernel's unmasked bits, qw35_gf4.metal:8-20) exactly: the main f16 tile holds
@@ -664,6 +716,8 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
         const float rs0 = lane < p.B ? p.rowscale[lane] : 0.0f;
         const float rs1 = (NP > 32 && 32 + lane < p.B) ? p.rowscale[32 + lane] : 0.0f;
         int ul = 0, sg = 0;
+        float amax_v = -INFINITY;  // fused argmax: best of column amax_column<NP>(lane) so far
+        uint32_t amax_i = 0xffffffffu;
         DQ_FOR_SEGMENTS(p, nch, gbeg, gend, m, tile, c0, c1, {
             if (!*abort_flag) {
                 const int row = tile * TM + row_in_tile;
@@ -738,8 +792,24 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
                         if (lane == 0) mbar_arrive(&acc_empty[ab]);
                         ++ul;
                     }
+                    if (dq_amax<CODEC, MODE>() && p.amax_val != nullptr) {
+                        // whole tile: this row's logits of every batch column, reduced over
+                        // the warp's rows into the running (max, lowest id) per column
+                        uint32_t ids[NP];
 #pragma unroll
-                    for (int n0 = 0; n0 < NP; n0 += 16) emit16(n0, acc + n0);
+                        for (int n = 0; n < NP; ++n) {
+                            const float rs = __shfl_sync(0xffffffffu, n < 32 ? rs0 : rs1, n & 31);
+                            acc[n] = row < p.rows ? acc[n] * es * rs : -INFINITY;
+                            ids[n] = row < p.rows ? (uint32_t)row : 0xffffffffu;
+                        }
+                        float tv;
+                        uint32_t ti;
+                        warp_amax_scatter<NP>(acc, ids, lane, tv, ti);
+                        if (amax_better(tv, ti, amax_v, amax_i)) { amax_v = tv; amax_i = ti; }
+                    } else {
+#pragma unroll
+                        for (int n0 = 0; n0 < NP; n0 += 16) emit16(n0, acc + n0);
+                    }
                 } else {
                     // one accumulation per segment, streamed out 16 columns at a time
                     const int ab = ul & 1;
@@ -766,6 +836,31 @@ dq_kernel(const __grid_constant__ CUtensorMap map0, const __grid_constant__ CUte
             }
         })
         if (ew == 0 && lane == 0) bulk_wait_all();  // our reductions are complete before exit
+        if constexpr (NP <= 32 && dq_amax<CODEC, MODE>()) {
+            if (p.amax_val != nullptr) {
+                // the epilogue warps' column bests, combined in warp order (the staging
+                // buffer is free: whole-tile schedules store nothing through it)
+                float *sv = stg;
+                uint32_t *si = reinterpret_cast<uint32_t *>(stg + 128);
+                sv[ew * 32 + lane] = amax_v;
+                si[ew * 32 + lane] = amax_i;
+                named_sync(1, EPI * 32);
+                if (ew == 0) {
+                    float bv = sv[lane];
+                    uint32_t bi = si[lane];
+                    for (int w = 1; w < EPI; ++w)
+                        if (amax_better(sv[w * 32 + lane], si[w * 32 + lane], bv, bi)) {
+                            bv = sv[w * 32 + lane];
+                            bi = si[w * 32 + lane];
+                        }
+                    const int col = amax_column<NP>(lane);
+                    if (col < p.B) {  // lanes sharing a column write the same pair
+                        p.amax_val[(size_t)blockIdx.x * p.B + col] = bv;
+                        p.amax_idx[(size_t)blockIdx.x * p.B + col] = bi;
+                    }
+                }
+            }
+        }
     }
 
     // No programmatic launch trigger in this kernel: the next one (normally the
@@ -963,6 +1058,10 @@ cudaError_t swiglu_run(const float *gate, const float *up, float *h, size_t n, c
     dq_swiglu_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256, 0, st>>>(gate, up, h, n);
     return cudaGetLastError();
 }
+
+// final (max, lowest id) over per-CTA partials (matvec.cu)
+__global__ void argmax_reduce_kernel(const float *pv, const uint32_t *pi, int n, int B, uint32_t *out_tok,
+                                     float *out_val);
 
 // lowest-id argmax of each logits row (one CTA of 1024 threads per row)
 __global__ void __launch_bounds__(1024) dq_argmax_rows_kernel(const float *logits, int V, uint32_t *tok, float *val) {
@@ -1279,7 +1378,13 @@ cudaError_t dq_run(const MatvecArgs &a, int mode, uint32_t *tok, float *val, cud
         M.s1 = M.s0;
         M.h1 = M.h0;
     }
-    const size_t extra = (mode == 2) ? (size_t)2 * B * rows * 4 : (mode == 3 && !a.y) ? (size_t)B * rows * 4 : 0;
+    // mode 3 without a logits buffer (Q8_0 / Q6_K heads): the argmax is fused
+    // into the epilogue and only per-CTA partials ([grid][B] value + id) go
+    // through the scratch
+    const bool amax_fused = mode == 3 && !a.y && (a.type_id == QW35_Q8_0_TYPE || a.type_id == QW35_Q6_K_TYPE);
+    const size_t extra = (mode == 2) ? (size_t)2 * B * rows * 4
+                         : amax_fused ? (size_t)qw35h::sm_count() * B * 8
+                         : (mode == 3 && !a.y) ? (size_t)B * rows * 4 : 0;
     const DqScratch lay = dq_scratch_layout(B, a.k, a.rows, extra);
     // the caller's scratch (a runtime owns one for its lifetime), else a
     // stream-ordered allocation returned after this call's kernels
@@ -1327,6 +1432,12 @@ static cudaError_t dq_enqueue(const MatvecArgs &a, int mode, uint32_t *tok, floa
     if (mode == 2) { y0 = ext; y1 = ext + (size_t)B * rows; dmode = DQ_DUAL; }
     else if (mode == 3) { y0 = a.y ? a.y : ext; dmode = DQ_STORE; }
     else { y0 = a.y; dmode = mode == 1 ? DQ_ACCUM : DQ_STORE; }
+    const bool fused_amax = mode == 3 && !a.y && (a.type_id == QW35_Q8_0_TYPE || a.type_id == QW35_Q6_K_TYPE);
+    const int grid = std::min(p.granules, qw35h::sm_count());  // as dq_launch
+    if (fused_amax) {
+        p.amax_val = ext;
+        p.amax_idx = reinterpret_cast<uint32_t *>(ext + (size_t)grid * B);
+    }
     p.y[0] = y0;
     p.y[1] = y1;
     if (a.type_id == QW35_Q8_0_TYPE) {
@@ -1378,6 +1489,9 @@ static cudaError_t dq_enqueue(const MatvecArgs &a, int mode, uint32_t *tok, floa
     if (mode == 2) {
         const size_t n = (size_t)B * rows;
         dq_swiglu_kernel<<<(unsigned)std::min<size_t>((n + 255) / 256, 4096), 256, 0, st>>>(y0, y1, a.y, n);
+        e = cudaGetLastError();
+    } else if (mode == 3 && fused_amax) {
+        argmax_reduce_kernel<<<B, 256, 0, st>>>(p.amax_val, p.amax_idx, grid, B, tok, val);
         e = cudaGetLastError();
     } else if (mode == 3) {
         dq_argmax_rows_kernel<<<B, 1024, 0, st>>>(y0, rows, tok, val);
