@@ -2,6 +2,7 @@
 extensions) on a small synthetic model, against the fp64 oracle model."""
 import numpy as np
 from parity import modelerr as relerr  # decode-step logits (see parity.py)
+from parity import relerr as elem_relerr
 import pytest
 
 from oracle.model import OracleModel
@@ -276,6 +277,26 @@ def test_batched_prefill_matches_oracle(small, monkeypatch, mode):
     assert relerr(rt.copy_logits(), single.copy_logits().astype(np.float64)) < TOL
     rt.close()
     single.close()
+
+
+@pytest.mark.parametrize("T", [1, 7, 64])
+def test_deltanet_run_kernel_equals_step_launches(small, monkeypatch, T):
+    """The batched prefill's DeltaNet recurrence as one run launch per layer
+    (the default) against the same pass with one step launch per token
+    (QW35_PREFILL=1): conv windows, SSM state and the last token's logits agree
+    (the rest of the pass is the same code; its split-tile sums may add in
+    another order, hence a tolerance rather than bit equality)."""
+    toks = [(7 * i + 3) % small.cfg.vocab for i in range(T)]
+    out = {}
+    for mode in ("1", "2"):
+        monkeypatch.setenv("QW35_PREFILL", mode)
+        rt = Runtime(small, ctx=512, prefill_chunk=64)
+        rt.eval_prefill_chunk(toks, 0, LogitsMode.FULL)
+        out[mode] = (np.frombuffer(rt.state_export(), dtype=np.float32).astype(np.float64), rt.copy_logits())
+        rt.close()
+    (s1, l1), (s2, l2) = out["1"], out["2"]
+    assert elem_relerr(s2, s1) < TOL
+    assert relerr(l2, l1.astype(np.float64)) < TOL
 
 
 def test_runtimes_own_their_tensor_core_scratch(small):
