@@ -73,21 +73,31 @@ __device__ __forceinline__ void q8_block_store(const float *x, uint8_t *blk, int
 }
 
 // ---- preprocess: RMS norm + NeoX RoPE + f16 (or q8_0) KV write ----------------
-__global__ void __launch_bounds__(256) attn_pre_kernel(AttnPreArgs p) {
+// One warp per head row (16 q heads + 4 kv heads = 20 warps): every row's
+// load -> norm -> RoPE -> store chain runs at once.
+constexpr int APRE_THREADS = (AH + AKV) * 32;
+__global__ void __launch_bounds__(APRE_THREADS) attn_pre_kernel(AttnPreArgs p) {
     const int seq = blockIdx.x;
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int pos = p.pos[seq];
     const float *src = p.qkv + (size_t)seq * p.qkv_stride;
     const int d0 = lane * 8;
-    for (int task = wid; task < AH + AKV; task += 8) {
+    for (int task = wid; task < AH + AKV; task += APRE_THREADS / 32) {
         const bool isq = task < AH;
         const int h = isq ? task : task - AH;
         const float *x = isq ? src + h * 2 * AHD : src + QFULL + h * AHD;
         const float *nw = isq ? p.q_norm_w : p.k_norm_w;
         float v[8];
         float ss = 0.0f;
+        if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {  // a row stride of 4k floats: 16-byte loads
+            const float4 a = *reinterpret_cast<const float4 *>(x + d0), b = *reinterpret_cast<const float4 *>(x + d0 + 4);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) { v[i] = x[d0 + i]; ss = fmaf(v[i], v[i], ss); }
+            for (int i = 0; i < 8; ++i) v[i] = x[d0 + i];
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
         ss = warp_sum(ss);
         const float inv = rsqrtf(ss / (float)AHD + p.eps);
 #pragma unroll
@@ -524,7 +534,7 @@ size_t attn_workspace_bytes(int n_seq, int max_len) {
 
 cudaError_t attn_preprocess_run(const AttnPreArgs &a, cudaStream_t st) {
     if (a.n_seq <= 0) return cudaSuccess;
-    attn_pre_kernel<<<a.n_seq, 256, 0, st>>>(a);
+    attn_pre_kernel<<<a.n_seq, APRE_THREADS, 0, st>>>(a);
     return cudaGetLastError();
 }
 
